@@ -1,0 +1,378 @@
+#!/usr/bin/env python
+"""Benchmark: Llama-2-7B-shape int4 (W4A16) greedy decode, batch 1, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl aion|reference] [--matvec]
+
+Workload: the 7B shape (dim 4096, hidden 11008, 32 layers, 32 heads, vocab
+32000) with seed-1 random-init N(0, 0.02) weights quantized by the
+quantize.c arithmetic, fp32 activations and KV cache; greedy decode from
+BOS=1 over the 512-token workload.  One step = one decode token (one
+replay of the per-token CUDA graph).  W warm-up tokens take positions
+0..W-1, the K timed tokens continue the same greedy stream (a new
+sequence starts from BOS at position 0 after 512 tokens).  The weights
+(4.13 GB per token) are far larger than L2, so every step streams them
+from HBM.
+
+N > 1: independent replicas, one per GPU (the 7B path does not shard;
+"scaling": "weak"); value = N * K / (max over ranks of the timed region).
+
+--impl reference times the reference's own CPU int4 path (oracle/_ref,
+built from the reference's src/kernel_simd.c; scalar int4 kernel, host
+thread pool) on the same workload, bounded to a few minutes.
+--matvec times the isolated matvec shapes only (for profiling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CFG_7B = (4096, 11008, 32, 32, 32, 32000, 2048)
+SEED_7B = 1
+BOS = 1
+WORKLOAD_TOKENS = 512
+WEIGHT_BYTES_PER_TOKEN = 4_129_423_360          # 0.625 B x 6,607,077,376 weights
+MATVEC_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
+FALLBACK_HBM_GBS = 6650.0
+
+
+def matvec_bytes(d: int, n: int) -> int:
+    """Algorithmic bytes of one d x n int4 matvec: packed + scales + x + y."""
+    return int(0.625 * d * n) + 4 * n + 4 * d
+
+
+def hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ckpt_dir() -> Path:
+    d = Path(os.environ.get("AION_CKPT_DIR", Path(tempfile.gettempdir()) / "aion_ckpt"))
+    d.mkdir(parents=True, exist_ok=True)
+    return d
+
+
+def ensure_7b(rank: int) -> Path:
+    """Writes the seeded 7B int4 checkpoint once per host (rank 0)."""
+    import aion_b200 as A
+    path = ckpt_dir() / "llama2_7b_seed1.int4"
+    done = path.with_suffix(".done")
+    if rank == 0 and not done.exists():
+        tmp = path.with_suffix(".tmp")
+        A.synth_checkpoint(tmp, CFG_7B, SEED_7B, int4=True)
+        tmp.rename(path)
+        done.write_text("ok")
+    while not done.exists():
+        time.sleep(1.0)
+    return path
+
+
+class Clocks:
+    """Samples SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except FileNotFoundError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_reference_decode(path: Path, warmup: int, max_tokens: int, budget_s: float) -> dict:
+    """The reference's own CPU int4 path (scalar int4 kernel, pthread pool)
+    on the 7B checkpoint: tokens/s over a bounded sample of the workload."""
+    from oracle.oracle import REF_DIR, Oracle, Reference
+    cores = os.cpu_count() or 1
+    threads = max(1, cores - 1)       # T = cores oversubscribes the spin barrier
+    if (REF_DIR / "libaionref.so").exists():
+        ref = Reference().open(path, threads=threads, scalar=True)
+        fwd = ref.L.ref_forward
+        logits = lambda: np.ctypeslib.as_array(ref.L.ref_logits(), (CFG_7B[5],))  # noqa: E731
+        kind = "reference"
+    else:
+        orc = Oracle()
+        orc.set_threads(threads)
+        m = orc.open(path)
+        fwd = lambda t, p: m.o.L.orc_forward(m.h, t, p, 0)  # noqa: E731
+        logits = lambda: np.ctypeslib.as_array(m.o.L.orc_logits(m.h), (CFG_7B[5],))  # noqa: E731
+        kind = "port"
+    tok = BOS
+    for pos in range(warmup):
+        fwd(tok, pos)
+        tok = int(np.argmax(logits()))
+    n, t0 = 0, time.perf_counter()
+    pos = warmup
+    while n < max_tokens and (time.perf_counter() - t0) < budget_s:
+        fwd(tok, pos)
+        tok = int(np.argmax(logits()))
+        pos += 1
+        n += 1
+    secs = time.perf_counter() - t0
+    return {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": kind, "tokens": n, "seconds": secs,
+            "sample": f"7B W4A16 greedy decode from BOS, {n} tokens at positions {warmup}..{warmup + n - 1} "
+                      f"after {warmup} warm-up tokens; reference scalar int4 path, {threads} pthreads on "
+                      f"{cores} host cores"}
+
+
+def run_reference_arm(args) -> None:
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    path = ensure_7b(0)
+    cb = cpu_reference_decode(path, min(args.warmup, 3), args.steps, budget_s=args.ref_budget)
+    line = {"metric": "Llama-2-7B int4 decode tok/s (batch 1)", "value": cb["value"], "unit": "tok/s",
+            "n_gpus": world, "steps": cb["tokens"], "warmup": min(args.warmup, 3),
+            "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights, fp32 activations", "data": "synthetic",
+            "config": {"workload": "llama2-7b-shape W4A16 greedy decode, batch 1, 512-token workload",
+                       "dim": 4096, "hidden": 11008, "layers": 32, "vocab": 32000, "seed": SEED_7B},
+            "impl": "reference",
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def isolated_matvecs(device: int, reps: int) -> dict:
+    """GB/s of the W4A16 matvec kernel on the isolated 7B shapes, rotating over
+    enough distinct weight copies to exceed 2x L2 so every launch reads HBM."""
+    import torch
+    import aion_b200 as A
+    rng = np.random.default_rng(5)
+    out = {}
+    for d, n in MATVEC_SHAPES:
+        copies = max(2, int(np.ceil(2 * 126e6 / (0.625 * d * n))) + 1)
+        mats = []
+        for _ in range(copies):
+            packed = rng.integers(0, 256, d * n // 2, dtype=np.uint8)
+            scales = (rng.random(d * n // 32, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+            mats.append(A.QMatrix(scales, packed, d, n, device=device))
+        x = torch.randn(n, device=f"cuda:{device}")
+        y = torch.empty(d, device=f"cuda:{device}")
+        for m in mats:
+            m.matvec_w4a16(x, y)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            for m in mats:
+                m.matvec_w4a16(x, y)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / (reps * copies)
+        out[f"{d}x{n}"] = {"us": ms * 1e3, "GBps": matvec_bytes(d, n) / (ms * 1e-3) / 1e9}
+        for m in mats:
+            m.free()
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=WORKLOAD_TOKENS - 3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["aion", "reference"], default="aion")
+    ap.add_argument("--matvec", action="store_true", help="isolated matvec shapes only")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import aion_b200 as A
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device(f"cuda:{local}"))
+        pg = dist
+
+    def barrier():
+        if pg:
+            pg.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if not pg:
+            return v
+        t = torch.tensor([v], device=f"cuda:{local}", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    if args.matvec:
+        res = isolated_matvecs(local, reps=max(args.steps, 1))
+        if rank == 0:
+            print(json.dumps({"metric": "int4 matvec HBM GB/s (isolated 7B shapes)", "matvec": res}), flush=True)
+        return
+
+    path = ensure_7b(rank)
+    model = A.Model(path, device=local)
+    L = model.config.n_layers
+    launches_per_step = 5 * L + 2
+    stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{local}")
+
+    # Warm-up: positions 0..W-1 of the greedy stream.
+    model.step_async(BOS, 0)
+    for _ in range(args.warmup - 1):
+        model.step_async()
+    torch.cuda.synchronize()
+
+    clocks = Clocks(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    pos = args.warmup
+    for _ in range(args.steps):
+        if pos >= WORKLOAD_TOKENS:
+            model.step_async(BOS, 0)
+            pos = 1
+        else:
+            model.step_async()
+            pos += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    tok_s = world * args.steps / (ms * 1e-3)
+    stream_tokens = model.tokens(min(args.warmup + args.steps, WORKLOAD_TOKENS))
+
+    # Parity sanity: the stream against the reference's 7B stream, where recorded.
+    parity = None
+    gold = ROOT / "tests" / "golden" / "7b.json"
+    if gold.exists():
+        want = json.loads(gold.read_text())["w4a16_tokens"]
+        k = min(len(want), len(stream_tokens))
+        parity = {"tokens_compared": k, "identical": stream_tokens[:k] == want[:k]}
+
+    # Per-kernel device times (isolated, CUDA events on the model's stream).
+    kt = model.time_kernels(reps=3)
+    dim, hid, vocab = CFG_7B[0], CFG_7B[1], CFG_7B[5]
+    shapes = {"qkv": (3 * dim, dim), "wo": (dim, dim), "w13": (2 * hid, dim), "w2": (dim, hid),
+              "classifier": (vocab, dim)}
+    per_kernel = {}
+    for k, ms_k in kt.items():
+        share = ms_k * (1 if k in ("classifier", "embed") else L)
+        entry = {"us_per_launch": ms_k * 1e3, "ms_per_step": share}
+        if k in shapes:
+            entry["GBps"] = matvec_bytes(*shapes[k]) / (ms_k * 1e-3) / 1e9
+        per_kernel[k] = entry
+    dominant = max(shapes, key=lambda k: per_kernel[k]["ms_per_step"])
+    peak, peak_kind = hbm_peak()
+    dom = per_kernel[dominant]
+    roofline = {"kernel": f"k_matvec W4A16 ({dominant}: {shapes[dominant][0]}x{shapes[dominant][1]})",
+                "bound": "hbm", "achieved": dom["GBps"], "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": dom["GBps"] / peak, "traffic": None,
+                "bytes_per_launch": matvec_bytes(*shapes[dominant])}
+    step_gbs = WEIGHT_BYTES_PER_TOKEN * tok_s / world / 1e9
+
+    # End-to-end: the reference-facing call transformer(token, pos) per token
+    # with host buffers (token/pos in from pinned memory, logits out to pinned
+    # memory, argmax on the host), as the reference's main loop drives it.
+    logits = torch.empty(vocab, dtype=torch.float32, pin_memory=True)
+    lib = A.lib()
+    barrier()
+    tok = BOS
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        p = i % WORKLOAD_TOKENS
+        if p == 0:
+            tok = BOS
+        st = lib.aion_forward(model._h, tok, p, logits.data_ptr())
+        if st != 0:
+            raise A.AionError(st, lib.aion_last_error(model._h).decode())
+        tok = int(np.argmax(logits.numpy()))
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cb = cpu_reference_decode(path, 2, 1000, budget_s=20.0)
+        cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {
+            "metric": "Llama-2-7B int4 decode tok/s (batch 1)",
+            "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights (W4A16), fp32 activations/accumulate", "data": "synthetic",
+            "config": {"workload": "llama2-7b-shape W4A16 greedy decode, batch 1, 512-token workload",
+                       "dim": dim, "hidden": hid, "layers": L, "heads": 32, "vocab": vocab, "seed": SEED_7B,
+                       "parallelism": f"replicas x{world}", "l2": "weights 4.13 GB/token > L2 (no flush needed)"},
+            "weights_GBps_per_gpu": step_gbs, "weights_roofline_frac": step_gbs / peak,
+            "roofline": roofline, "kernels": per_kernel,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "e2e": {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 32,
+                    "d2h_bytes_per_step": vocab * 4},
+            "cpu_baseline": cpu,
+            "parity": parity,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

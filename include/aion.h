@@ -1,0 +1,174 @@
+/*
+ * aion.h -- C ABI of the B200 int4 Llama-2 decode library (libaion.so).
+ *
+ * Drop-in boundary for the int4 path of the reference engine
+ * (farukalpay/AION, src/kernel_simd.c).  Plain C11, no CUDA or torch types:
+ * device pointers are passed as plain pointers, CUDA streams as void*.
+ * Every call returns an aion_status; no call exits or aborts the process.
+ * The message of the last failure is available from aion_last_error().
+ *
+ * Threading: one aion_ctx is used by one host thread at a time; distinct
+ * contexts are independent.  All work of a context runs on its own stream.
+ */
+#ifndef AION_H
+#define AION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define AION_API __attribute__((visibility("default")))
+#else
+#define AION_API
+#endif
+
+typedef enum aion_status {
+    AION_OK = 0,
+    AION_ERR_IO = 1,      /* open / read / write failed                       */
+    AION_ERR_FORMAT = 2,  /* file size or header inconsistent with the format */
+    AION_ERR_SHAPE = 3,   /* unsupported or inconsistent dimensions           */
+    AION_ERR_OOM = 4,     /* device or host allocation failed                 */
+    AION_ERR_CUDA = 5,    /* CUDA runtime error                               */
+    AION_ERR_NCCL = 6,    /* NCCL error (tensor-parallel contexts)            */
+    AION_ERR_TIMEOUT = 7, /* a bounded device-side wait gave up               */
+    AION_ERR_ARG = 8,     /* invalid argument (token, position, pointer ...)  */
+    AION_ERR_STATE = 9    /* call not valid in the context's current state    */
+} aion_status;
+
+/* The 28-byte packed checkpoint header, field for field
+ * (src/kernel_simd.c:40-48, quantize.c:33-41). */
+typedef struct aion_config {
+    int32_t dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len;
+} aion_config;
+
+enum { AION_MODE_W4A16 = 0, AION_MODE_W4A8 = 1 };
+
+typedef struct aion_opts {
+    int32_t device;     /* CUDA device ordinal                                        */
+    int32_t mode;       /* AION_MODE_W4A16 (default) or AION_MODE_W4A8                */
+    int32_t max_batch;  /* sequences decoded in lock-step (default 1)                  */
+    int32_t max_pos;    /* KV positions allocated (0 = header seq_len; <= seq_len)     */
+    int32_t tp_size;    /* tensor-parallel ranks (default 1)                           */
+    int32_t tp_rank;    /* this rank, 0 <= tp_rank < tp_size                           */
+    const void* nccl_id;/* 128-byte ncclUniqueId shared by all ranks when tp_size > 1  */
+    int32_t use_graph;  /* 1 (default): replay one CUDA graph per decode step          */
+    int32_t reserved[7];
+} aion_opts;
+
+typedef struct aion_ctx aion_ctx;
+
+/* Fills *opts with the defaults listed above. */
+AION_API void aion_default_opts(aion_opts* opts);
+
+/* Text of the last failure of ctx, or of the calling thread's last
+ * context-free call (load, kernel-level, tools) when ctx is NULL. */
+AION_API const char* aion_last_error(const aion_ctx* ctx);
+
+/* ---------------------------------------------------------------------------
+ * Model level
+ * ------------------------------------------------------------------------- */
+
+/* Replaces load_checkpoint_int4 (src/kernel_simd.c:941-989) + malloc_run_state
+ * (:991-1008).  Validates the file size against the header in 64-bit
+ * arithmetic before any upload, uploads every tensor once to HBM re-tiled
+ * for the decode kernels, allocates the KV cache and activations, and
+ * unmaps the file.  The context owns all device memory. */
+AION_API aion_status aion_load(const char* int4_path, const aion_opts* opts, aion_ctx** out);
+AION_API aion_status aion_free(aion_ctx* ctx);
+AION_API aion_status aion_get_config(const aion_ctx* ctx, aion_config* out);
+
+/* Replaces transformer(token, pos, ...) (src/kernel_simd.c:1014-1169, int4
+ * branch): writes the KV cache at `pos` and produces the logits of (token,
+ * pos).  logits_host (vocab floats) may be NULL; the device copy stays
+ * readable through aion_logits_dev().  Requires 0 <= pos < max_pos. */
+AION_API aion_status aion_forward(aion_ctx* ctx, int32_t token, int32_t pos, float* logits_host);
+
+/* Device pointer to the logits of the last step ([max_batch][vocab] fp32). */
+AION_API const float* aion_logits_dev(const aion_ctx* ctx);
+
+/* Replaces the greedy loop of main (src/kernel_simd.c:1223-1258): starts at
+ * pos 0 from `bos`, runs `steps` forward steps, picks the first index of the
+ * maximum logit (strict '>', from -1e9; :1236-1243) on the device, and
+ * writes tokens_out[pos] = input token of step pos (what :1245 prints).
+ * *seconds (may be NULL) receives the wall time of the loop. */
+AION_API aion_status aion_generate(aion_ctx* ctx, int32_t bos, int32_t steps, int32_t* tokens_out,
+                                   double* seconds);
+
+/* The context's cudaStream_t (all of its work runs there). */
+AION_API void* aion_stream(const aion_ctx* ctx);
+
+/* Enqueues one decode step on the context's stream without waiting (the
+ * asynchronous form of one iteration of aion_generate).  token >= 0 forces
+ * the input token, token < 0 takes the previous step's argmax; pos >= 0
+ * sets the position, pos < 0 continues at the next one. */
+AION_API aion_status aion_step_async(aion_ctx* ctx, int32_t token, int32_t pos);
+
+/* Copies the input tokens of positions [0, n) recorded on the device. */
+AION_API aion_status aion_tokens(aion_ctx* ctx, int32_t* out, int32_t n);
+
+/* Diagnostics: mean device time of one launch of each kernel class of the
+ * decode step, timed in isolation with CUDA events (out_ms[7]: QKV, attention,
+ * wo, w1/w3, w2, classifier, embed).  Clobbers activations; no reference
+ * counterpart. */
+AION_API aion_status aion_time_kernels(aion_ctx* ctx, int32_t reps, float* out_ms);
+
+/* Clears the KV cache (a new sequence). */
+AION_API aion_status aion_reset(aion_ctx* ctx);
+
+/* ---------------------------------------------------------------------------
+ * Kernel level (device pointers; stream = cudaStream_t or NULL)
+ * ------------------------------------------------------------------------- */
+
+typedef struct aion_qmatrix aion_qmatrix;
+
+/* Uploads one int4 matrix [rows][cols] given in the quantize.c layout (the
+ * QWeight view of src/kernel_simd.c:113-116: fp32 scales[rows*cols/32] and
+ * packed bytes[rows*cols/2], host memory) and re-tiles it on the device.
+ * cols must be a multiple of 32. */
+AION_API aion_status aion_qmatrix_upload(const float* scales, const uint8_t* packed, int64_t rows, int64_t cols,
+                                         int32_t device, aion_qmatrix** out);
+/* Exact inverse of the re-tile: writes the quantize.c layout back to host
+ * memory, byte for byte. */
+AION_API aion_status aion_qmatrix_download(const aion_qmatrix* w, float* scales, uint8_t* packed);
+AION_API aion_status aion_qmatrix_free(aion_qmatrix* w);
+
+/* W4A16 matvec y[rows] = W x[cols] (fp32 in, fp32 accumulate, fp32 out).
+ * Replaces matmul_int4_scalar / matmul_int4_neon (src/kernel_simd.c:341,377)
+ * as dispatched by dispatch_matmul_int4 (:752) over all rows. */
+AION_API aion_status aion_matvec_w4a16(const aion_qmatrix* w, const float* x_dev, float* y_dev, void* stream);
+
+/* W4A8 matvec: per-32 dynamic int8 quantization of x fused with the int4 x
+ * int8 group dot and the per-row sequential fp32 epilogue.  Replaces
+ * quantize_activations_neon (:186) + matmul_w4a8_neon (:244) as
+ * dispatch_matmul_w4a8 (:771) would run them.  Bit-exact with them. */
+AION_API aion_status aion_matvec_w4a8(const aion_qmatrix* w, const float* x_dev, float* y_dev, void* stream);
+
+/* Per-32 symmetric int8 activation quantization (quantize_activations_neon,
+ * src/kernel_simd.c:186-227): qx[n] int8, xs[n/32] fp32.  Bit-exact. */
+AION_API aion_status aion_quantize_activations(const float* x_dev, int8_t* qx_dev, float* xs_dev, int64_t n,
+                                               void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Checkpoint tools (host)
+ * ------------------------------------------------------------------------- */
+
+/* quantize_buffer (quantize.c:59-109) with 64-bit element counts. */
+AION_API void aion_quantize_buffer(const float* in, uint8_t* packed, float* scales, int64_t n);
+/* Byte size of a checkpoint for a 7-int header, fp32 (int4 = 0) or int4. */
+AION_API int64_t aion_checkpoint_bytes(const int32_t* cfg7, int int4);
+/* fp32 llama2.c legacy file -> int4 file in the quantize.c format
+ * (quantize.c:119-238), 64-bit clean. */
+AION_API int aion_quantize_file(const char* in_path, const char* out_path, int threads, char* err, int errlen);
+/* Seeded random-init checkpoint: matrices N(0, 0.02), RMSNorm weights 1.0,
+ * RoPE tables; written as fp32 (int4 = 0) or directly as int4. */
+AION_API int aion_synth_checkpoint(const char* path, const int32_t* cfg7, uint64_t seed, int int4, int threads,
+                                   char* err, int errlen);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AION_H */

@@ -1,0 +1,131 @@
+"""Generates the golden fixtures of tests/golden/ from the REFERENCE itself.
+
+Run in a container that has the reference tree (the binaries of
+oracle/_ref/ are built from it by `make -C oracle`):
+
+    python tests/golden/make_golden.py [--7b]
+
+Every expected value here comes from the reference's own code: the
+`quantize` binary and quantize_buffer() of quantize.c, and the functions of
+src/kernel_simd.c through oracle/_ref/libaionref.so (its CLI for the token
+stream).  The fixtures are hashes and short token lists; the tests check the
+oracle restatement against them, and the GPU path against the oracle.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests"))
+
+import aion_b200 as A  # noqa: E402
+import cases  # noqa: E402
+from oracle.oracle import REF_DIR, Reference  # noqa: E402
+
+OUT = Path(__file__).resolve().parent
+
+
+def file_sha(p: Path) -> str:
+    h = hashlib.sha256()
+    with open(p, "rb") as f:
+        for b in iter(lambda: f.read(1 << 24), b""):
+            h.update(b)
+    return h.hexdigest()
+
+
+def model_fixture(ref: Reference, path: Path, steps: int, w4a8_steps: int, threads: int, cli: bool) -> dict:
+    out = {}
+    if cli:
+        r = subprocess.run([str(REF_DIR / "kernel_simd"), str(path), str(steps), str(threads), "int4", "scalar"],
+                           capture_output=True, text=True, check=True, cwd=tempfile.gettempdir())
+        out["w4a16_cli_tokens"] = [int(l.split()[1]) for l in r.stdout.strip().splitlines()]
+    ref.open(path, threads=threads, scalar=True)
+    t0 = time.time()
+    toks, gaps, logits = ref.generate(steps, dump_logits=True)
+    out["w4a16_seconds"] = time.time() - t0
+    out["w4a16_tokens"] = toks.tolist()
+    out["w4a16_gaps"] = [float(g) for g in gaps]
+    out["w4a16_logits_sha"] = [cases.sha(l) for l in logits]
+    out["w4a16_logits_head"] = [[float(v) for v in l[:4]] for l in logits[:4]]
+    toks8, gaps8, logits8 = ref.generate(w4a8_steps, w4a8=True, dump_logits=True)
+    out["w4a8_tokens"] = toks8.tolist()
+    out["w4a8_gaps"] = [float(g) for g in gaps8]
+    out["w4a8_logits_sha"] = [cases.sha(l) for l in logits8]
+    return out
+
+
+def kat_fixture(ref: Reference) -> dict:
+    kat: dict = {"quantizer": {}, "actquant": {}, "matvec": {}}
+    for name, w in cases.quantizer_kat_inputs().items():
+        packed, scales = ref.quantize_buffer(w)
+        kat["quantizer"][name] = {"packed": packed.tolist(), "scales_hex": scales.view(np.uint32).tolist()}
+    for name, x in cases.actquant_kat_inputs().items():
+        qx, xs = ref.quantize_activations(x)
+        kat["actquant"][name] = {"qx": qx.tolist(), "xs_hex": xs.view(np.uint32).tolist()}
+    for d, n in cases.MATVEC_7B + cases.MATVEC_EDGE:
+        seed = cases.case_seed(d, n)
+        w = cases.matrix(d, n, seed)
+        packed, scales = ref.quantize_buffer(w)
+        x = cases.vector(n, seed)
+        y16 = ref.matmul_int4_scalar(x, scales, packed, n, d)
+        y8 = ref.matmul_w4a8(x, scales, packed, n, d)
+        kat["matvec"][f"{d}x{n}"] = {
+            "seed": seed,
+            "packed_sha": cases.sha(packed), "scales_sha": cases.sha(scales),
+            "w4a16_sha": cases.sha(y16), "w4a8_sha": cases.sha(y8),
+            "w4a16_head": [float(v) for v in y16[:4]], "w4a8_head": [float(v) for v in y8[:4]],
+        }
+    return kat
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--7b", dest="b7", action="store_true", help="also the 7B stream (needs ~5 GB disk, minutes)")
+    ap.add_argument("--threads", type=int, default=7)
+    ap.add_argument("--tmp", default=tempfile.gettempdir())
+    args = ap.parse_args()
+    ref = Reference()
+    tmp = Path(args.tmp)
+
+    (OUT / "kat.json").write_text(json.dumps(kat_fixture(ref)))
+    print("kat.json written")
+
+    f32 = tmp / "aion_tiny_f32.bin"
+    q = tmp / "aion_tiny_int4_ref.bin"
+    A.synth_checkpoint(f32, cases.TINY, cases.SEEDS["tiny"], int4=False)
+    subprocess.run([str(REF_DIR / "quantize"), str(f32), str(q)], check=True, capture_output=True)
+    tiny = {"config": list(cases.TINY), "seed": cases.SEEDS["tiny"], "fp32_sha": file_sha(f32),
+            "int4_sha": file_sha(q), "int4_bytes": q.stat().st_size}
+    tiny.update(model_fixture(ref, q, 256, 256, args.threads, cli=True))
+    (OUT / "tiny.json").write_text(json.dumps(tiny))
+    print("tiny.json written; min gap", min(tiny["w4a16_gaps"]))
+
+    if args.b7:
+        p7 = tmp / "aion_7b_int4.bin"
+        if not p7.exists():
+            A.synth_checkpoint(p7, cases.LLAMA7B, cases.SEEDS["7b"], int4=True)
+        b7 = {"config": list(cases.LLAMA7B), "seed": cases.SEEDS["7b"], "int4_sha": file_sha(p7),
+              "int4_bytes": p7.stat().st_size}
+        # The reference engine is process-global: run the 7B model in a child.
+        code = ("import sys, json; sys.path.insert(0, %r); sys.path.insert(0, %r);"
+                "from tests.golden.make_golden import model_fixture; from oracle.oracle import Reference;"
+                "print(json.dumps(model_fixture(Reference(), %r, 64, 32, %d, cli=False)))"
+                % (str(ROOT), str(ROOT / "tests"), str(p7), args.threads))
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
+        b7.update(json.loads(r.stdout.strip().splitlines()[-1]))
+        (OUT / "7b.json").write_text(json.dumps(b7))
+        print("7b.json written; min gap", min(b7["w4a16_gaps"]))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,132 @@
+"""Kernel-level parity on the GPU, through the C ABI.
+
+Tolerances:
+  - re-tile / inverse, activation quantization, W4A8 matvec: bit-exact;
+  - W4A16 matvec: fp32 accumulation in a different order than the scalar
+    reference, so |y - y_oracle| <= 2e-5 * max|y_oracle|, and the error
+    against a float64 evaluation of the same int4 matrix is at most twice
+    the oracle's own error plus 1e-6 * max|y|.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cases
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = cases.MATVEC_7B + cases.MATVEC_EDGE
+
+
+def dequant(packed: np.ndarray, scales: np.ndarray, d: int, n: int) -> np.ndarray:
+    lo = (packed & 0xF).astype(np.int8) - 8
+    hi = (packed >> 4).astype(np.int8) - 8
+    q = np.stack([lo, hi], axis=-1).reshape(d, n).astype(np.float64)
+    return q * np.repeat(scales.astype(np.float64).reshape(d, n // 32), 32, axis=1)
+
+
+@pytest.fixture(scope="module")
+def mats():
+    import aion_b200 as A
+    out = {}
+    for d, n in SHAPES:
+        seed = cases.case_seed(d, n)
+        packed, scales = A.quantize_buffer(cases.matrix(d, n, seed))
+        out[(d, n)] = (seed, packed, scales)
+    return out
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_retile_roundtrip(cuda, mats, shape):
+    import aion_b200 as A
+    d, n = shape
+    _, packed, scales = mats[shape]
+    q = A.QMatrix(scales, packed, d, n)
+    s2, p2 = q.download()
+    assert (p2 == packed).all() and (s2.view(np.uint32) == scales.view(np.uint32)).all()
+    q.free()
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+@pytest.mark.parametrize("xscale", [1.0, 1e-3, 1e3])
+def test_matvec_w4a16(cuda, oracle, mats, shape, xscale):
+    import aion_b200 as A
+    torch = cuda
+    d, n = shape
+    seed, packed, scales = mats[shape]
+    x = (cases.vector(n, seed) * np.float32(xscale)).astype(np.float32)
+    q = A.QMatrix(scales, packed, d, n)
+    xt = torch.from_numpy(x).cuda()
+    y = torch.full((d,), float("nan"), device="cuda")
+    q.matvec_w4a16(xt, y)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    ref = oracle.matvec_w4a16(x, scales, packed, n, d)
+    scale = np.abs(ref).max()
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= 2e-5 * scale
+    exact = dequant(packed, scales, d, n) @ x.astype(np.float64)
+    assert np.abs(got - exact).max() <= 2 * np.abs(ref - exact).max() + 1e-6 * scale
+    q.free()
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+def test_matvec_w4a8_bit_exact(cuda, oracle, mats, shape):
+    import aion_b200 as A
+    torch = cuda
+    d, n = shape
+    seed, packed, scales = mats[shape]
+    x = cases.vector(n, seed)
+    if n >= 64:
+        x[32:64] = 0.0          # a group with amax <= 1e-9 (scale 1, all-zero int8)
+    q = A.QMatrix(scales, packed, d, n)
+    y = torch.empty(d, device="cuda")
+    q.matvec_w4a8(torch.from_numpy(x).cuda(), y)
+    torch.cuda.synchronize()
+    ref = oracle.matvec_w4a8(x, scales, packed, n, d)
+    assert (y.cpu().numpy().view(np.uint32) == ref.view(np.uint32)).all()
+    q.free()
+
+
+@pytest.mark.parametrize("name", sorted(cases.actquant_kat_inputs()))
+def test_quantize_activations_bit_exact(cuda, golden_kat, name):
+    import aion_b200 as A
+    torch = cuda
+    x = cases.actquant_kat_inputs()[name]
+    qx = torch.empty(x.size, dtype=torch.int8, device="cuda")
+    xs = torch.empty(x.size // 32, dtype=torch.float32, device="cuda")
+    A.quantize_activations(torch.from_numpy(x).cuda(), qx, xs)
+    torch.cuda.synchronize()
+    want = golden_kat["actquant"][name]
+    assert qx.cpu().numpy().tolist() == want["qx"]
+    assert xs.cpu().numpy().view(np.uint32).tolist() == want["xs_hex"]
+
+
+def test_quantize_activations_large(cuda, oracle):
+    import aion_b200 as A
+    torch = cuda
+    x = cases.vector(11008, 77) * np.float32(4.0)
+    qx = torch.empty(x.size, dtype=torch.int8, device="cuda")
+    xs = torch.empty(x.size // 32, dtype=torch.float32, device="cuda")
+    A.quantize_activations(torch.from_numpy(x).cuda(), qx, xs)
+    rq, rs = oracle.quantize_activations(x)
+    assert (qx.cpu().numpy() == rq).all() and (xs.cpu().numpy().view(np.uint32) == rs.view(np.uint32)).all()
+
+
+def test_matvec_on_a_side_stream(cuda, oracle, mats):
+    import aion_b200 as A
+    torch = cuda
+    d, n = 4096, 4096
+    seed, packed, scales = mats[(d, n)]
+    x = cases.vector(n, seed)
+    q = A.QMatrix(scales, packed, d, n)
+    s = torch.cuda.Stream()
+    xt = torch.from_numpy(x).cuda()
+    with torch.cuda.stream(s):
+        y = torch.empty(d, device="cuda")
+        for _ in range(3):
+            q.matvec_w4a16(xt, y, stream=s)
+    s.synchronize()
+    ref = oracle.matvec_w4a16(x, scales, packed, n, d)
+    assert np.abs(y.cpu().numpy() - ref).max() <= 2e-5 * np.abs(ref).max()
