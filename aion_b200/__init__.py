@@ -85,9 +85,8 @@ def lib() -> ctypes.CDLL:
         "aion_generate": (I32, [VP, I32, I32, VP, P(ctypes.c_double)]),
         "aion_reset": (I32, [VP]),
         "aion_stream": (VP, [VP]),
-        "aion_step_async": (I32, [VP, I32, I32]),
+        "aion_decode_async": (I32, [VP, I32, I32, I32]),
         "aion_tokens": (I32, [VP, VP, I32]),
-        "aion_time_kernels": (I32, [VP, I32, VP]),
         "aion_qmatrix_upload": (I32, [VP, VP, I64, I64, I32, P(VP)]),
         "aion_qmatrix_download": (I32, [VP, VP, VP]),
         "aion_qmatrix_free": (I32, [VP]),
@@ -213,9 +212,9 @@ class Model:
     def reset(self) -> None:
         _check(lib().aion_reset(self._h), self._h)
 
-    def step_async(self, token: int = -1, pos: int = -1) -> None:
-        """Enqueues one decode step without waiting (token/pos < 0: continue greedily)."""
-        _check(lib().aion_step_async(self._h, token, pos), self._h)
+    def decode_async(self, steps: int, token: int = -1, pos: int = -1) -> None:
+        """Enqueues `steps` greedy steps without waiting (token/pos < 0: continue)."""
+        _check(lib().aion_decode_async(self._h, token, pos, steps), self._h)
 
     def stream_ptr(self) -> int:
         """The context's cudaStream_t, for events recorded by the caller."""
@@ -226,14 +225,6 @@ class Model:
         out = np.zeros(max(n, 1), np.int32)
         _check(lib().aion_tokens(self._h, _ptr(out), n), self._h)
         return out[:n].tolist()
-
-    KERNEL_CLASSES = ("qkv", "attention", "wo", "w13", "w2", "classifier", "embed")
-
-    def time_kernels(self, reps: int = 3) -> dict[str, float]:
-        """Mean device ms of one launch per kernel class (clobbers activations)."""
-        out = np.zeros(7, np.float32)
-        _check(lib().aion_time_kernels(self._h, reps, _ptr(out)), self._h)
-        return dict(zip(self.KERNEL_CLASSES, (float(v) for v in out)))
 
     def logits_dev_ptr(self) -> int:
         return int(lib().aion_logits_dev(self._h))

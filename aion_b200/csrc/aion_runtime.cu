@@ -1,10 +1,11 @@
 // Host side of libaion: the C ABI declared in include/aion.h.
 //
 // Replaces the reference's loader, run state, thread pool and forward driver
-// (src/kernel_simd.c:631-787, 906-1169): the int4 checkpoint is uploaded
-// once and re-tiled in HBM, and one decode step is a fixed sequence of
-// fused kernels on one stream, captured once as a CUDA graph and replayed
-// per token.  No host thread spins; nothing here exits the process.
+// (src/kernel_simd.c:631-787, 906-1169).  The int4 checkpoint is uploaded
+// once and re-tiled in HBM; decode runs as one persistent cooperative kernel
+// per launch (one CTA per SM) that executes `steps` greedy tokens; one
+// decode step is captured once as a CUDA graph and replayed per token.  No
+// host thread spins; nothing here exits the process.
 #include <cuda_runtime.h>
 #include <errno.h>
 #include <fcntl.h>
@@ -15,11 +16,12 @@
 #include <time.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
 #include "../../include/aion.h"
-#include "decode_kernels.cuh"
+#include "decode_step.cuh"
 
 using namespace aion;
 
@@ -28,7 +30,6 @@ using namespace aion;
 // ---------------------------------------------------------------------------
 static thread_local std::string g_thread_err;
 
-struct aion_ctx;
 static void set_err(std::string* dst, const char* fmt, ...) {
     char buf[512];
     va_list ap;
@@ -54,144 +55,122 @@ static aion_status cuda_status(cudaError_t e) {
     } while (0)
 
 // ---------------------------------------------------------------------------
-// Tiled device matrices
+// Device properties and launch geometry
 // ---------------------------------------------------------------------------
-struct DevMatrix {
-    uint8_t* w = nullptr;
-    long long tile_bytes = 0;
-    int n = 0;
-    long long rows = 0;      // logical rows
-    long long rows_pad = 0;  // multiple of kRB
-    int ntiles = 0;
+struct DevInfo {
+    int sms = 0, smem_optin = 0;
 };
+static DevInfo g_dev[64];
 
-static long long tiled_bytes(long long rows, int n) {
-    long long rp = (rows + kRB - 1) / kRB * kRB;
-    return rp / kRB * ((long long)kRB * n / 32 * 4 + (long long)kRB * n / 2);
-}
-
-static void dev_matrix_init(DevMatrix* m, uint8_t* w, long long rows, int n) {
-    m->w = w;
-    m->n = n;
-    m->rows = rows;
-    m->rows_pad = (rows + kRB - 1) / kRB * kRB;
-    m->tile_bytes = (long long)kRB * n / 32 * 4 + (long long)kRB * n / 2;
-    m->ntiles = (int)(m->rows_pad / kRB);
-}
-
-static int g_num_sms[64];
-
-static int num_sms(int dev) {
-    if (dev < 0 || dev >= 64) return 148;
-    if (!g_num_sms[dev]) {
+static const DevInfo& dev_info(int dev) {
+    static DevInfo fallback = {148, 227 * 1024};
+    if (dev < 0 || dev >= 64) return fallback;
+    DevInfo& d = g_dev[dev];
+    if (!d.sms) {
         int v = 0;
         if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
-        g_num_sms[dev] = v;
+        d.sms = v;
+        v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0)
+            v = 227 * 1024;
+        d.smem_optin = v;
     }
-    return g_num_sms[dev];
+    return d;
 }
 
-// Launch with the programmatic-stream-serialization attribute (PDL): the
-// kernel may start while its predecessor drains; it synchronises on the
-// predecessor with griddepcontrol.wait before touching its outputs.
+static int round128(int b) { return (b + 127) & ~127; }
+
+// Dynamic shared memory plan of the streaming kernels: x' area, then the
+// per-warp rings of P slots.
+struct SmemPlan {
+    int xbytes = 0, slot_bytes = 0, P = 0, total = 0;
+};
+
+static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int mode, int smem_optin, int static_bytes) {
+    SmemPlan p;
+    p.xbytes = round128(xbuf_bytes(max_n, mode));
+    p.slot_bytes = round128(max_chunk_bytes);
+    const int avail = smem_optin - static_bytes - 1024 - p.xbytes;
+    p.P = std::min(8, avail / (kWarps * p.slot_bytes));
+    p.total = p.xbytes + kWarps * std::max(p.P, 0) * p.slot_bytes;
+    return p;
+}
+
 template <typename... KArgs, typename... Args>
-static cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
-                          Args&&... args) {
+static cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                             bool coop, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (coop) {
+        attr[na].id = cudaLaunchAttributeCooperative;
+        attr[na].val.cooperative = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-typedef void (*MatvecKernel)(MatvecArgs);
-
-template <int MODE>
-static MatvecKernel pick_matvec(int pro, int epi) {
-    if (pro == PRO_PLAIN) {
-        switch (epi) {
-        case EPI_STORE: return k_matvec<MODE, PRO_PLAIN, EPI_STORE>;
-        case EPI_RESIDUAL: return k_matvec<MODE, PRO_PLAIN, EPI_RESIDUAL>;
-        default: return nullptr;
-        }
-    }
-    switch (epi) {
-    case EPI_QKV: return k_matvec<MODE, PRO_RMSNORM, EPI_QKV>;
-    case EPI_SWIGLU: return k_matvec<MODE, PRO_RMSNORM, EPI_SWIGLU>;
-    case EPI_LOGITS: return k_matvec<MODE, PRO_RMSNORM, EPI_LOGITS>;
-    case EPI_STORE: return k_matvec<MODE, PRO_RMSNORM, EPI_STORE>;
-    default: return nullptr;
-    }
-}
-
-static MatvecKernel matvec_kernel(int mode, int pro, int epi) {
-    return mode == MODE_W4A8 ? pick_matvec<MODE_W4A8>(pro, epi) : pick_matvec<MODE_W4A16>(pro, epi);
-}
-
-static cudaError_t raise_smem_limits() {
-    static bool done = false;
-    if (done) return cudaSuccess;
-    const int pros[2] = {PRO_PLAIN, PRO_RMSNORM};
-    const int epis[5] = {EPI_STORE, EPI_RESIDUAL, EPI_QKV, EPI_SWIGLU, EPI_LOGITS};
-    for (int mode = 0; mode < 2; mode++)
-        for (int p = 0; p < 2; p++)
-            for (int e = 0; e < 5; e++) {
-                MatvecKernel k = matvec_kernel(mode, pros[p], epis[e]);
-                if (!k) continue;
-                cudaError_t err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-                if (err != cudaSuccess) return err;
-            }
-    done = true;
-    return cudaSuccess;
-}
-
-static cudaError_t launch_matvec(int mode, int pro, int epi, const DevMatrix& m, MatvecArgs a, int dev, cudaStream_t st,
-                                 bool pdl) {
-    a.w = m.w;
-    a.tile_bytes = m.tile_bytes;
-    a.n = m.n;
-    a.ntiles = m.ntiles;
-    if (a.d == 0) a.d = (int)m.rows;
-    a.prefetch_tiles = kMvWarps;
-    const int sms = num_sms(dev);
-    int grid = (m.ntiles + kMvWarps - 1) / kMvWarps;
-    if (grid > 2 * sms) grid = 2 * sms;
-    if (grid < 1) grid = 1;
-    return launch(matvec_kernel(mode, pro, epi), dim3(grid), dim3(kMvThreads), (size_t)matvec_smem_bytes(m.n, mode),
-                  st, pdl, a);
-}
-
-static cudaError_t retile(const DevMatrix& m, const float* scales, const uint8_t* packed, long long rows,
-                          int row_offset, int interleave, int slot, int inverse, cudaStream_t st) {
+static cudaError_t retile(const MatDesc& m, const float* scales, const uint8_t* packed, long long rows, int row_offset,
+                          int interleave, int slot, int inverse, cudaStream_t st) {
     RetileArgs a;
     a.src_scales = scales;
     a.src_packed = packed;
-    a.dst = m.w;
-    a.tile_bytes = m.tile_bytes;
+    a.m = m;
     a.rows = rows;
-    a.n = m.n;
     a.row_offset = row_offset;
     a.interleave = interleave;
     a.slot = slot;
     a.inverse = inverse;
-    long long total = rows * (m.n / 32);
-    int grid = (int)((total + 255) / 256);
-    if (grid > 65535) grid = 65535;
+    const long long total = rows * (m.n / 32);
+    int grid = (int)std::min<long long>((total + 255) / 256, 65535);
     if (grid < 1) grid = 1;
     k_retile<<<grid, 256, 0, st>>>(a);
     return cudaGetLastError();
 }
 
-static cudaError_t fill_pad(const DevMatrix& m, cudaStream_t st) {
-    if (m.rows_pad == m.rows) return cudaSuccess;
-    k_fill_pad<<<8, 256, 0, st>>>(m.w, m.tile_bytes, m.rows, m.rows_pad, m.n);
+static cudaError_t fill_pad(const MatDesc& m, cudaStream_t st) {
+    if ((long long)m.ntiles * kRB == m.d) return cudaSuccess;
+    k_fill_pad<<<8, 256, 0, st>>>(m);
     return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Standalone matvec (kernel-level API)
+// ---------------------------------------------------------------------------
+template <int MODE>
+static cudaError_t launch_standalone(const MatDesc& m, const float* x, float* y, int dev, cudaStream_t st) {
+    static bool attr_done[2] = {false, false};
+    const DevInfo& di = dev_info(dev);
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, k_matvec<MODE>);
+    if (e != cudaSuccess) return e;
+    SmemPlan p = plan_smem(m.n, m.chunk_bytes, MODE, di.smem_optin, (int)fa.sharedSizeBytes);
+    if (p.P < 1) return cudaErrorInvalidConfiguration;
+    if (!attr_done[MODE]) {
+        e = cudaFuncSetAttribute(k_matvec<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 di.smem_optin - (int)fa.sharedSizeBytes);
+        if (e != cudaSuccess) return e;
+        attr_done[MODE] = true;
+    }
+    StandaloneArgs a;
+    a.m = m;
+    a.x = x;
+    a.y = y;
+    a.P = p.P;
+    a.slot_bytes = p.slot_bytes;
+    const int grid = std::min(di.sms, m.ntiles);
+    return launch_ex(k_matvec<MODE>, dim3(grid), dim3(kThreads), (size_t)p.total, st, true, false, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -207,17 +186,21 @@ struct aion_ctx {
     cudaStream_t stream = nullptr;
     uint8_t* arena = nullptr;
     size_t arena_bytes = 0, arena_used = 0;
-    DevMatrix emb;
-    std::vector<DevMatrix> qkv, wo, w13, w2;
+    MatDesc emb;
+    std::vector<MatDesc> qkv, wo, w13, w2;
     float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr, *freq_re = nullptr, *freq_im = nullptr;
     float *kcache = nullptr, *vcache = nullptr;
     float *x = nullptr, *q = nullptr, *att = nullptr, *hb = nullptr, *logits = nullptr;
-    float* attn_partial = nullptr;
-    int* attn_counters = nullptr;
-    int split_len = 64, n_splits = 1;
+    float* attn_part = nullptr;
+    int* attn_cnt = nullptr;
+    int max_chunks = 1;
     StepState* step = nullptr;
     unsigned long long* argmax = nullptr;
     int32_t* history = nullptr;
+    OpDesc* ops = nullptr;
+    int nops = 0;
+    SmemPlan plan;
+    int grid = 0;
     StepState* h_step = nullptr;   // pinned
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
@@ -235,13 +218,9 @@ static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
 extern "C" AION_API void aion_default_opts(aion_opts* o) {
     if (!o) return;
     memset(o, 0, sizeof(*o));
-    o->device = 0;
     o->mode = AION_MODE_W4A16;
     o->max_batch = 1;
-    o->max_pos = 0;
     o->tp_size = 1;
-    o->tp_rank = 0;
-    o->nccl_id = nullptr;
     o->use_graph = 1;
 }
 
@@ -278,6 +257,8 @@ extern "C" AION_API aion_status aion_get_config(const aion_ctx* ctx, aion_config
 
 extern "C" AION_API const float* aion_logits_dev(const aion_ctx* ctx) { return ctx ? ctx->logits : nullptr; }
 
+extern "C" AION_API void* aion_stream(const aion_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
 // Byte size of an int4 checkpoint for a header, 64-bit.
 static long long int4_file_bytes(const aion_config& c) {
     long long dim = c.dim, hid = c.hidden_dim, L = c.n_layers, nh = c.n_heads, nkv = c.n_kv_heads,
@@ -289,91 +270,59 @@ static long long int4_file_bytes(const aion_config& c) {
 }
 
 // ---------------------------------------------------------------------------
-// One decode step: the kernel sequence of transformer() (src/kernel_simd.c:
-// 1014-1169) with the matvecs fused to their neighbours:
-//   embed | per layer: [rmsnorm + QKV + RoPE + KV append] [attention]
-//   [wo + residual] [rmsnorm + w1/w3 + SwiGLU] [w2 + residual]
-//   | [final rmsnorm + classifier + argmax]
+// Decode launches
 // ---------------------------------------------------------------------------
-static cudaError_t enqueue_step(aion_ctx* c) {
-    cudaError_t e;
-    cudaStream_t st = c->stream;
-    EmbedArgs ea;
-    ea.emb = c->emb.w;
-    ea.tile_bytes = c->emb.tile_bytes;
-    ea.dim = (int)c->dim;
-    ea.vocab = (int)c->vocab;
-    ea.max_pos = c->max_pos;
-    ea.x = c->x;
-    ea.step = c->step;
-    ea.argmax = c->argmax;
-    ea.history = c->history;
-    if ((e = launch(k_embed, dim3(1), dim3(256), 0, st, true, ea)) != cudaSuccess) return e;
+template <int MODE>
+static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
+    DecodeArgs a;
+    a.ops = c->ops;
+    a.nops = c->nops;
+    a.emb = c->emb;
+    a.dim = (int)c->dim;
+    a.hidden = (int)c->hidden;
+    a.n_layers = (int)c->L;
+    a.n_heads = (int)c->nh;
+    a.kv_mul = (int)c->kv_mul;
+    a.head_size = (int)c->hs;
+    a.kv_dim = (int)c->kv_dim;
+    a.vocab = (int)c->vocab;
+    a.max_pos = c->max_pos;
+    a.rms_att = c->rms_att;
+    a.rms_ffn = c->rms_ffn;
+    a.rms_final = c->rms_final;
+    a.freq_re = c->freq_re;
+    a.freq_im = c->freq_im;
+    a.x = c->x;
+    a.q = c->q;
+    a.att = c->att;
+    a.hb = c->hb;
+    a.logits = c->logits;
+    a.kcache = c->kcache;
+    a.vcache = c->vcache;
+    a.attn_part = c->attn_part;
+    a.attn_cnt = c->attn_cnt;
+    a.max_chunks = c->max_chunks;
+    a.step = c->step;
+    a.argmax = c->argmax;
+    a.history = c->history;
+    a.steps = steps;
+    a.P = c->plan.P;
+    a.slot_bytes = c->plan.slot_bytes;
+    a.xbytes = c->plan.xbytes;
+    // The grid-barrier counter starts from zero in every launch.
+    cudaError_t e = cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream);
+    if (e != cudaSuccess) return e;
+    return launch_ex(k_decode<MODE>, dim3(c->grid), dim3(kThreads), (size_t)c->plan.total, c->stream, false, true, a);
+}
 
-    const size_t layer_kv = (size_t)c->max_pos * c->kv_dim;
-    for (long long l = 0; l < c->L; l++) {
-        MatvecArgs a = {};
-        a.x = c->x;
-        a.norm_w = c->rms_att + l * c->dim;
-        a.q_out = c->q;
-        a.kcache = c->kcache + l * layer_kv;
-        a.vcache = c->vcache + l * layer_kv;
-        a.freq_re = c->freq_re;
-        a.freq_im = c->freq_im;
-        a.dim = (int)c->dim;
-        a.kv_dim = (int)c->kv_dim;
-        a.head_size = (int)c->hs;
-        a.step = c->step;
-        if ((e = launch_matvec(c->mode, PRO_RMSNORM, EPI_QKV, c->qkv[l], a, c->dev, st, true)) != cudaSuccess) return e;
-
-        AttnArgs aa;
-        aa.q = c->q;
-        aa.kcache = c->kcache + l * layer_kv;
-        aa.vcache = c->vcache + l * layer_kv;
-        aa.out = c->att;
-        aa.partial = c->attn_partial;
-        aa.counters = c->attn_counters;
-        aa.step = c->step;
-        aa.n_heads = (int)c->nh;
-        aa.kv_mul = (int)c->kv_mul;
-        aa.head_size = (int)c->hs;
-        aa.kv_dim = (int)c->kv_dim;
-        aa.split_len = c->split_len;
-        aa.n_splits = c->n_splits;
-        if ((e = launch(k_attention, dim3((unsigned)c->nh, (unsigned)c->n_splits), dim3(kAttnThreads), 0, st, true, aa)) !=
-            cudaSuccess)
-            return e;
-
-        MatvecArgs o = {};
-        o.x = c->att;
-        o.y = c->x;
-        if ((e = launch_matvec(c->mode, PRO_PLAIN, EPI_RESIDUAL, c->wo[l], o, c->dev, st, true)) != cudaSuccess) return e;
-
-        MatvecArgs f = {};
-        f.x = c->x;
-        f.norm_w = c->rms_ffn + l * c->dim;
-        f.y = c->hb;
-        f.d = (int)c->hidden;
-        if ((e = launch_matvec(c->mode, PRO_RMSNORM, EPI_SWIGLU, c->w13[l], f, c->dev, st, true)) != cudaSuccess) return e;
-
-        MatvecArgs d = {};
-        d.x = c->hb;
-        d.y = c->x;
-        if ((e = launch_matvec(c->mode, PRO_PLAIN, EPI_RESIDUAL, c->w2[l], d, c->dev, st, true)) != cudaSuccess) return e;
-    }
-    MatvecArgs z = {};
-    z.x = c->x;
-    z.norm_w = c->rms_final;
-    z.y = c->logits;
-    z.argmax = c->argmax;
-    z.step = c->step;
-    return launch_matvec(c->mode, PRO_RMSNORM, EPI_LOGITS, c->emb, z, c->dev, st, true);
+static cudaError_t launch_decode(aion_ctx* c, int steps) {
+    return c->mode == MODE_W4A8 ? launch_decode_mode<MODE_W4A8>(c, steps) : launch_decode_mode<MODE_W4A16>(c, steps);
 }
 
 static aion_status build_graph(aion_ctx* c) {
     if (c->gexec) return AION_OK;
     CK_RET(&c->err, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t e = enqueue_step(c);
+    cudaError_t e = launch_decode(c, 1);
     cudaGraph_t g = nullptr;
     cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
     if (e != cudaSuccess || e2 != cudaSuccess) {
@@ -387,15 +336,31 @@ static aion_status build_graph(aion_ctx* c) {
     return AION_OK;
 }
 
-static aion_status run_step(aion_ctx* c) {
-    if (c->opts.use_graph) {
+// Enqueues `steps` decode steps: one graph replay when steps == 1 and graphs
+// are on, else one launch that runs all steps.
+static aion_status enqueue_steps(aion_ctx* c, int steps) {
+    if (steps <= 0) return AION_OK;
+    if (steps == 1 && c->opts.use_graph) {
         aion_status s = build_graph(c);
         if (s != AION_OK) return s;
         CK_RET(&c->err, cudaGraphLaunch(c->gexec, c->stream));
-    } else {
-        CK_RET(&c->err, enqueue_step(c));
+        return AION_OK;
     }
+    CK_RET(&c->err, launch_decode(c, steps));
     return AION_OK;
+}
+
+static aion_status check_device_error(aion_ctx* c) {
+    CK_RET(&c->err, cudaMemcpy(c->h_step, c->step, sizeof(StepState), cudaMemcpyDeviceToHost));
+    switch (c->h_step->error) {
+    case DEV_OK: return AION_OK;
+    case DEV_BAD_INPUT:
+        set_err(&c->err, "a decode step rejected its token or position");
+        return AION_ERR_STATE;
+    default:
+        set_err(&c->err, "a bounded device wait gave up (code %d); call aion_reset", c->h_step->error);
+        return AION_ERR_TIMEOUT;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -412,35 +377,12 @@ static aion_status validate_config(const aion_config& c, std::string* err) {
         return AION_ERR_SHAPE;
     }
     const long long hs = c.dim / c.n_heads, kv = (long long)c.dim * c.n_kv_heads / c.n_heads;
-    if (hs % 2 || hs > kMaxHeadSize || c.dim % 32 || c.hidden_dim % 32 || kv % 32) {
-        set_err(err, "unsupported shape: head_size %lld, dim %d, hidden %d, kv_dim %lld (need even head_size <= %d, "
-                     "multiples of 32)", hs, c.dim, c.hidden_dim, kv, kMaxHeadSize);
+    if (hs % 4 || hs > kMaxHead || c.dim % 32 || c.hidden_dim % 32 || kv % 32) {
+        set_err(err,
+                "unsupported shape: head_size %lld, dim %d, hidden %d, kv_dim %lld (need head_size a multiple of 4, "
+                "<= %d; dim, hidden, kv_dim multiples of 32)",
+                hs, c.dim, c.hidden_dim, kv, kMaxHead);
         return AION_ERR_SHAPE;
-    }
-    return AION_OK;
-}
-
-static aion_status upload_range(aion_ctx* c, int fd, long long off, long long bytes, uint8_t* dst, uint8_t* pinned[2],
-                                cudaEvent_t ev[2], size_t chunk) {
-    long long done = 0;
-    int i = 0;
-    while (done < bytes) {
-        size_t n = (size_t)((bytes - done) < (long long)chunk ? (bytes - done) : (long long)chunk);
-        CK_RET(&c->err, cudaEventSynchronize(ev[i]));
-        size_t got = 0;
-        while (got < n) {
-            ssize_t r = pread(fd, pinned[i] + got, n - got, (off_t)(off + done + (long long)got));
-            if (r < 0 && errno == EINTR) continue;
-            if (r <= 0) {
-                set_err(&c->err, "read failed at offset %lld: %s", off + done, r < 0 ? strerror(errno) : "end of file");
-                return AION_ERR_IO;
-            }
-            got += (size_t)r;
-        }
-        CK_RET(&c->err, cudaMemcpyAsync(dst + done, pinned[i], n, cudaMemcpyHostToDevice, c->stream));
-        CK_RET(&c->err, cudaEventRecord(ev[i], c->stream));
-        done += (long long)n;
-        i ^= 1;
     }
     return AION_OK;
 }
@@ -476,6 +418,52 @@ static aion_status read_header(const char* path, aion_config* cfg, std::string* 
     return s;
 }
 
+static aion_status upload_range(aion_ctx* c, int fd, long long off, long long bytes, uint8_t* dst, uint8_t* pinned[2],
+                                cudaEvent_t ev[2], size_t chunk) {
+    long long done = 0;
+    int i = 0;
+    while (done < bytes) {
+        size_t n = (size_t)std::min<long long>(bytes - done, (long long)chunk);
+        CK_RET(&c->err, cudaEventSynchronize(ev[i]));
+        size_t got = 0;
+        while (got < n) {
+            ssize_t r = pread(fd, pinned[i] + got, n - got, (off_t)(off + done + (long long)got));
+            if (r < 0 && errno == EINTR) continue;
+            if (r <= 0) {
+                set_err(&c->err, "read failed at offset %lld: %s", off + done, r < 0 ? strerror(errno) : "end of file");
+                return AION_ERR_IO;
+            }
+            got += (size_t)r;
+        }
+        CK_RET(&c->err, cudaMemcpyAsync(dst + done, pinned[i], n, cudaMemcpyHostToDevice, c->stream));
+        CK_RET(&c->err, cudaEventRecord(ev[i], c->stream));
+        done += (long long)n;
+        i ^= 1;
+    }
+    return AION_OK;
+}
+
+template <int MODE>
+static aion_status setup_decode_kernel(aion_ctx* c, int max_n, int max_chunk) {
+    const DevInfo& di = dev_info(c->dev);
+    cudaFuncAttributes fa;
+    CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode<MODE>));
+    c->plan = plan_smem(max_n, max_chunk, MODE, di.smem_optin, (int)fa.sharedSizeBytes);
+    if (c->plan.P < 2) {
+        set_err(&c->err, "shared memory too small for the decode rings (P = %d)", c->plan.P);
+        return AION_ERR_SHAPE;
+    }
+    CK_RET(&c->err, cudaFuncSetAttribute(k_decode<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->plan.total));
+    int nb = 0;
+    CK_RET(&c->err, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_decode<MODE>, kThreads, c->plan.total));
+    if (nb < 1) {
+        set_err(&c->err, "decode kernel cannot be resident (smem %d)", c->plan.total);
+        return AION_ERR_CUDA;
+    }
+    c->grid = di.sms;
+    return AION_OK;
+}
+
 static aion_status load_impl(aion_ctx* c, const char* path) {
     int fd = open(path, O_RDONLY);
     if (fd < 0) {
@@ -497,30 +485,34 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             s = AION_ERR_ARG;
             break;
         }
-        c->split_len = 64;
-        c->n_splits = (c->max_pos + c->split_len - 1) / c->split_len;
-
-        // Arena: weights + fp32 tensors + KV cache + activations + scratch.
+        c->max_chunks = (c->max_pos + kAttnLen - 1) / kAttnLen;
         const long long dim = c->dim, hid = c->hidden, L = c->L, kv = c->kv_dim;
-        size_t bytes = align256(tiled_bytes(c->vocab, (int)dim));
-        bytes += L * (align256(tiled_bytes(dim + 2 * kv, (int)dim)) + align256(tiled_bytes(dim, (int)dim)) +
-                      align256(tiled_bytes(2 * hid, (int)dim)) + align256(tiled_bytes(dim, (int)hid)));
+
+        // Matrix layouts (pointers filled below).
+        c->emb = make_desc(nullptr, c->vocab, (int)dim);
+        MatDesc dq = make_desc(nullptr, dim + 2 * kv, (int)dim), dwo = make_desc(nullptr, dim, (int)dim);
+        MatDesc d13 = make_desc(nullptr, 2 * hid, (int)dim), d2 = make_desc(nullptr, dim, (int)hid);
+
+        size_t bytes = align256(desc_bytes(c->emb));
+        bytes += L * (align256(desc_bytes(dq)) + align256(desc_bytes(dwo)) + align256(desc_bytes(d13)) +
+                      align256(desc_bytes(d2)));
         bytes += align256(L * dim * 4) * 2 + align256(dim * 4) + 2 * align256(c->seq * (c->hs / 2) * 4);
         bytes += 2 * align256((size_t)L * c->max_pos * kv * 4);
         bytes += 3 * align256(dim * 4) + align256(hid * 4) + align256(c->vocab * 4);
-        bytes += align256((size_t)c->nh * c->n_splits * (c->hs + 2) * 4) + align256(c->nh * 4);
+        bytes += align256((size_t)c->nh * c->max_chunks * (c->hs + 2) * 4) + align256(c->nh * 4);
         bytes += align256(sizeof(StepState)) + align256(8) + align256((size_t)c->max_pos * 4);
+        bytes += align256((size_t)(4 * L + 1) * sizeof(OpDesc));
         c->arena_bytes = bytes + 4096;
         CK_RET(&c->err, cudaMalloc(&c->arena, c->arena_bytes));
         CK_RET(&c->err, cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream));
 
-        dev_matrix_init(&c->emb, arena_take(c, tiled_bytes(c->vocab, (int)dim)), c->vocab, (int)dim);
-        c->qkv.resize(L); c->wo.resize(L); c->w13.resize(L); c->w2.resize(L);
+        c->emb.w = arena_take(c, desc_bytes(c->emb));
+        c->qkv.assign(L, dq); c->wo.assign(L, dwo); c->w13.assign(L, d13); c->w2.assign(L, d2);
         for (long long l = 0; l < L; l++) {
-            dev_matrix_init(&c->qkv[l], arena_take(c, tiled_bytes(dim + 2 * kv, (int)dim)), dim + 2 * kv, (int)dim);
-            dev_matrix_init(&c->wo[l], arena_take(c, tiled_bytes(dim, (int)dim)), dim, (int)dim);
-            dev_matrix_init(&c->w13[l], arena_take(c, tiled_bytes(2 * hid, (int)dim)), 2 * hid, (int)dim);
-            dev_matrix_init(&c->w2[l], arena_take(c, tiled_bytes(dim, (int)hid)), dim, (int)hid);
+            c->qkv[l].w = arena_take(c, desc_bytes(dq));
+            c->wo[l].w = arena_take(c, desc_bytes(dwo));
+            c->w13[l].w = arena_take(c, desc_bytes(d13));
+            c->w2[l].w = arena_take(c, desc_bytes(d2));
         }
         c->rms_att = (float*)arena_take(c, L * dim * 4);
         c->rms_ffn = (float*)arena_take(c, L * dim * 4);
@@ -534,23 +526,20 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         c->att = (float*)arena_take(c, dim * 4);
         c->hb = (float*)arena_take(c, hid * 4);
         c->logits = (float*)arena_take(c, c->vocab * 4);
-        c->attn_partial = (float*)arena_take(c, (size_t)c->nh * c->n_splits * (c->hs + 2) * 4);
-        c->attn_counters = (int*)arena_take(c, c->nh * 4);
+        c->attn_part = (float*)arena_take(c, (size_t)c->nh * c->max_chunks * (c->hs + 2) * 4);
+        c->attn_cnt = (int*)arena_take(c, c->nh * 4);
         c->step = (StepState*)arena_take(c, sizeof(StepState));
         c->argmax = (unsigned long long*)arena_take(c, 8);
         c->history = (int32_t*)arena_take(c, (size_t)c->max_pos * 4);
-        if (!c->history) {
+        c->ops = (OpDesc*)arena_take(c, (size_t)(4 * L + 1) * sizeof(OpDesc));
+        if (!c->ops) {
             set_err(&c->err, "internal: arena too small");
             s = AION_ERR_OOM;
             break;
         }
 
-        // Largest quantized stacked tensor: the staging area for re-tiling.
         auto qb = [](long long cnt) { return cnt / 32 * 4 + cnt / 2; };
-        long long stage = qb(c->vocab * dim);
-        stage = std::max(stage, qb(L * dim * hid));
-        stage = std::max(stage, qb(L * dim * dim));
-        stage = std::max(stage, L * dim * 4);
+        long long stage = std::max({qb(c->vocab * dim), qb(L * dim * hid), qb(L * dim * dim)});
         CK_RET(&c->err, cudaMalloc(&staging, (size_t)stage));
         CK_RET(&c->err, cudaHostAlloc(&pinned[0], chunk, cudaHostAllocDefault));
         CK_RET(&c->err, cudaHostAlloc(&pinned[1], chunk, cudaHostAllocDefault));
@@ -561,14 +550,12 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
 
         long long off = 28;
         // Walks the file in the order of quantize.c:192-229 /
-        // src/kernel_simd.c:970-986; `fn` re-tiles or copies each tensor.
+        // src/kernel_simd.c:970-986; `fn` re-tiles each quantized tensor.
         auto qtensor = [&](long long count, auto fn) -> aion_status {
-            long long b = qb(count);
+            const long long b = qb(count);
             aion_status r = upload_range(c, fd, off, b, staging, pinned, ev, chunk);
             if (r != AION_OK) return r;
-            const float* sc = (const float*)staging;
-            const uint8_t* pk = staging + count / 32 * 4;
-            cudaError_t e = fn(sc, pk);
+            cudaError_t e = fn((const float*)staging, staging + count / 32 * 4);
             if (e != cudaSuccess) {
                 set_err(&c->err, "re-tile failed: %s", cudaGetErrorString(e));
                 return AION_ERR_CUDA;
@@ -581,12 +568,12 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             off += count * 4;
             return r;
         };
-        auto per_layer = [&](long long rows, long long n, std::vector<DevMatrix>& dst, int row_offset, int interleave,
+        auto per_layer = [&](long long rows, long long n, std::vector<MatDesc>* dst, int row_offset, int interleave,
                              int slot) {
-            return [&, rows, n, row_offset, interleave, slot](const float* sc, const uint8_t* pk) -> cudaError_t {
+            return [c, L, rows, n, dst, row_offset, interleave, slot](const float* sc, const uint8_t* pk) -> cudaError_t {
                 for (long long l = 0; l < L; l++) {
-                    long long e0 = l * rows * n;
-                    cudaError_t e = retile(dst[l], sc + e0 / 32, pk + e0 / 2, rows, row_offset, interleave, slot, 0,
+                    const long long e0 = l * rows * n;
+                    cudaError_t e = retile((*dst)[l], sc + e0 / 32, pk + e0 / 2, rows, row_offset, interleave, slot, 0,
                                            c->stream);
                     if (e != cudaSuccess) return e;
                 }
@@ -598,14 +585,14 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
                  return e != cudaSuccess ? e : fill_pad(c->emb, c->stream);
              })) != AION_OK) break;
         if ((s = ftensor(L * dim, c->rms_att)) != AION_OK) break;
-        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, c->qkv, 0, 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, c->qkv, (int)dim, 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, c->qkv, (int)(dim + kv), 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, c->wo, 0, 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, &c->qkv, 0, 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, &c->qkv, (int)dim, 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, &c->qkv, (int)(dim + kv), 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, &c->wo, 0, 0, 0))) != AION_OK) break;
         if ((s = ftensor(L * dim, c->rms_ffn)) != AION_OK) break;
-        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, c->w13, 0, 1, 0))) != AION_OK) break;
-        if ((s = qtensor(L * hid * dim, per_layer(dim, hid, c->w2, 0, 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, c->w13, 0, 1, 1))) != AION_OK) break;
+        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, &c->w13, 0, 1, 0))) != AION_OK) break;
+        if ((s = qtensor(L * hid * dim, per_layer(dim, hid, &c->w2, 0, 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, &c->w13, 0, 1, 1))) != AION_OK) break;
         if ((s = ftensor(dim, c->rms_final)) != AION_OK) break;
         if ((s = ftensor(c->seq * (c->hs / 2), c->freq_re)) != AION_OK) break;
         if ((s = ftensor(c->seq * (c->hs / 2), c->freq_im)) != AION_OK) break;
@@ -615,10 +602,30 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             if (e == cudaSuccess) e = fill_pad(c->w2[l], c->stream);
             CK_RET(&c->err, e);
         }
+
+        // Op table of one token.
+        std::vector<OpDesc> ops;
+        int max_chunk = 0;
+        for (long long l = 0; l < L; l++) {
+            ops.push_back({c->qkv[l], OP_QKV, (int)l});
+            ops.push_back({c->wo[l], OP_WO, (int)l});
+            ops.push_back({c->w13[l], OP_W13, (int)l});
+            ops.push_back({c->w2[l], OP_W2, (int)l});
+        }
+        ops.push_back({c->emb, OP_CLS, 0});
+        for (const OpDesc& o : ops) max_chunk = std::max(max_chunk, o.m.chunk_bytes);
+        c->nops = (int)ops.size();
+        CK_RET(&c->err, cudaMemcpyAsync(c->ops, ops.data(), ops.size() * sizeof(OpDesc), cudaMemcpyHostToDevice,
+                                        c->stream));
+        const int max_n = (int)std::max(dim, hid);
+        s = c->mode == MODE_W4A8 ? setup_decode_kernel<MODE_W4A8>(c, max_n, max_chunk)
+                                 : setup_decode_kernel<MODE_W4A16>(c, max_n, max_chunk);
+        if (s != AION_OK) break;
+
         // Step state: pos 0, no forced token, argmax key at its initial value.
         StepState init = {};
         init.forced_token = -1;
-        unsigned long long key0 = argmax_key(-1e9f, 0);
+        const unsigned long long key0 = argmax_key(-1e9f, 0);
         CK_RET(&c->err, cudaMemcpyAsync(c->step, &init, sizeof(init), cudaMemcpyHostToDevice, c->stream));
         CK_RET(&c->err, cudaMemcpyAsync(c->argmax, &key0, 8, cudaMemcpyHostToDevice, c->stream));
         CK_RET(&c->err, cudaStreamSynchronize(c->stream));
@@ -659,7 +666,6 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
     }
     cudaError_t e = cudaSetDevice(c->dev);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = raise_smem_limits();
     if (e == cudaSuccess) e = cudaHostAlloc(&c->h_step, sizeof(StepState), cudaHostAllocDefault);
     if (e != cudaSuccess) {
         set_err(&c->err, "CUDA init failed: %s", cudaGetErrorString(e));
@@ -676,6 +682,16 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
     return AION_OK;
 }
 
+static aion_status set_step(aion_ctx* c, int32_t token, int32_t pos) {
+    memset(c->h_step, 0, sizeof(StepState));
+    c->h_step->pos_next = pos;
+    c->h_step->forced_token = token;
+    // The pinned host buffer is reused: wait for the copy before returning.
+    CK_RET(&c->err, cudaMemcpyAsync(c->step, c->h_step, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    return AION_OK;
+}
+
 extern "C" AION_API aion_status aion_forward(aion_ctx* c, int32_t token, int32_t pos, float* logits_host) {
     if (!c) return AION_ERR_ARG;
     if (token < 0 || token >= c->vocab || pos < 0 || pos >= c->max_pos) {
@@ -684,16 +700,13 @@ extern "C" AION_API aion_status aion_forward(aion_ctx* c, int32_t token, int32_t
         return AION_ERR_ARG;
     }
     CK_RET(&c->err, cudaSetDevice(c->dev));
-    memset(c->h_step, 0, sizeof(StepState));
-    c->h_step->pos_next = pos;
-    c->h_step->forced_token = token;
-    CK_RET(&c->err, cudaMemcpyAsync(c->step, c->h_step, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
-    aion_status s = run_step(c);
+    aion_status s = set_step(c, token, pos);
+    if (s == AION_OK) s = enqueue_steps(c, 1);
     if (s != AION_OK) return s;
     if (logits_host)
         CK_RET(&c->err, cudaMemcpyAsync(logits_host, c->logits, c->vocab * 4, cudaMemcpyDeviceToHost, c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
-    return AION_OK;
+    return check_device_error(c);
 }
 
 extern "C" AION_API aion_status aion_generate(aion_ctx* c, int32_t bos, int32_t steps, int32_t* tokens_out,
@@ -705,40 +718,24 @@ extern "C" AION_API aion_status aion_generate(aion_ctx* c, int32_t bos, int32_t 
         return AION_ERR_ARG;
     }
     CK_RET(&c->err, cudaSetDevice(c->dev));
-    memset(c->h_step, 0, sizeof(StepState));
-    c->h_step->pos_next = 0;
-    c->h_step->forced_token = bos;
-    CK_RET(&c->err, cudaMemcpyAsync(c->step, c->h_step, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
-    if (c->opts.use_graph) {
-        aion_status s = build_graph(c);
-        if (s != AION_OK) return s;
-    }
-    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    aion_status s = set_step(c, bos, 0);
+    if (s != AION_OK) return s;
     struct timespec t0, t1;
     clock_gettime(CLOCK_MONOTONIC, &t0);
-    for (int i = 0; i < steps; i++) {
-        aion_status s = run_step(c);
-        if (s != AION_OK) return s;
-    }
+    s = enqueue_steps(c, steps);
+    if (s != AION_OK) return s;
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     clock_gettime(CLOCK_MONOTONIC, &t1);
     if (seconds) *seconds = (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
     if (tokens_out && steps > 0)
         CK_RET(&c->err, cudaMemcpy(tokens_out, c->history, (size_t)steps * 4, cudaMemcpyDeviceToHost));
-    CK_RET(&c->err, cudaMemcpy(c->h_step, c->step, sizeof(StepState), cudaMemcpyDeviceToHost));
-    if (c->h_step->error) {
-        set_err(&c->err, "a decode step rejected its token or position");
-        return AION_ERR_STATE;
-    }
-    return AION_OK;
+    return check_device_error(c);
 }
 
-extern "C" AION_API void* aion_stream(const aion_ctx* c) { return c ? (void*)c->stream : nullptr; }
-
-extern "C" AION_API aion_status aion_step_async(aion_ctx* c, int32_t token, int32_t pos) {
-    if (!c) return AION_ERR_ARG;
+extern "C" AION_API aion_status aion_decode_async(aion_ctx* c, int32_t token, int32_t pos, int32_t steps) {
+    if (!c || steps < 0) return AION_ERR_ARG;
     if (token >= c->vocab || pos >= c->max_pos) {
-        set_err(&c->err, "aion_step_async: token %d or pos %d out of range", token, pos);
+        set_err(&c->err, "aion_decode_async: token %d or pos %d out of range", token, pos);
         return AION_ERR_ARG;
     }
     CK_RET(&c->err, cudaSetDevice(c->dev));
@@ -746,7 +743,7 @@ extern "C" AION_API aion_status aion_step_async(aion_ctx* c, int32_t token, int3
         k_set_step<<<1, 32, 0, c->stream>>>(c->step, pos, token);
         CK_RET(&c->err, cudaGetLastError());
     }
-    return run_step(c);
+    return enqueue_steps(c, steps);
 }
 
 extern "C" AION_API aion_status aion_tokens(aion_ctx* c, int32_t* out, int32_t n) {
@@ -754,82 +751,7 @@ extern "C" AION_API aion_status aion_tokens(aion_ctx* c, int32_t* out, int32_t n
     CK_RET(&c->err, cudaSetDevice(c->dev));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     if (n) CK_RET(&c->err, cudaMemcpy(out, c->history, (size_t)n * 4, cudaMemcpyDeviceToHost));
-    return AION_OK;
-}
-
-// Times each kernel class of the decode step in isolation on the context's
-// stream: for every class the per-layer launches of all layers run back to
-// back `reps` times between two events; out_ms[k] receives the mean time of
-// one launch.  Classes: 0 rmsnorm+QKV+RoPE, 1 attention, 2 wo+residual,
-// 3 rmsnorm+w1/w3+SwiGLU, 4 w2+residual, 5 rmsnorm+classifier+argmax,
-// 6 embed.  Clobbers the activations and the KV cache row of the current
-// position; call it between sequences.
-extern "C" AION_API aion_status aion_time_kernels(aion_ctx* c, int32_t reps, float* out_ms) {
-    if (!c || !out_ms || reps <= 0) return AION_ERR_ARG;
-    CK_RET(&c->err, cudaSetDevice(c->dev));
-    cudaEvent_t e0, e1;
-    CK_RET(&c->err, cudaEventCreate(&e0));
-    CK_RET(&c->err, cudaEventCreate(&e1));
-    const size_t layer_kv = (size_t)c->max_pos * c->kv_dim;
-    aion_status status = AION_OK;
-    for (int k = 0; k < 7 && status == AION_OK; k++) {
-        cudaError_t e = cudaEventRecord(e0, c->stream);
-        int launches = 0;
-        for (int r = 0; r < reps && e == cudaSuccess; r++) {
-            const long long nl = (k == 5 || k == 6) ? 1 : c->L;
-            for (long long l = 0; l < nl && e == cudaSuccess; l++) {
-                launches++;
-                if (k == 0) {
-                    MatvecArgs a = {};
-                    a.x = c->x; a.norm_w = c->rms_att + l * c->dim; a.q_out = c->q;
-                    a.kcache = c->kcache + l * layer_kv; a.vcache = c->vcache + l * layer_kv;
-                    a.freq_re = c->freq_re; a.freq_im = c->freq_im; a.dim = (int)c->dim; a.kv_dim = (int)c->kv_dim;
-                    a.head_size = (int)c->hs; a.step = c->step;
-                    e = launch_matvec(c->mode, PRO_RMSNORM, EPI_QKV, c->qkv[l], a, c->dev, c->stream, true);
-                } else if (k == 1) {
-                    AttnArgs aa;
-                    aa.q = c->q; aa.kcache = c->kcache + l * layer_kv; aa.vcache = c->vcache + l * layer_kv;
-                    aa.out = c->att; aa.partial = c->attn_partial; aa.counters = c->attn_counters; aa.step = c->step;
-                    aa.n_heads = (int)c->nh; aa.kv_mul = (int)c->kv_mul; aa.head_size = (int)c->hs;
-                    aa.kv_dim = (int)c->kv_dim; aa.split_len = c->split_len; aa.n_splits = c->n_splits;
-                    e = launch(k_attention, dim3((unsigned)c->nh, (unsigned)c->n_splits), dim3(kAttnThreads), 0,
-                               c->stream, true, aa);
-                } else if (k == 2 || k == 4) {
-                    MatvecArgs o = {};
-                    o.x = k == 2 ? c->att : c->hb;
-                    o.y = c->x;
-                    e = launch_matvec(c->mode, PRO_PLAIN, EPI_RESIDUAL, k == 2 ? c->wo[l] : c->w2[l], o, c->dev,
-                                      c->stream, true);
-                } else if (k == 3) {
-                    MatvecArgs f = {};
-                    f.x = c->x; f.norm_w = c->rms_ffn + l * c->dim; f.y = c->hb; f.d = (int)c->hidden;
-                    e = launch_matvec(c->mode, PRO_RMSNORM, EPI_SWIGLU, c->w13[l], f, c->dev, c->stream, true);
-                } else if (k == 5) {
-                    MatvecArgs z = {};
-                    z.x = c->x; z.norm_w = c->rms_final; z.y = c->logits; z.argmax = c->argmax; z.step = c->step;
-                    e = launch_matvec(c->mode, PRO_RMSNORM, EPI_LOGITS, c->emb, z, c->dev, c->stream, true);
-                } else {
-                    EmbedArgs ea;
-                    ea.emb = c->emb.w; ea.tile_bytes = c->emb.tile_bytes; ea.dim = (int)c->dim;
-                    ea.vocab = (int)c->vocab; ea.max_pos = c->max_pos; ea.x = c->x; ea.step = c->step;
-                    ea.argmax = c->argmax; ea.history = c->history;
-                    e = launch(k_embed, dim3(1), dim3(256), 0, c->stream, true, ea);
-                }
-            }
-        }
-        if (e == cudaSuccess) e = cudaEventRecord(e1, c->stream);
-        if (e == cudaSuccess) e = cudaEventSynchronize(e1);
-        float ms = 0.0f;
-        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
-        if (e != cudaSuccess) {
-            set_err(&c->err, "aion_time_kernels: %s", cudaGetErrorString(e));
-            status = cuda_status(e);
-        }
-        out_ms[k] = ms / (float)launches;
-    }
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    return status;
+    return check_device_error(c);
 }
 
 extern "C" AION_API aion_status aion_reset(aion_ctx* c) {
@@ -838,6 +760,8 @@ extern "C" AION_API aion_status aion_reset(aion_ctx* c) {
     const size_t kvb = (size_t)c->L * c->max_pos * c->kv_dim * 4;
     CK_RET(&c->err, cudaMemsetAsync(c->kcache, 0, kvb, c->stream));
     CK_RET(&c->err, cudaMemsetAsync(c->vcache, 0, kvb, c->stream));
+    CK_RET(&c->err, cudaMemsetAsync(&c->step->error, 0, sizeof(int32_t), c->stream));
+    CK_RET(&c->err, cudaMemsetAsync(c->attn_cnt, 0, c->nh * 4, c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return AION_OK;
 }
@@ -847,43 +771,43 @@ extern "C" AION_API aion_status aion_reset(aion_ctx* c) {
 // ---------------------------------------------------------------------------
 struct aion_qmatrix {
     int device;
-    DevMatrix m;
+    MatDesc m;
 };
 
 extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const uint8_t* packed, int64_t rows,
                                                     int64_t cols, int32_t device, aion_qmatrix** out) {
-    if (!scales || !packed || !out || rows <= 0 || cols <= 0 || cols % 32 || cols > (1 << 30)) {
+    if (!scales || !packed || !out || rows <= 0 || cols <= 0 || cols % 32 || cols > (1 << 24) || rows > (1 << 28)) {
         set_err(nullptr, "aion_qmatrix_upload: invalid arguments (rows %lld, cols %lld; cols must be a multiple of 32)",
                 (long long)rows, (long long)cols);
         return AION_ERR_ARG;
     }
     *out = nullptr;
     CK_RET(nullptr, cudaSetDevice(device));
-    aion_qmatrix* q = new aion_qmatrix();
-    q->device = device;
+    MatDesc m = make_desc(nullptr, rows, (int)cols);
     uint8_t* w = nullptr;
-    cudaError_t e = cudaMalloc(&w, (size_t)tiled_bytes(rows, (int)cols));
+    cudaError_t e = cudaMalloc(&w, (size_t)desc_bytes(m));
     if (e != cudaSuccess) {
-        delete q;
         set_err(nullptr, "cudaMalloc failed: %s", cudaGetErrorString(e));
         return cuda_status(e);
     }
-    dev_matrix_init(&q->m, w, rows, (int)cols);
+    m.w = w;
     const size_t sb = (size_t)(rows * cols / 32 * 4), pb = (size_t)(rows * cols / 2);
     uint8_t* stage = nullptr;
     e = cudaMalloc(&stage, sb + pb);
     if (e == cudaSuccess) e = cudaMemcpy(stage, scales, sb, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(stage + sb, packed, pb, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = retile(q->m, (const float*)stage, stage + sb, rows, 0, 0, 0, 0, 0);
-    if (e == cudaSuccess) e = fill_pad(q->m, 0);
+    if (e == cudaSuccess) e = retile(m, (const float*)stage, stage + sb, rows, 0, 0, 0, 0, 0);
+    if (e == cudaSuccess) e = fill_pad(m, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (stage) cudaFree(stage);
     if (e != cudaSuccess) {
         cudaFree(w);
-        delete q;
         set_err(nullptr, "aion_qmatrix_upload: %s", cudaGetErrorString(e));
         return cuda_status(e);
     }
+    aion_qmatrix* q = new aion_qmatrix();
+    q->device = device;
+    q->m = m;
     *out = q;
     return AION_OK;
 }
@@ -891,7 +815,7 @@ extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const u
 extern "C" AION_API aion_status aion_qmatrix_download(const aion_qmatrix* q, float* scales, uint8_t* packed) {
     if (!q || !scales || !packed) return AION_ERR_ARG;
     CK_RET(nullptr, cudaSetDevice(q->device));
-    const long long rows = q->m.rows, cols = q->m.n;
+    const long long rows = q->m.d, cols = q->m.n;
     const size_t sb = (size_t)(rows * cols / 32 * 4), pb = (size_t)(rows * cols / 2);
     uint8_t* stage = nullptr;
     cudaError_t e = cudaMalloc(&stage, sb + pb);
@@ -909,7 +833,7 @@ extern "C" AION_API aion_status aion_qmatrix_download(const aion_qmatrix* q, flo
 extern "C" AION_API aion_status aion_qmatrix_free(aion_qmatrix* q) {
     if (!q) return AION_OK;
     cudaSetDevice(q->device);
-    cudaFree(q->m.w);
+    cudaFree((void*)q->m.w);
     delete q;
     return AION_OK;
 }
@@ -924,11 +848,9 @@ static aion_status matvec_api(int mode, const aion_qmatrix* q, const float* x, f
         return AION_ERR_ARG;
     }
     CK_RET(nullptr, cudaSetDevice(q->device));
-    CK_RET(nullptr, raise_smem_limits());
-    MatvecArgs a = {};
-    a.x = x;
-    a.y = y;
-    CK_RET(nullptr, launch_matvec(mode, PRO_PLAIN, EPI_STORE, q->m, a, q->device, (cudaStream_t)stream, false));
+    cudaError_t e = mode == MODE_W4A8 ? launch_standalone<MODE_W4A8>(q->m, x, y, q->device, (cudaStream_t)stream)
+                                      : launch_standalone<MODE_W4A16>(q->m, x, y, q->device, (cudaStream_t)stream);
+    CK_RET(nullptr, e);
     return AION_OK;
 }
 
@@ -945,8 +867,7 @@ extern "C" AION_API aion_status aion_quantize_activations(const float* x, int8_t
         set_err(nullptr, "aion_quantize_activations: invalid arguments (n must be a positive multiple of 32)");
         return AION_ERR_ARG;
     }
-    int grid = (int)((n / 32 + 255) / 256);
-    if (grid > 4096) grid = 4096;
+    int grid = (int)std::min<long long>((n / 32 + 255) / 256, 4096);
     k_quantize_act<<<grid, 256, 0, (cudaStream_t)stream>>>(x, qx, xs, n);
     CK_RET(nullptr, cudaGetLastError());
     return AION_OK;

@@ -1,0 +1,199 @@
+// Shared device helpers for sm_100a: PDL, mbarriers, bulk (TMA) copies,
+// bounded grid barrier, warp reductions, the device-side argmax key and the
+// per-step state.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+namespace aion {
+
+// Error codes a kernel can leave in StepState::error (first one wins).
+enum DeviceError : int32_t {
+    DEV_OK = 0,
+    DEV_BAD_INPUT = 1,       // token or position out of range
+    DEV_BARRIER_TIMEOUT = 2, // a grid barrier wait gave up
+    DEV_COPY_TIMEOUT = 3,    // a bulk-copy mbarrier wait gave up
+};
+
+// Per-step state shared by the kernels of one decode step.  A step takes
+// pos from pos_next, the token from forced_token (>= 0) or from the previous
+// step's argmax key, records the token in the history and publishes
+// pos/token for the rest of the step.
+struct StepState {
+    int32_t pos_next;
+    int32_t forced_token;
+    int32_t pos;
+    int32_t token;
+    int32_t error;
+    uint32_t barrier;        // grid-barrier arrival counter of the persistent decode kernel
+    int32_t pad[2];
+};
+
+// Argmax key: (order-preserving float bits << 32) | (0xFFFFFFFF - index).
+// The max over keys picks the largest logit and, among equal logits, the
+// smallest index: the first-max rule of the reference greedy loop
+// (src/kernel_simd.c:1236-1243).  The initial key encodes (-1e9, index 0).
+__host__ __device__ inline uint32_t order_bits(float f) {
+    uint32_t u;
+#ifdef __CUDA_ARCH__
+    u = __float_as_uint(f);
+#else
+    memcpy(&u, &f, 4);
+#endif
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__host__ __device__ inline unsigned long long argmax_key(float v, uint32_t idx) {
+    return ((unsigned long long)order_bits(v) << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+__host__ __device__ inline uint32_t key_index(unsigned long long k) {
+    return 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Memory helpers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Streaming 128-bit load of data that is constant for the kernel's lifetime.
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk copy (global -> shared, completion counted in bytes).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: false after `limit` unsuccessful polls (each poll itself
+// suspends for a hardware-defined interval).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+    for (uint32_t i = 0; i < limit; i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// ---------------------------------------------------------------------------
+// Grid barrier for a kernel whose CTAs are all co-resident (cooperative
+// launch).  The counter only grows within a launch; barrier k (0-based)
+// completes when it reaches (k + 1) * gridDim.x.  Bounded: after `limit`
+// polls the waiting thread records DEV_BARRIER_TIMEOUT and returns false.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int32_t ld_relaxed_i32(const int32_t* p) {
+    int32_t v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void set_error(StepState* st, int32_t code) { atomicCAS(&st->error, 0, code); }
+
+// All threads of the CTA call this; returns false (uniformly) on timeout or
+// when another CTA already recorded an error.
+__device__ __forceinline__ bool grid_barrier(StepState* st, uint32_t& k, uint32_t limit = (1u << 26)) {
+    __shared__ int s_ok;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        red_release_add(&st->barrier, 1u);
+        const uint32_t target = (k + 1) * gridDim.x;
+        int ok = 1;
+        uint32_t i = 0;
+        while (ld_acquire_u32(&st->barrier) < target) {
+            if (++i > limit || ld_relaxed_i32(&st->error) != 0) {
+                ok = 0;
+                break;
+            }
+        }
+        if (!ok) set_error(st, DEV_BARRIER_TIMEOUT);
+        __threadfence();
+        s_ok = ok;
+    }
+    __syncthreads();
+    k++;
+    return s_ok != 0;
+}
+
+// ---------------------------------------------------------------------------
+// Reductions.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Block-wide sum; every thread receives the result.  red: >= 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0.0f;
+    return warp_sum(t);
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+    v = warp_max(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = (lane < (int)(blockDim.x >> 5)) ? red[lane] : -INFINITY;
+    return warp_max(t);
+}
+
+}  // namespace aion

@@ -6,10 +6,11 @@
 Workload: the 7B shape (dim 4096, hidden 11008, 32 layers, 32 heads, vocab
 32000) with seed-1 random-init N(0, 0.02) weights quantized by the
 quantize.c arithmetic, fp32 activations and KV cache; greedy decode from
-BOS=1 over the 512-token workload.  One step = one decode token (one
-replay of the per-token CUDA graph).  W warm-up tokens take positions
-0..W-1, the K timed tokens continue the same greedy stream (a new
-sequence starts from BOS at position 0 after 512 tokens).  The weights
+BOS=1 over the 512-token workload.  One step = one decode token; the K
+timed steps run in one persistent decode launch (split where the stream
+restarts).  W warm-up tokens take positions 0..W-1, the K timed tokens
+continue the same greedy stream (a new sequence starts from BOS at
+position 0 after 512 tokens).  The weights
 (4.13 GB per token) are far larger than L2, so every step streams them
 from HBM.
 
@@ -225,6 +226,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["aion", "reference"], default="aion")
     ap.add_argument("--matvec", action="store_true", help="isolated matvec shapes only")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-matvec", action="store_true", help="skip the isolated matvec shapes")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -266,13 +268,28 @@ def main() -> None:
     path = ensure_7b(rank)
     model = A.Model(path, device=local)
     L = model.config.n_layers
-    launches_per_step = 5 * L + 2
     stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{local}")
 
+    def decode(count: int, start_pos: int) -> int:
+        """Enqueues `count` greedy steps from start_pos, restarting from BOS
+        at position 0 after the 512-token workload; returns kernel launches."""
+        launches, pos = 0, start_pos
+        while count > 0:
+            if pos >= WORKLOAD_TOKENS:
+                pos = 0
+            n = min(count, WORKLOAD_TOKENS - pos)
+            if pos == 0:
+                model.decode_async(n, BOS, 0)
+                launches += 2            # k_set_step + k_decode
+            else:
+                model.decode_async(n)
+                launches += 1
+            count -= n
+            pos += n
+        return launches
+
     # Warm-up: positions 0..W-1 of the greedy stream.
-    model.step_async(BOS, 0)
-    for _ in range(args.warmup - 1):
-        model.step_async()
+    decode(args.warmup, 0)
     torch.cuda.synchronize()
 
     clocks = Clocks(local)
@@ -281,19 +298,13 @@ def main() -> None:
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    pos = args.warmup
-    for _ in range(args.steps):
-        if pos >= WORKLOAD_TOKENS:
-            model.step_async(BOS, 0)
-            pos = 1
-        else:
-            model.step_async()
-            pos += 1
+    launches = decode(args.steps, args.warmup)
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local)
     tok_s = world * args.steps / (ms * 1e-3)
     stream_tokens = model.tokens(min(args.warmup + args.steps, WORKLOAD_TOKENS))
 
@@ -305,26 +316,25 @@ def main() -> None:
         k = min(len(want), len(stream_tokens))
         parity = {"tokens_compared": k, "identical": stream_tokens[:k] == want[:k]}
 
-    # Per-kernel device times (isolated, CUDA events on the model's stream).
-    kt = model.time_kernels(reps=3)
+    # Roofline of the decode kernel (one persistent launch runs all steps):
+    # algorithmic bytes = int4 weights of every token (+ KV cache reads,
+    # reported separately), over the CUDA-event time of the launches.
     dim, hid, vocab = CFG_7B[0], CFG_7B[1], CFG_7B[5]
-    shapes = {"qkv": (3 * dim, dim), "wo": (dim, dim), "w13": (2 * hid, dim), "w2": (dim, hid),
-              "classifier": (vocab, dim)}
-    per_kernel = {}
-    for k, ms_k in kt.items():
-        share = ms_k * (1 if k in ("classifier", "embed") else L)
-        entry = {"us_per_launch": ms_k * 1e3, "ms_per_step": share}
-        if k in shapes:
-            entry["GBps"] = matvec_bytes(*shapes[k]) / (ms_k * 1e-3) / 1e9
-        per_kernel[k] = entry
-    dominant = max(shapes, key=lambda k: per_kernel[k]["ms_per_step"])
+    kv_bytes = 0
+    pos = args.warmup
+    for _ in range(args.steps):
+        if pos >= WORKLOAD_TOKENS:
+            pos = 0
+        kv_bytes += 2 * L * dim * 4 * (pos + 1)
+        pos += 1
+    weights_gbs = WEIGHT_BYTES_PER_TOKEN * args.steps / (ms_local * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
-    dom = per_kernel[dominant]
-    roofline = {"kernel": f"k_matvec W4A16 ({dominant}: {shapes[dominant][0]}x{shapes[dominant][1]})",
-                "bound": "hbm", "achieved": dom["GBps"], "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                "frac": dom["GBps"] / peak, "traffic": None,
-                "bytes_per_launch": matvec_bytes(*shapes[dominant])}
-    step_gbs = WEIGHT_BYTES_PER_TOKEN * tok_s / world / 1e9
+    roofline = {"kernel": "k_decode<W4A16> (persistent decode, all steps)", "bound": "hbm",
+                "achieved": weights_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": weights_gbs / peak, "traffic": None,
+                "bytes_per_token": WEIGHT_BYTES_PER_TOKEN,
+                "with_kv_GBps": (WEIGHT_BYTES_PER_TOKEN * args.steps + kv_bytes) / (ms_local * 1e-3) / 1e9}
+    matvec = isolated_matvecs(local, reps=5) if (rank == 0 and not args.no_matvec) else None
 
     # End-to-end: the reference-facing call transformer(token, pos) per token
     # with host buffers (token/pos in from pinned memory, logits out to pinned
@@ -359,9 +369,8 @@ def main() -> None:
             "config": {"workload": "llama2-7b-shape W4A16 greedy decode, batch 1, 512-token workload",
                        "dim": dim, "hidden": hid, "layers": L, "heads": 32, "vocab": vocab, "seed": SEED_7B,
                        "parallelism": f"replicas x{world}", "l2": "weights 4.13 GB/token > L2 (no flush needed)"},
-            "weights_GBps_per_gpu": step_gbs, "weights_roofline_frac": step_gbs / peak,
-            "roofline": roofline, "kernels": per_kernel,
-            "gpu_launches": launches_per_step * args.steps,
+            "roofline": roofline, "matvec": matvec,
+            "gpu_launches": launches,
             "clocks": clk,
             "e2e": {"value": world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 32,
                     "d2h_bytes_per_step": vocab * 4},

@@ -101,20 +101,15 @@ AION_API aion_status aion_generate(aion_ctx* ctx, int32_t bos, int32_t steps, in
 /* The context's cudaStream_t (all of its work runs there). */
 AION_API void* aion_stream(const aion_ctx* ctx);
 
-/* Enqueues one decode step on the context's stream without waiting (the
- * asynchronous form of one iteration of aion_generate).  token >= 0 forces
- * the input token, token < 0 takes the previous step's argmax; pos >= 0
- * sets the position, pos < 0 continues at the next one. */
-AION_API aion_status aion_step_async(aion_ctx* ctx, int32_t token, int32_t pos);
+/* Enqueues `steps` greedy decode steps on the context's stream without
+ * waiting (the asynchronous form of aion_generate's loop; one persistent
+ * kernel launch).  token >= 0 forces the input token of the first step,
+ * token < 0 takes the previous step's argmax; pos >= 0 sets the first
+ * position, pos < 0 continues at the next one. */
+AION_API aion_status aion_decode_async(aion_ctx* ctx, int32_t token, int32_t pos, int32_t steps);
 
 /* Copies the input tokens of positions [0, n) recorded on the device. */
 AION_API aion_status aion_tokens(aion_ctx* ctx, int32_t* out, int32_t n);
-
-/* Diagnostics: mean device time of one launch of each kernel class of the
- * decode step, timed in isolation with CUDA events (out_ms[7]: QKV, attention,
- * wo, w1/w3, w2, classifier, embed).  Clobbers activations; no reference
- * counterpart. */
-AION_API aion_status aion_time_kernels(aion_ctx* ctx, int32_t reps, float* out_ms);
 
 /* Clears the KV cache (a new sequence). */
 AION_API aion_status aion_reset(aion_ctx* ctx);
