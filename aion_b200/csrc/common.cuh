@@ -139,7 +139,7 @@ __device__ __forceinline__ void set_error(StepState* st, int32_t code) { atomicC
 
 // All threads of the CTA call this; returns false (uniformly) on timeout or
 // when another CTA already recorded an error.
-__device__ __forceinline__ bool grid_barrier(StepState* st, uint32_t& k, uint32_t limit = (1u << 26)) {
+__device__ __forceinline__ bool grid_barrier(StepState* st, uint32_t& k, uint32_t limit = (1u << 24)) {
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
