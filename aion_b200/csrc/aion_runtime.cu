@@ -86,9 +86,10 @@ struct SmemPlan {
     int xbytes = 0, slot_bytes = 0, P = 0, total = 0;
 };
 
-static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int mode, int smem_optin, int static_bytes) {
+static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int mode, int smem_optin, int static_bytes,
+                          int min_xbytes = 0) {
     SmemPlan p;
-    p.xbytes = round128(xbuf_bytes(max_n, mode));
+    p.xbytes = round128(std::max(xbuf_bytes(max_n, mode), min_xbytes));
     p.slot_bytes = round128(max_chunk_bytes);
     const int avail = smem_optin - static_bytes - 1024 - p.xbytes;
     p.P = std::min(8, avail / (kWarps * p.slot_bytes));
@@ -448,7 +449,9 @@ static aion_status setup_decode_kernel(aion_ctx* c, int max_n, int max_chunk) {
     const DevInfo& di = dev_info(c->dev);
     cudaFuncAttributes fa;
     CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode<MODE>));
-    c->plan = plan_smem(max_n, max_chunk, MODE, di.smem_optin, (int)fa.sharedSizeBytes);
+    // W4A8 runs the reference-order attention, whose scores use the x' area.
+    c->plan = plan_smem(max_n, max_chunk, MODE, di.smem_optin, (int)fa.sharedSizeBytes,
+                        MODE == MODE_W4A8 ? c->max_pos * 4 : 0);
     if (c->plan.P < 2) {
         set_err(&c->err, "shared memory too small for the decode rings (P = %d)", c->plan.P);
         return AION_ERR_SHAPE;
@@ -539,7 +542,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         }
 
         auto qb = [](long long cnt) { return cnt / 32 * 4 + cnt / 2; };
-        long long stage = std::max({qb(c->vocab * dim), qb(L * dim * hid), qb(L * dim * dim)});
+        long long stage = std::max({qb(c->vocab * dim), qb(L * dim * hid), qb(L * dim * dim)}) + 256;
         CK_RET(&c->err, cudaMalloc(&staging, (size_t)stage));
         CK_RET(&c->err, cudaHostAlloc(&pinned[0], chunk, cudaHostAllocDefault));
         CK_RET(&c->err, cudaHostAlloc(&pinned[1], chunk, cudaHostAllocDefault));
@@ -552,10 +555,14 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         // Walks the file in the order of quantize.c:192-229 /
         // src/kernel_simd.c:970-986; `fn` re-tiles each quantized tensor.
         auto qtensor = [&](long long count, auto fn) -> aion_status {
-            const long long b = qb(count);
-            aion_status r = upload_range(c, fd, off, b, staging, pinned, ev, chunk);
+            // Scales, then the packed bytes on a 256-byte boundary (the file
+            // places them right after the scales, at any 4-byte offset).
+            const long long sb = count / 32 * 4, po = (long long)align256((size_t)sb);
+            aion_status r = upload_range(c, fd, off, sb, staging, pinned, ev, chunk);
+            if (r == AION_OK) r = upload_range(c, fd, off + sb, count / 2, staging + po, pinned, ev, chunk);
             if (r != AION_OK) return r;
-            cudaError_t e = fn((const float*)staging, staging + count / 32 * 4);
+            const long long b = qb(count);
+            cudaError_t e = fn((const float*)staging, staging + po);
             if (e != cudaSuccess) {
                 set_err(&c->err, "re-tile failed: %s", cudaGetErrorString(e));
                 return AION_ERR_CUDA;
@@ -791,12 +798,14 @@ extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const u
         return cuda_status(e);
     }
     m.w = w;
-    const size_t sb = (size_t)(rows * cols / 32 * 4), pb = (size_t)(rows * cols / 2);
+    // Packed bytes start on a 256-byte boundary of the staging buffer: the
+    // re-tile moves them as 16-byte vectors.
+    const size_t sb = (size_t)(rows * cols / 32 * 4), pb = (size_t)(rows * cols / 2), po = align256(sb);
     uint8_t* stage = nullptr;
-    e = cudaMalloc(&stage, sb + pb);
+    e = cudaMalloc(&stage, po + pb);
     if (e == cudaSuccess) e = cudaMemcpy(stage, scales, sb, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(stage + sb, packed, pb, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = retile(m, (const float*)stage, stage + sb, rows, 0, 0, 0, 0, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(stage + po, packed, pb, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = retile(m, (const float*)stage, stage + po, rows, 0, 0, 0, 0, 0);
     if (e == cudaSuccess) e = fill_pad(m, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (stage) cudaFree(stage);
@@ -816,12 +825,12 @@ extern "C" AION_API aion_status aion_qmatrix_download(const aion_qmatrix* q, flo
     if (!q || !scales || !packed) return AION_ERR_ARG;
     CK_RET(nullptr, cudaSetDevice(q->device));
     const long long rows = q->m.d, cols = q->m.n;
-    const size_t sb = (size_t)(rows * cols / 32 * 4), pb = (size_t)(rows * cols / 2);
+    const size_t sb = (size_t)(rows * cols / 32 * 4), pb = (size_t)(rows * cols / 2), po = align256(sb);
     uint8_t* stage = nullptr;
-    cudaError_t e = cudaMalloc(&stage, sb + pb);
-    if (e == cudaSuccess) e = retile(q->m, (const float*)stage, stage + sb, rows, 0, 0, 0, 1, 0);
+    cudaError_t e = cudaMalloc(&stage, po + pb);
+    if (e == cudaSuccess) e = retile(q->m, (const float*)stage, stage + po, rows, 0, 0, 0, 1, 0);
     if (e == cudaSuccess) e = cudaMemcpy(scales, stage, sb, cudaMemcpyDeviceToHost);
-    if (e == cudaSuccess) e = cudaMemcpy(packed, stage + sb, pb, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(packed, stage + po, pb, cudaMemcpyDeviceToHost);
     if (stage) cudaFree(stage);
     if (e != cudaSuccess) {
         set_err(nullptr, "aion_qmatrix_download: %s", cudaGetErrorString(e));

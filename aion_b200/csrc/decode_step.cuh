@@ -87,6 +87,32 @@ __device__ __forceinline__ float src_rms_scale(const VecSrc& s, int n, float* re
     return 1.0f / sqrtf(__fdiv_rn(acc, (float)n) + 1e-5f);
 }
 
+// The rmsnorm scale in the reference's own order (src/kernel_simd.c:793-803):
+// four lane sums of x[4m + l]^2 (product rounded, then added), reduced
+// pairwise, then mean, + 1e-5, 1 / sqrtf.  A sequential chain of n/4 adds
+// per lane: used where bit-exact parity with the reference is the contract.
+__device__ __forceinline__ float src_rms_scale_exact(const VecSrc& s, int n, float* red) {
+    if (threadIdx.x < 4) {
+        float acc = 0.0f;
+        for (int i = 0; i < n / 4; i++) {
+            const float4 v = src_load4(s, i);
+            const float e = threadIdx.x == 0 ? v.x : threadIdx.x == 1 ? v.y : threadIdx.x == 2 ? v.z : v.w;
+            acc = __fadd_rn(acc, __fmul_rn(e, e));
+        }
+        red[threadIdx.x] = acc;
+    }
+    __syncthreads();
+    const float sum = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+    __syncthreads();
+    return 1.0f / sqrtf(__fdiv_rn(sum, (float)n) + 1e-5f);
+}
+
+// e^x rounded once to float: the double-precision exponential rounded to
+// the nearest float (CUDA exp() is accurate to < 1 double ulp, so only
+// inputs within ~1e-16 relative of a float rounding boundary can differ
+// from the correctly rounded value).
+__device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+
 template <int MODE>
 __device__ __forceinline__ void src_build_x(unsigned char* xbuf, const VecSrc& s, int n, const float* norm_w, float ss) {
     const int G = n / 32;
@@ -238,7 +264,7 @@ __device__ __forceinline__ void decode_epilogue(const DecodeArgs& a, const OpDes
         for (int r = 0; r < 2; r++)
             if (h0 + r < a.hidden) {
                 const float g = v[r];
-                const float s = __fdiv_rn(g, 1.0f + expf(-g));
+                const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g)));
                 __stcg(a.hb + h0 + r, __fmul_rn(s, v[2 + r]));
             }
         break;
@@ -311,7 +337,7 @@ __device__ void attention_layer(const DecodeArgs& a, int layer, int pos, AttnSme
         m = block_max(m, sm.red);
         float e = 0.0f;
         if (tid < n) {
-            e = expf(sm.s[tid] - m);
+            e = expf_cr(sm.s[tid] - m);
             sm.s[tid] = e;
         }
         const float l = block_sum(e, sm.red);   // contains a __syncthreads before its smem use
@@ -357,6 +383,54 @@ __device__ void attention_layer(const DecodeArgs& a, int layer, int pos, AttnSme
                 __stcg(a.att + h * hs + i, o * inv);
             }
             if (tid == 0) a.attn_cnt[h] = 0;
+        }
+        __syncthreads();
+    }
+}
+
+// Attention of one layer in the reference's own order (src/kernel_simd.c:
+// 1099-1117, softmax :816-826), one CTA per head: score_t = (sum_j q_j k_j
+// sequentially) / sqrtf(head_size); max; e_t = e^(score_t - max); sum of e_t
+// sequentially; a_t = e_t * (1 / sum); out_j = sum_t a_t v_t[j] sequentially.
+// `sc` holds max_pos floats of shared memory.
+__device__ void attention_layer_exact(const DecodeArgs& a, int layer, int pos, float* sc, float* red) {
+    const int hs = a.head_size, tid = threadIdx.x;
+    const size_t lkv = (size_t)layer * a.max_pos * a.kv_dim;
+    const float* kc = a.kcache + lkv;
+    const float* vc = a.vcache + lkv;
+    const float rs = sqrtf((float)hs);
+    __shared__ float s_q[kMaxHead];
+    __shared__ float s_sum;
+    for (int h = blockIdx.x; h < a.n_heads; h += gridDim.x) {
+        const int kvh = h / a.kv_mul;
+        for (int i = tid; i < hs; i += blockDim.x) s_q[i] = __ldcg(a.q + h * hs + i);
+        __syncthreads();
+        float m = -INFINITY;
+        for (int t = tid; t <= pos; t += blockDim.x) {
+            const float* kr = kc + (size_t)t * a.kv_dim + kvh * hs;
+            float d = 0.0f;
+            for (int j = 0; j < hs; j++) d = __fadd_rn(d, __fmul_rn(s_q[j], __ldcg(kr + j)));
+            d = __fdiv_rn(d, rs);
+            sc[t] = d;
+            m = fmaxf(m, d);
+        }
+        m = block_max(m, red);
+        for (int t = tid; t <= pos; t += blockDim.x) sc[t] = expf_cr(__fsub_rn(sc[t], m));
+        __syncthreads();
+        if (tid == 0) {
+            float sum = 0.0f;
+            for (int t = 0; t <= pos; t++) sum = __fadd_rn(sum, sc[t]);
+            s_sum = sum;
+        }
+        __syncthreads();
+        const float scale = __fdiv_rn(1.0f, s_sum);
+        for (int t = tid; t <= pos; t += blockDim.x) sc[t] = __fmul_rn(sc[t], scale);
+        __syncthreads();
+        for (int j = tid; j < hs; j += blockDim.x) {
+            float o = 0.0f;
+            for (int t = 0; t <= pos; t++)
+                o = __fadd_rn(o, __fmul_rn(sc[t], __ldcg(vc + (size_t)t * a.kv_dim + kvh * hs + j)));
+            __stcg(a.att + h * hs + j, o);
         }
         __syncthreads();
     }
@@ -440,7 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
             } else {
                 src.p = op.kind == OP_WO ? a.att : a.hb;
             }
-            const float ss = nw ? src_rms_scale(src, op.m.n, red) : 1.0f;
+            const float ss = !nw ? 1.0f
+                             : (MODE == MODE_W4A8 ? src_rms_scale_exact(src, op.m.n, red) : src_rms_scale(src, op.m.n, red));
             src_build_x<MODE>(xbuf, src, op.m.n, nw, ss);
             __syncthreads();
             // ---- this warp's tiles of the op
@@ -484,7 +559,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
                     *a.argmax = argmax_key(-1e9f, 0);
                     __threadfence();
                 }
-                attention_layer(a, op.layer, tc.pos, attn);
+                if (MODE == MODE_W4A8)
+                    attention_layer_exact(a, op.layer, tc.pos, reinterpret_cast<float*>(xbuf), red);
+                else
+                    attention_layer(a, op.layer, tc.pos, attn);
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             }
         }

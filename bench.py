@@ -185,14 +185,14 @@ def run_reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def isolated_matvecs(device: int, reps: int) -> dict:
+def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
     """GB/s of the W4A16 matvec kernel on the isolated 7B shapes, rotating over
     enough distinct weight copies to exceed 2x L2 so every launch reads HBM."""
     import torch
     import aion_b200 as A
     rng = np.random.default_rng(5)
     out = {}
-    for d, n in MATVEC_SHAPES:
+    for d, n in shapes or MATVEC_SHAPES:
         copies = max(2, int(np.ceil(2 * 126e6 / (0.625 * d * n))) + 1)
         mats = []
         for _ in range(copies):
@@ -225,6 +225,7 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["aion", "reference"], default="aion")
     ap.add_argument("--matvec", action="store_true", help="isolated matvec shapes only")
+    ap.add_argument("--shape", default=None, help="with --matvec: one shape, e.g. 32000x4096")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the isolated matvec shapes")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
@@ -260,7 +261,8 @@ def main() -> None:
         return float(t.item())
 
     if args.matvec:
-        res = isolated_matvecs(local, reps=max(args.steps, 1))
+        shapes = [tuple(int(v) for v in args.shape.split("x"))] if args.shape else None
+        res = isolated_matvecs(local, reps=max(args.steps, 1), shapes=shapes)
         if rank == 0:
             print(json.dumps({"metric": "int4 matvec HBM GB/s (isolated 7B shapes)", "matvec": res}), flush=True)
         return
