@@ -80,16 +80,18 @@ static const DevInfo& dev_info(int dev) {
 
 static int round128(int b) { return (b + 127) & ~127; }
 
-// Dynamic shared memory plan of the streaming kernels: x' area, then the
-// per-warp rings of P slots.
+// Dynamic shared memory plan of the streaming kernels: activation digits
+// (G * 96 bytes) and group factors (G * 4), then the per-warp rings of P
+// slots.
 struct SmemPlan {
-    int xbytes = 0, slot_bytes = 0, P = 0, total = 0;
+    int xbytes = 0, xs_off = 0, slot_bytes = 0, P = 0, total = 0;
 };
 
-static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int mode, int smem_optin, int static_bytes,
-                          int min_xbytes = 0) {
+static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int smem_optin, int static_bytes, int min_xbytes = 0) {
     SmemPlan p;
-    p.xbytes = round128(std::max(xbuf_bytes(max_n, mode), min_xbytes));
+    const int G = max_n / 32;
+    p.xs_off = G * kXF;
+    p.xbytes = round128(std::max(xbuf_bytes(max_n), min_xbytes));
     p.slot_bytes = round128(max_chunk_bytes);
     const int avail = smem_optin - static_bytes - 1024 - p.xbytes;
     p.P = std::min(8, avail / (kWarps * p.slot_bytes));
@@ -133,7 +135,7 @@ static cudaError_t retile(const MatDesc& m, const float* scales, const uint8_t* 
     a.interleave = interleave;
     a.slot = slot;
     a.inverse = inverse;
-    const long long total = rows * (m.n / 32);
+    const long long total = rows * m.G;
     int grid = (int)std::min<long long>((total + 255) / 256, 65535);
     if (grid < 1) grid = 1;
     k_retile<<<grid, 256, 0, st>>>(a);
@@ -141,7 +143,7 @@ static cudaError_t retile(const MatDesc& m, const float* scales, const uint8_t* 
 }
 
 static cudaError_t fill_pad(const MatDesc& m, cudaStream_t st) {
-    if ((long long)m.ntiles * kRB == m.d) return cudaSuccess;
+    if ((long long)m.ntiles * kTR == m.d) return cudaSuccess;
     k_fill_pad<<<8, 256, 0, st>>>(m);
     return cudaGetLastError();
 }
@@ -149,14 +151,21 @@ static cudaError_t fill_pad(const MatDesc& m, cudaStream_t st) {
 // ---------------------------------------------------------------------------
 // Standalone matvec (kernel-level API)
 // ---------------------------------------------------------------------------
+struct Scratch {
+    float* split_part = nullptr;   // [ntiles][2][16]
+    int* split_cnt = nullptr;      // [ntiles]
+    int* error = nullptr;
+};
+
 template <int MODE>
-static cudaError_t launch_standalone(const MatDesc& m, const float* x, float* y, int dev, cudaStream_t st) {
+static cudaError_t launch_standalone(const MatDesc& m, const Scratch& sc, const float* x, float* y, int dev,
+                                     cudaStream_t st) {
     static bool attr_done[2] = {false, false};
     const DevInfo& di = dev_info(dev);
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, k_matvec<MODE>);
     if (e != cudaSuccess) return e;
-    SmemPlan p = plan_smem(m.n, m.chunk_bytes, MODE, di.smem_optin, (int)fa.sharedSizeBytes);
+    SmemPlan p = plan_smem(m.n, max_chunk_bytes(m), di.smem_optin, (int)fa.sharedSizeBytes);
     if (p.P < 1) return cudaErrorInvalidConfiguration;
     if (!attr_done[MODE]) {
         e = cudaFuncSetAttribute(k_matvec<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -165,13 +174,19 @@ static cudaError_t launch_standalone(const MatDesc& m, const float* x, float* y,
         attr_done[MODE] = true;
     }
     StandaloneArgs a;
-    a.m = m;
+    a.op.m = m;
+    a.op.kind = OP_STORE;
+    a.op.layer = 0;
     a.x = x;
     a.y = y;
+    a.split_part = sc.split_part;
+    a.split_cnt = sc.split_cnt;
+    a.error = sc.error;
     a.P = p.P;
     a.slot_bytes = p.slot_bytes;
-    const int grid = std::min(di.sms, m.ntiles);
-    return launch_ex(k_matvec<MODE>, dim3(grid), dim3(kThreads), (size_t)p.total, st, true, false, a);
+    a.xbytes = p.xbytes;
+    a.xs_off = p.xs_off;
+    return launch_ex(k_matvec<MODE>, dim3(di.sms), dim3(kThreads), (size_t)p.total, st, true, false, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -195,6 +210,9 @@ struct aion_ctx {
     float* attn_part = nullptr;
     int* attn_cnt = nullptr;
     int max_chunks = 1;
+    float* split_part = nullptr;
+    int* split_cnt = nullptr;
+    int max_tiles = 0;
     StepState* step = nullptr;
     unsigned long long* argmax = nullptr;
     int32_t* history = nullptr;
@@ -303,6 +321,8 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.attn_part = c->attn_part;
     a.attn_cnt = c->attn_cnt;
     a.max_chunks = c->max_chunks;
+    a.split_part = c->split_part;
+    a.split_cnt = c->split_cnt;
     a.step = c->step;
     a.argmax = c->argmax;
     a.history = c->history;
@@ -310,6 +330,7 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.P = c->plan.P;
     a.slot_bytes = c->plan.slot_bytes;
     a.xbytes = c->plan.xbytes;
+    a.xs_off = c->plan.xs_off;
     // The grid-barrier counter starts from zero in every launch.
     cudaError_t e = cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream);
     if (e != cudaSuccess) return e;
@@ -449,9 +470,8 @@ static aion_status setup_decode_kernel(aion_ctx* c, int max_n, int max_chunk) {
     const DevInfo& di = dev_info(c->dev);
     cudaFuncAttributes fa;
     CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode<MODE>));
-    // W4A8 runs the reference-order attention, whose scores use the x' area.
-    c->plan = plan_smem(max_n, max_chunk, MODE, di.smem_optin, (int)fa.sharedSizeBytes,
-                        MODE == MODE_W4A8 ? c->max_pos * 4 : 0);
+    // W4A8 runs the reference-order attention, whose scores use the digit area.
+    c->plan = plan_smem(max_n, max_chunk, di.smem_optin, (int)fa.sharedSizeBytes, MODE == MODE_W4A8 ? c->max_pos * 4 : 0);
     if (c->plan.P < 2) {
         set_err(&c->err, "shared memory too small for the decode rings (P = %d)", c->plan.P);
         return AION_ERR_SHAPE;
@@ -505,6 +525,8 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         bytes += align256((size_t)c->nh * c->max_chunks * (c->hs + 2) * 4) + align256(c->nh * 4);
         bytes += align256(sizeof(StepState)) + align256(8) + align256((size_t)c->max_pos * 4);
         bytes += align256((size_t)(4 * L + 1) * sizeof(OpDesc));
+        c->max_tiles = std::max({c->emb.ntiles, dq.ntiles, dwo.ntiles, d13.ntiles, d2.ntiles});
+        bytes += align256((size_t)c->max_tiles * 2 * kTR * 4) + align256((size_t)c->max_tiles * 4);
         c->arena_bytes = bytes + 4096;
         CK_RET(&c->err, cudaMalloc(&c->arena, c->arena_bytes));
         CK_RET(&c->err, cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream));
@@ -535,7 +557,9 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         c->argmax = (unsigned long long*)arena_take(c, 8);
         c->history = (int32_t*)arena_take(c, (size_t)c->max_pos * 4);
         c->ops = (OpDesc*)arena_take(c, (size_t)(4 * L + 1) * sizeof(OpDesc));
-        if (!c->ops) {
+        c->split_part = (float*)arena_take(c, (size_t)c->max_tiles * 2 * kTR * 4);
+        c->split_cnt = (int*)arena_take(c, (size_t)c->max_tiles * 4);
+        if (!c->split_cnt) {
             set_err(&c->err, "internal: arena too small");
             s = AION_ERR_OOM;
             break;
@@ -620,7 +644,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             ops.push_back({c->w2[l], OP_W2, (int)l});
         }
         ops.push_back({c->emb, OP_CLS, 0});
-        for (const OpDesc& o : ops) max_chunk = std::max(max_chunk, o.m.chunk_bytes);
+        for (const OpDesc& o : ops) max_chunk = std::max(max_chunk, max_chunk_bytes(o.m));
         c->nops = (int)ops.size();
         CK_RET(&c->err, cudaMemcpyAsync(c->ops, ops.data(), ops.size() * sizeof(OpDesc), cudaMemcpyHostToDevice,
                                         c->stream));
@@ -769,6 +793,7 @@ extern "C" AION_API aion_status aion_reset(aion_ctx* c) {
     CK_RET(&c->err, cudaMemsetAsync(c->vcache, 0, kvb, c->stream));
     CK_RET(&c->err, cudaMemsetAsync(&c->step->error, 0, sizeof(int32_t), c->stream));
     CK_RET(&c->err, cudaMemsetAsync(c->attn_cnt, 0, c->nh * 4, c->stream));
+    CK_RET(&c->err, cudaMemsetAsync(c->split_cnt, 0, (size_t)c->max_tiles * 4, c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return AION_OK;
 }
@@ -779,6 +804,8 @@ extern "C" AION_API aion_status aion_reset(aion_ctx* c) {
 struct aion_qmatrix {
     int device;
     MatDesc m;
+    Scratch sc;
+    uint8_t* scratch_mem;
 };
 
 extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const uint8_t* packed, int64_t rows,
@@ -814,9 +841,24 @@ extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const u
         set_err(nullptr, "aion_qmatrix_upload: %s", cudaGetErrorString(e));
         return cuda_status(e);
     }
+    // Scratch of the split-tile combine: partial rows and counters (zero).
+    const size_t pbytes = align256((size_t)m.ntiles * 2 * kTR * 4), cbytes = align256((size_t)m.ntiles * 4);
+    uint8_t* scr = nullptr;
+    e = cudaMalloc(&scr, pbytes + cbytes + 256);
+    if (e == cudaSuccess) e = cudaMemset(scr, 0, pbytes + cbytes + 256);
+    if (e != cudaSuccess) {
+        cudaFree(w);
+        if (scr) cudaFree(scr);
+        set_err(nullptr, "aion_qmatrix_upload: %s", cudaGetErrorString(e));
+        return cuda_status(e);
+    }
     aion_qmatrix* q = new aion_qmatrix();
     q->device = device;
     q->m = m;
+    q->scratch_mem = scr;
+    q->sc.split_part = (float*)scr;
+    q->sc.split_cnt = (int*)(scr + pbytes);
+    q->sc.error = (int*)(scr + pbytes + cbytes);
     *out = q;
     return AION_OK;
 }
@@ -843,6 +885,7 @@ extern "C" AION_API aion_status aion_qmatrix_free(aion_qmatrix* q) {
     if (!q) return AION_OK;
     cudaSetDevice(q->device);
     cudaFree((void*)q->m.w);
+    cudaFree(q->scratch_mem);
     delete q;
     return AION_OK;
 }
@@ -857,8 +900,9 @@ static aion_status matvec_api(int mode, const aion_qmatrix* q, const float* x, f
         return AION_ERR_ARG;
     }
     CK_RET(nullptr, cudaSetDevice(q->device));
-    cudaError_t e = mode == MODE_W4A8 ? launch_standalone<MODE_W4A8>(q->m, x, y, q->device, (cudaStream_t)stream)
-                                      : launch_standalone<MODE_W4A16>(q->m, x, y, q->device, (cudaStream_t)stream);
+    cudaError_t e = mode == MODE_W4A8
+                        ? launch_standalone<MODE_W4A8>(q->m, q->sc, x, y, q->device, (cudaStream_t)stream)
+                        : launch_standalone<MODE_W4A16>(q->m, q->sc, x, y, q->device, (cudaStream_t)stream);
     CK_RET(nullptr, e);
     return AION_OK;
 }

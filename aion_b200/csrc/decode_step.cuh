@@ -1,30 +1,30 @@
-// Persistent decode kernel: `steps` greedy tokens of the int4 Llama-2
-// forward (src/kernel_simd.c:1014-1169 per token, :1223-1250 around it) in
-// one cooperative launch, one CTA per SM.
+// Streaming kernels: the persistent decode kernel and the standalone matvec.
 //
-// Every weight matrix of a token is an "op"; the ops of all steps form one
-// sequence.  CTA c owns tiles [c*T/G, (c+1)*T/G) of every op; warp w of the
-// CTA streams tiles t0 + w, t0 + w + 8, ... of each op, chunk by chunk,
-// through its own ring of bulk copies, always P chunks ahead -- across op
-// boundaries, grid barriers and tokens, since the weights never depend on
-// the activations.  Between dependent ops the CTAs meet at a bounded grid
-// barrier; the input vector of each op is rebuilt in shared memory ("x'")
-// with its fused prologue (RMSNorm, or the int4 embedding row).
+// Persistent decode: `steps` greedy tokens of the int4 Llama-2 forward
+// (src/kernel_simd.c:1014-1169 per token, :1223-1250 around it) in one
+// cooperative launch, one CTA per SM.  Every weight matrix of a token is an
+// "op"; the ops of all steps form one sequence.  Each warp streams its share
+// of every op (see op_work) through its own ring of bulk copies, always P
+// chunks ahead -- across op boundaries, grid barriers and tokens, since the
+// weights never depend on the activations.  Between dependent ops the CTAs
+// meet at a bounded grid barrier; the input of each op is rebuilt in shared
+// memory as activation digits (matvec.cuh) with its fused prologue (RMSNorm,
+// or the int4 embedding row).
 //
 // Per token (5 barriers per layer, 1 after the classifier):
-//   [QKV: rmsnorm x' | q, k, v rows | RoPE, KV append]  barrier
-//   [attention: (head, 64-position chunk) units, last CTA per head combines] barrier
-//   [wo: att x' | x += ]  barrier
-//   [w1/w3: rmsnorm x' | SwiGLU -> hb]  barrier
-//   [w2: hb x' | x += ]  barrier
-//   ... [classifier: rmsnorm x' | logits, argmax key]  barrier (next token)
+//   [QKV: rmsnorm | q, k, v rows | RoPE, KV append]  barrier
+//   [attention]  barrier
+//   [wo: att | x += ]  barrier
+//   [w1/w3: rmsnorm | SwiGLU -> hb]  barrier
+//   [w2: hb | x += ]  barrier
+//   ... [classifier: rmsnorm | logits, argmax key]  barrier (next token)
 #pragma once
 
 #include "matvec.cuh"
 
 namespace aion {
 
-enum OpKind { OP_QKV = 0, OP_WO = 1, OP_W13 = 2, OP_W2 = 3, OP_CLS = 4 };
+enum OpKind { OP_QKV = 0, OP_WO = 1, OP_W13 = 2, OP_W2 = 3, OP_CLS = 4, OP_STORE = 5 };
 
 struct OpDesc {
     MatDesc m;
@@ -45,35 +45,43 @@ struct DecodeArgs {
     float* attn_part;              // [n_heads][max_chunks][head_size + 2]
     int* attn_cnt;                 // [n_heads], zero between uses
     int max_chunks;
+    float* split_part;             // [max_tiles][2][16] partial rows of tiles cut by CTA boundaries
+    int* split_cnt;                // [max_tiles], zero between uses
     StepState* step;
     unsigned long long* argmax;
     int32_t* history;              // [max_pos]
     int steps;
-    int P, slot_bytes, xbytes;
+    int P, slot_bytes, xbytes, xs_off;
 };
 
 // ---------------------------------------------------------------------------
-// Input sources of an op's x': an fp32 vector in global memory (written by
-// other CTAs of this launch: read through L2), or the int4 embedding row of
-// a token (src/kernel_simd.c:1032-1040: x[i] = (int8)(nibble - 8) * scale).
+// Input sources of an op: an fp32 vector in global memory (written by other
+// CTAs of this launch: read through L2), or the int4 embedding row of a
+// token (src/kernel_simd.c:1032-1040: x[i] = (int8)(nibble - 8) * scale).
 // ---------------------------------------------------------------------------
 struct VecSrc {
     const float* p;                // fp32 vector, or nullptr for the embedding row
-    const uint8_t* emb_w;
     MatDesc emb;
     int tok;
 };
 
 __device__ __forceinline__ float4 src_load4(const VecSrc& s, int i) {
     if (s.p) return __ldcg(reinterpret_cast<const float4*>(s.p) + i);
-    const int e = 4 * i, g = e / 32;
-    const float sc = __ldg(reinterpret_cast<const float*>(s.emb_w + scale_offset(s.emb, s.tok, g)));
-    const uint16_t b = __ldg(reinterpret_cast<const uint16_t*>(s.emb_w + group_offset(s.emb, s.tok, g) + (e % 32) / 2));
+    // elements 4i..4i+3 of row tok: group g, elements k..k+3 of the group
+    const int g = i >> 3, k = (i & 7) * 4;
+    const long long R = s.tok;
+    const int rr = (int)(R % kTR), lr = rr & 7, half = rr >> 3;
+    const uint8_t* gp = s.emb.w + (R / kTR) * s.emb.tile_bytes + (size_t)g * kGB;
+    const float sc = __ldg(reinterpret_cast<const float*>(gp + 256 + 8 * lr + 4 * half));
+    // element e of the group: lane t = (e % 16) / 4, byte b = e % 4, high nibble if e >= 16
+    const int t = (k & 15) >> 2;
+    const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(gp + 8 * (4 * lr + t) + 4 * half));
+    const int shift = k >= 16 ? 4 : 0;
     float4 v;
-    v.x = (float)((int)(b & 0xF) - 8) * sc;
-    v.y = (float)((int)((b >> 4) & 0xF) - 8) * sc;
-    v.z = (float)((int)((b >> 8) & 0xF) - 8) * sc;
-    v.w = (float)((int)((b >> 12) & 0xF) - 8) * sc;
+    v.x = (float)((int)((w >> shift) & 0xF) - 8) * sc;
+    v.y = (float)((int)((w >> (8 + shift)) & 0xF) - 8) * sc;
+    v.z = (float)((int)((w >> (16 + shift)) & 0xF) - 8) * sc;
+    v.w = (float)((int)((w >> (24 + shift)) & 0xF) - 8) * sc;
     return v;
 }
 
@@ -113,88 +121,45 @@ __device__ __forceinline__ float src_rms_scale_exact(const VecSrc& s, int n, flo
 // from the correctly rounded value).
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
 
+// Activation digits of an op's input (optionally RMS-normalised as
+// (x * ss) * w, src/kernel_simd.c:805-813).  Thread per group.
 template <int MODE>
-__device__ __forceinline__ void src_build_x(unsigned char* xbuf, const VecSrc& s, int n, const float* norm_w, float ss) {
-    const int G = n / 32;
-    if (MODE == MODE_W4A16) {
-        float4* xs4 = reinterpret_cast<float4*>(xbuf);
-        for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
-            float4 v = src_load4(s, i);
+__device__ __forceinline__ void src_build_digits(unsigned char* xf, float* xs, const VecSrc& s, int n,
+                                                 const float* norm_w, float ss) {
+    for (int g = threadIdx.x; g < n / 32; g += blockDim.x) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float4 t = src_load4(s, g * 8 + j);
             if (norm_w) {
-                const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + i);
-                v.x = __fmul_rn(__fmul_rn(v.x, ss), w.x);
-                v.y = __fmul_rn(__fmul_rn(v.y, ss), w.y);
-                v.z = __fmul_rn(__fmul_rn(v.z, ss), w.z);
-                v.w = __fmul_rn(__fmul_rn(v.w, ss), w.w);
+                const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + g * 8 + j);
+                t.x = __fmul_rn(__fmul_rn(t.x, ss), w.x);
+                t.y = __fmul_rn(__fmul_rn(t.y, ss), w.y);
+                t.z = __fmul_rn(__fmul_rn(t.z, ss), w.z);
+                t.w = __fmul_rn(__fmul_rn(t.w, ss), w.w);
             }
-            const int e0 = (i & 1) * 4;
-            v.x *= prescale(e0);
-            v.y *= prescale(e0 + 1);
-            v.z *= prescale(e0 + 2);
-            v.w *= prescale(e0 + 3);
-            xs4[xperm(i >> 3, i & 7)] = v;
+            v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
         }
-    } else {
-        const int chunks = (G + 31) / 32;
-        uint4* qx = reinterpret_cast<uint4*>(xbuf);
-        float* xsc = reinterpret_cast<float*>(xbuf + chunks * 2 * 32 * 16);
-        for (int g = threadIdx.x; g < G; g += blockDim.x) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                float4 t = src_load4(s, g * 8 + j);
-                if (norm_w) {
-                    const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + g * 8 + j);
-                    t.x = __fmul_rn(__fmul_rn(t.x, ss), w.x);
-                    t.y = __fmul_rn(__fmul_rn(t.y, ss), w.y);
-                    t.z = __fmul_rn(__fmul_rn(t.z, ss), w.z);
-                    t.w = __fmul_rn(__fmul_rn(t.w, ss), w.w);
-                }
-                v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
-            }
-            float amax = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
-            const bool big = amax > 1e-9f;
-            const float scale = big ? __fdiv_rn(127.0f, amax) : 1.0f;
-            xsc[g] = big ? __fdiv_rn(amax, 127.0f) : 1.0f;
-            uint32_t words[8];
-#pragma unroll
-            for (int wd = 0; wd < 4; wd++) {
-                uint32_t ev = 0, od = 0;
-#pragma unroll
-                for (int b = 0; b < 4; b++) {
-                    const int qe = (int)roundf(__fmul_rn(v[8 * wd + 2 * b], scale));
-                    const int qo = (int)roundf(__fmul_rn(v[8 * wd + 2 * b + 1], scale));
-                    ev |= (uint32_t)(qe & 0xFF) << (8 * b);
-                    od |= (uint32_t)(qo & 0xFF) << (8 * b);
-                }
-                words[2 * wd] = ev;
-                words[2 * wd + 1] = od;
-            }
-            qx[((g >> 5) * 2 + 0) * 32 + (g & 31)] = make_uint4(words[0], words[1], words[2], words[3]);
-            qx[((g >> 5) * 2 + 1) * 32 + (g & 31)] = make_uint4(words[4], words[5], words[6], words[7]);
-        }
+        group_digits<MODE>(xf, xs, g, v);
     }
 }
 
 // ---------------------------------------------------------------------------
-// Producer position of a warp in the op sequence (all lanes keep it).
+// Producer position of a warp in the sequence of (step, op) chunk streams.
 // ---------------------------------------------------------------------------
 struct Seq {
-    int step, op, t, c, t1;        // op == nops: end of the sequence
+    int step, op;                  // op == nops: end of the sequence
+    OpWork w;
+    OpCursor cu;
 };
 
-__device__ __forceinline__ void seq_enter(Seq& s, const DecodeArgs& a, int step, int op) {
-    const int warp = threadIdx.x >> 5;
-    while (step < a.steps) {
-        while (op < a.nops) {
-            const int T = a.ops[op].m.ntiles;
-            int t0, t1;
-            t0 = (int)(((long long)blockIdx.x * T) / gridDim.x);
-            t1 = (int)(((long long)(blockIdx.x + 1) * T) / gridDim.x);
-            if (t0 + warp < t1) {
-                s.step = step; s.op = op; s.t = t0 + warp; s.c = 0; s.t1 = t1;
+__device__ __forceinline__ void seq_enter(Seq& s, const OpDesc* ops, int nops, int steps, int mode, int step, int op) {
+    while (step < steps) {
+        while (op < nops) {
+            s.w = op_work(ops[op].m, mode);
+            if (cursor_begin(s.cu, s.w)) {
+                s.step = step;
+                s.op = op;
                 return;
             }
             op++;
@@ -202,82 +167,219 @@ __device__ __forceinline__ void seq_enter(Seq& s, const DecodeArgs& a, int step,
         op = 0;
         step++;
     }
-    s.step = a.steps; s.op = a.nops;
+    s.step = steps;
+    s.op = nops;
 }
 
-__device__ __forceinline__ void seq_issue_next(Seq& s, Ring& r, const DecodeArgs& a) {
-    if (s.step >= a.steps) return;
-    const MatDesc& m = a.ops[s.op].m;
-    ring_issue(r, m.w + (size_t)s.t * m.tile_bytes + (size_t)s.c * m.chunk_bytes, m.chunk_bytes);
-    if (++s.c == m.nch) {
-        s.c = 0;
-        s.t += kWarps;
-        if (s.t >= s.t1) seq_enter(s, a, s.step, s.op + 1);
-    }
+__device__ __forceinline__ void seq_issue_next(Seq& s, Ring& r, const OpDesc* ops, int nops, int steps, int mode) {
+    if (s.step >= steps) return;
+    const MatDesc& m = ops[s.op].m;
+    int tile, c, bytes;
+    cursor_tc(s.cu, s.w, m, tile, c);
+    const uint8_t* src = chunk_src(m, tile, c, bytes);
+    ring_issue(r, src, bytes);
+    if (!cursor_next(s.cu, s.w, m)) seq_enter(s, ops, nops, steps, mode, s.step, s.op + 1);
 }
 
 // ---------------------------------------------------------------------------
-// Epilogue of one finished tile (runs on lane 0).
+// One op on this CTA: consume its chunks from the rings, reduce, combine the
+// tiles cut by CTA boundaries, and hand every finished quad of rows to
+// `epi(first_row, values[4])`.  Returns false if a wait gave up.
 // ---------------------------------------------------------------------------
-struct TokenCtx {
-    int pos, tok;
-    float best;
-    uint32_t best_i;
+struct OpSmem {
+    float part[kMaxLocalTiles * kWarps * kTR];   // split: warp partials per local tile
+    float vals[kMaxLocalTiles * kTR];            // split: finished rows per local tile
+    int state[2];
 };
 
-__device__ __forceinline__ void decode_epilogue(const DecodeArgs& a, const OpDesc& op, int r0, const float* v,
-                                                TokenCtx& tc) {
-    const int d = op.m.d;
-    switch (op.kind) {
-    case OP_QKV: {
-        const int hs = a.head_size, pos = tc.pos;
-        const size_t lkv = (size_t)op.layer * a.max_pos * a.kv_dim;
-        if (r0 < a.dim + a.kv_dim) {
-            // RoPE on adjacent pairs (src/kernel_simd.c:1068-1085)
-            const bool is_q = r0 < a.dim;
-            const int base = is_q ? r0 : r0 - a.dim;
-            float out[kRB];
-            for (int r = 0; r < kRB; r += 2) {
-                const int hd = (base + r) % hs;
-                const float fr = __ldg(a.freq_re + pos * (hs / 2) + hd / 2);
-                const float fi = __ldg(a.freq_im + pos * (hs / 2) + hd / 2);
-                out[r] = __fsub_rn(__fmul_rn(v[r], fr), __fmul_rn(v[r + 1], fi));
-                out[r + 1] = __fadd_rn(__fmul_rn(v[r], fi), __fmul_rn(v[r + 1], fr));
+template <int MODE, class Epi>
+__device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, Seq& seq, const OpDesc* ops, int nops,
+                       int steps, const unsigned char* xf, const float* xs, OpSmem& os, float* split_part,
+                       int* split_cnt, Epi& epi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const float lf = MODE == MODE_W4A16 ? w4a16_lane_factor() : 0.0f;
+    const OpWork w = op_work(m, MODE);
+    bool ok = true;
+    OpCursor cu;
+    bool more = cursor_begin(cu, w);
+    if (w.split) {
+        const int tf = w.u0 / m.nch, tl = (w.u1 - 1) / m.nch, ntl = tl - tf + 1;
+        for (int i = tid; i < ntl * kWarps * kTR; i += blockDim.x) os.part[i] = 0.0f;
+        __syncthreads();
+        float a0 = 0.0f, a1 = 0.0f;
+        int cur = -1;
+        while (more) {
+            int tile, c;
+            cursor_tc(cu, w, m, tile, c);
+            if (tile != cur) {
+                if (cur >= 0) {
+                    quad_reduce<MODE>(a0, a1);
+                    if ((lane & 3) == 0) {
+                        float* p = os.part + ((cur - tf) * kWarps + warp) * kTR;
+                        p[lane >> 2] = a0;
+                        p[(lane >> 2) + 8] = a1;
+                    }
+                }
+                a0 = a1 = 0.0f;
+                cur = tile;
             }
-            float* dst = is_q ? a.q + base : a.kcache + lkv + (size_t)pos * a.kv_dim + base;
-            __stcg(reinterpret_cast<float4*>(dst), make_float4(out[0], out[1], out[2], out[3]));
-        } else {
-            const int base = r0 - a.dim - a.kv_dim;
-            __stcg(reinterpret_cast<float4*>(a.vcache + lkv + (size_t)pos * a.kv_dim + base),
-                   make_float4(v[0], v[1], v[2], v[3]));
+            const unsigned char* ch = ring_wait(ring, ring_base);
+            if (!ch) { ok = false; break; }
+            const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
+            chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, lf, a0, a1);
+            __syncwarp();
+            ring.consumed++;
+            seq_issue_next(seq, ring, ops, nops, steps, MODE);
+            more = cursor_next(cu, w, m);
         }
-        break;
-    }
-    case OP_WO:
-    case OP_W2:
-        for (int r = 0; r < kRB; r++)
-            if (r0 + r < d) __stcg(a.x + r0 + r, __ldcg(a.x + r0 + r) + v[r]);
-        break;
-    case OP_W13: {
-        // tile rows w1[2t], w1[2t+1], w3[2t], w3[2t+1]; swiglu (src/kernel_simd.c:836-841)
-        const int h0 = r0 / 2;
-        for (int r = 0; r < 2; r++)
-            if (h0 + r < a.hidden) {
-                const float g = v[r];
-                const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g)));
-                __stcg(a.hb + h0 + r, __fmul_rn(s, v[2 + r]));
+        if (ok && cur >= 0) {
+            quad_reduce<MODE>(a0, a1);
+            if ((lane & 3) == 0) {
+                float* p = os.part + ((cur - tf) * kWarps + warp) * kTR;
+                p[lane >> 2] = a0;
+                p[(lane >> 2) + 8] = a1;
             }
-        break;
-    }
-    default:  // OP_CLS
-        for (int r = 0; r < kRB; r++)
-            if (r0 + r < d) {
-                __stcg(a.logits + r0 + r, v[r]);
-                if (v[r] > tc.best) { tc.best = v[r]; tc.best_i = (uint32_t)(r0 + r); }
+        }
+        if (__syncthreads_or(!ok)) return false;
+        for (int i = tid; i < ntl * kTR; i += blockDim.x) {
+            const int lt = i / kTR, r = i % kTR;
+            float v = 0.0f;
+            for (int k = 0; k < kWarps; k++) v += os.part[(lt * kWarps + k) * kTR + r];
+            os.vals[i] = v;
+        }
+        __syncthreads();
+        // Tiles cut by a CTA boundary: local tile 0 when u0 is inside a tile
+        // (this CTA has the tile's second part), the last local tile when u1
+        // is (this CTA has the first part).  The CTA arriving second adds
+        // first + second and finishes the tile.
+        int finish[2] = {1, 1};
+        for (int k = 0; k < 2; k++) {
+            const bool cut = k == 0 ? (w.u0 % m.nch) != 0 : (w.u1 % m.nch) != 0;
+            if (!cut) continue;
+            const int lt = k == 0 ? 0 : ntl - 1, partno = k == 0 ? 1 : 0, tile = tf + lt;
+            if (tid < kTR) __stcg(split_part + ((size_t)tile * 2 + partno) * kTR + tid, os.vals[lt * kTR + tid]);
+            __threadfence();
+            __syncthreads();
+            if (tid == 0) os.state[k] = atomicAdd(split_cnt + tile, 1);
+            __syncthreads();
+            if (os.state[k] == 1) {
+                __threadfence();
+                if (tid < kTR) {
+                    const float mine = os.vals[lt * kTR + tid];
+                    const float other = __ldcg(split_part + ((size_t)tile * 2 + (1 - partno)) * kTR + tid);
+                    os.vals[lt * kTR + tid] = partno == 0 ? mine + other : other + mine;
+                }
+                if (tid == 0) split_cnt[tile] = 0;
+            } else {
+                finish[k] = 0;
             }
-        break;
+            __syncthreads();
+        }
+        for (int i = tid; i < ntl * (kTR / kRB); i += blockDim.x) {
+            const int lt = i / (kTR / kRB), q = i % (kTR / kRB);
+            if (lt == 0 && (w.u0 % m.nch) != 0 && !finish[0]) continue;
+            if (lt == ntl - 1 && (w.u1 % m.nch) != 0 && !finish[1]) continue;
+            epi((tf + lt) * kTR + q * kRB, os.vals + lt * kTR + q * kRB);
+        }
+    } else {
+        float a0 = 0.0f, a1 = 0.0f;
+        float* stage = os.part + warp * kTR;
+        while (more) {
+            int tile, c;
+            cursor_tc(cu, w, m, tile, c);
+            const unsigned char* ch = ring_wait(ring, ring_base);
+            if (!ch) { ok = false; break; }
+            const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
+            chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, lf, a0, a1);
+            __syncwarp();
+            ring.consumed++;
+            seq_issue_next(seq, ring, ops, nops, steps, MODE);
+            if (c == m.nch - 1) {
+                quad_reduce<MODE>(a0, a1);
+                if ((lane & 3) == 0) {
+                    stage[lane >> 2] = a0;
+                    stage[(lane >> 2) + 8] = a1;
+                }
+                __syncwarp();
+                if (lane < kTR / kRB) epi(tile * kTR + lane * kRB, stage + lane * kRB);
+                __syncwarp();
+                a0 = a1 = 0.0f;
+            }
+            more = cursor_next(cu, w, m);
+        }
+        if (__syncthreads_or(!ok)) return false;
     }
+    return true;
 }
+
+// ---------------------------------------------------------------------------
+// Epilogue of the decode ops, per quad of rows.
+// ---------------------------------------------------------------------------
+struct DecodeEpi {
+    const DecodeArgs* a;
+    const OpDesc* op;
+    int pos;
+    float best;
+    uint32_t best_i;
+
+    __device__ __forceinline__ void operator()(int r0, const float* v) {
+        const DecodeArgs& A = *a;
+        const int d = op->m.d;
+        switch (op->kind) {
+        case OP_QKV: {
+            if (r0 >= d) break;
+            const int hs = A.head_size;
+            const size_t lkv = (size_t)op->layer * A.max_pos * A.kv_dim;
+            if (r0 < A.dim + A.kv_dim) {
+                // RoPE on adjacent pairs (src/kernel_simd.c:1068-1085)
+                const bool is_q = r0 < A.dim;
+                const int base = is_q ? r0 : r0 - A.dim;
+                float out[kRB];
+                for (int r = 0; r < kRB; r += 2) {
+                    const int hd = (base + r) % hs;
+                    const float fr = __ldg(A.freq_re + pos * (hs / 2) + hd / 2);
+                    const float fi = __ldg(A.freq_im + pos * (hs / 2) + hd / 2);
+                    out[r] = __fsub_rn(__fmul_rn(v[r], fr), __fmul_rn(v[r + 1], fi));
+                    out[r + 1] = __fadd_rn(__fmul_rn(v[r], fi), __fmul_rn(v[r + 1], fr));
+                }
+                float* dst = is_q ? A.q + base : A.kcache + lkv + (size_t)pos * A.kv_dim + base;
+                __stcg(reinterpret_cast<float4*>(dst), make_float4(out[0], out[1], out[2], out[3]));
+            } else {
+                const int base = r0 - A.dim - A.kv_dim;
+                __stcg(reinterpret_cast<float4*>(A.vcache + lkv + (size_t)pos * A.kv_dim + base),
+                       make_float4(v[0], v[1], v[2], v[3]));
+            }
+            break;
+        }
+        case OP_WO:
+        case OP_W2:
+            for (int r = 0; r < kRB; r++)
+                if (r0 + r < d) __stcg(A.x + r0 + r, __ldcg(A.x + r0 + r) + v[r]);
+            break;
+        case OP_W13: {
+            // rows w1[2j], w1[2j+1], w3[2j], w3[2j+1]; swiglu (src/kernel_simd.c:836-841)
+            const int h0 = r0 / 2;
+            for (int r = 0; r < 2; r++)
+                if (h0 + r < A.hidden) {
+                    const float g = v[r];
+                    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g)));
+                    __stcg(A.hb + h0 + r, __fmul_rn(s, v[2 + r]));
+                }
+            break;
+        }
+        default:  // OP_CLS
+            for (int r = 0; r < kRB; r++)
+                if (r0 + r < d) {
+                    __stcg(A.logits + r0 + r, v[r]);
+                    if (v[r] > best) {
+                        best = v[r];
+                        best_i = (uint32_t)(r0 + r);
+                    }
+                }
+            break;
+        }
+    }
+};
 
 // ---------------------------------------------------------------------------
 // Attention of one layer (CTA-wide).  Unit (head h, chunk k) covers
@@ -340,7 +442,7 @@ __device__ void attention_layer(const DecodeArgs& a, int layer, int pos, AttnSme
             e = expf_cr(sm.s[tid] - m);
             sm.s[tid] = e;
         }
-        const float l = block_sum(e, sm.red);   // contains a __syncthreads before its smem use
+        const float l = block_sum(e, sm.red);
         __syncthreads();
         // V: thread (group gi, dim i) sums positions gi, gi + groups, ...;
         // the group sums are added in group order.
@@ -374,12 +476,13 @@ __device__ void attention_layer(const DecodeArgs& a, int layer, int pos, AttnSme
             float M = -INFINITY;
             for (int c = 0; c < nch; c++) M = fmaxf(M, __ldcg(ph + (size_t)c * (hs + 2)));
             float L = 0.0f;
-            for (int c = 0; c < nch; c++) L = fmaf(__ldcg(ph + (size_t)c * (hs + 2) + 1), expf(__ldcg(ph + (size_t)c * (hs + 2)) - M), L);
+            for (int c = 0; c < nch; c++)
+                L = fmaf(__ldcg(ph + (size_t)c * (hs + 2) + 1), expf_cr(__ldcg(ph + (size_t)c * (hs + 2)) - M), L);
             const float inv = 1.0f / L;
             for (int i = tid; i < hs; i += blockDim.x) {
                 float o = 0.0f;
                 for (int c = 0; c < nch; c++)
-                    o = fmaf(__ldcg(ph + (size_t)c * (hs + 2) + 2 + i), expf(__ldcg(ph + (size_t)c * (hs + 2)) - M), o);
+                    o = fmaf(__ldcg(ph + (size_t)c * (hs + 2) + 2 + i), expf_cr(__ldcg(ph + (size_t)c * (hs + 2)) - M), o);
                 __stcg(a.att + h * hs + i, o * inv);
             }
             if (tid == 0) a.attn_cnt[h] = 0;
@@ -444,25 +547,46 @@ __global__ void k_set_step(StepState* s, int pos, int token) {
     }
 }
 
+// Largest key of the CTA's threads -> one atomicMax.
+__device__ __forceinline__ void cta_argmax(unsigned long long* dst, float best, uint32_t best_i, unsigned long long* red64) {
+    unsigned long long k = best > -1e9f ? argmax_key(best, best_i) : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
+        k = other > k ? other : k;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red64[warp] = k;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = 0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) m = red64[i] > m ? red64[i] : m;
+        if (m) atomicMax(dst, m);
+    }
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
-// The kernel.
+// The persistent decode kernel.
 // ---------------------------------------------------------------------------
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kWarps * 8];
     __shared__ float red[32];
+    __shared__ unsigned long long red64[kWarps];
     __shared__ AttnSmem attn;
+    __shared__ OpSmem os;
     __shared__ int s_tok, s_pos, s_bad;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    unsigned char* xbuf = smem;
+    unsigned char* xf = smem;
+    float* xs = reinterpret_cast<float*>(smem + a.xs_off);
     unsigned char* ring_base = smem + a.xbytes;
 
     Ring ring;
     ring_init(ring, ring_base, bars, a.P, a.slot_bytes);
     Seq seq;
-    seq_enter(seq, a, 0, 0);
-    for (int i = 0; i < a.P; i++) seq_issue_next(seq, ring, a);
+    seq_enter(seq, a.ops, a.nops, a.steps, MODE, 0, 0);
+    for (int i = 0; i < a.P; i++) seq_issue_next(seq, ring, a.ops, a.nops, a.steps, MODE);
 
     uint32_t nbar = 0;
     bool ok = true;
@@ -482,25 +606,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
             if (blockIdx.x == 0 && threadIdx.x == 0) set_error(a.step, DEV_BAD_INPUT);
             break;
         }
-        TokenCtx tc;
-        tc.pos = s_pos;
-        tc.tok = s_tok;
-        tc.best = -1e9f;
-        tc.best_i = 0;
+        const int pos = s_pos, tok = s_tok;
         VecSrc emb_src;
         emb_src.p = nullptr;
-        emb_src.emb_w = a.emb.w;
         emb_src.emb = a.emb;
-        emb_src.tok = tc.tok;
+        emb_src.tok = tok;
         if (blockIdx.x == 0)   // x = embedding row, for the residual stream
             for (int i = threadIdx.x; i < a.dim / 4; i += blockDim.x)
                 __stcg(reinterpret_cast<float4*>(a.x) + i, src_load4(emb_src, i));
 
         for (int oi = 0; oi < a.nops && ok; oi++) {
             const OpDesc op = a.ops[oi];
-            // ---- input x' of this op
             VecSrc src;
-            src.p = nullptr; src.emb_w = a.emb.w; src.emb = a.emb; src.tok = tc.tok;
+            src.emb = a.emb;
+            src.tok = tok;
+            src.p = nullptr;
             const float* nw = nullptr;
             if (op.kind == OP_QKV) {
                 nw = a.rms_att + (size_t)op.layer * a.dim;
@@ -516,57 +636,91 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
             }
             const float ss = !nw ? 1.0f
                              : (MODE == MODE_W4A8 ? src_rms_scale_exact(src, op.m.n, red) : src_rms_scale(src, op.m.n, red));
-            src_build_x<MODE>(xbuf, src, op.m.n, nw, ss);
+            src_build_digits<MODE>(xf, xs, src, op.m.n, nw, ss);
             __syncthreads();
-            // ---- this warp's tiles of the op
-            int t0, t1;
-            t0 = (int)(((long long)blockIdx.x * op.m.ntiles) / gridDim.x);
-            t1 = (int)(((long long)(blockIdx.x + 1) * op.m.ntiles) / gridDim.x);
-            for (int t = t0 + warp; t < t1 && ok; t += kWarps) {
-                float acc[kRB] = {0.0f, 0.0f, 0.0f, 0.0f};
-                for (int c = 0; c < op.m.nch; c++) {
-                    const unsigned char* ch = ring_wait(ring, ring_base);
-                    if (!ch) {
-                        set_error(a.step, DEV_COPY_TIMEOUT);
-                        ok = false;
-                        break;
-                    }
-                    chunk_compute<MODE>(ch, op.m.kc, c * (op.m.kc / 32), xbuf, op.m.n, acc);
-                    __syncwarp();
-                    ring.consumed++;
-                    seq_issue_next(seq, ring, a);
-                }
-                if (!ok) break;
-                finish_rows<MODE>(acc);
-                if (lane == 0) decode_epilogue(a, op, t * kRB, acc, tc);
+            DecodeEpi epi{&a, &op, pos, -1e9f, 0u};
+            if (!run_op<MODE>(op.m, ring, ring_base, seq, a.ops, a.nops, a.steps, xf, xs, os, a.split_part, a.split_cnt,
+                              epi)) {
+                set_error(a.step, DEV_COPY_TIMEOUT);
+                ok = false;
+                break;
             }
-            if (op.kind == OP_CLS && lane == 0 && tc.best > -1e9f)
-                atomicMax(a.argmax, argmax_key(tc.best, tc.best_i));
-            // An error in one warp must stop the whole CTA consistently.
-            if (__syncthreads_or(!ok)) ok = false;
-            if (!ok) break;
+            if (op.kind == OP_CLS) cta_argmax(a.argmax, epi.best, epi.best_i, red64);
             if (oi == a.nops - 1 && step == a.steps - 1) break;   // nothing after the last classifier
             if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             if (op.kind == OP_QKV) {
                 if (op.layer == 0 && blockIdx.x == 0 && threadIdx.x == 0) {
                     // Every CTA has read the step state and the argmax key.
                     StepState* st = a.step;
-                    st->pos = tc.pos;
-                    st->token = tc.tok;
-                    st->pos_next = tc.pos + 1;
+                    st->pos = pos;
+                    st->token = tok;
+                    st->pos_next = pos + 1;
                     st->forced_token = -1;
-                    a.history[tc.pos] = tc.tok;
+                    a.history[pos] = tok;
                     *a.argmax = argmax_key(-1e9f, 0);
                     __threadfence();
                 }
                 if (MODE == MODE_W4A8)
-                    attention_layer_exact(a, op.layer, tc.pos, reinterpret_cast<float*>(xbuf), red);
+                    attention_layer_exact(a, op.layer, pos, reinterpret_cast<float*>(xf), red);
                 else
-                    attention_layer(a, op.layer, tc.pos, attn);
+                    attention_layer(a, op.layer, pos, attn);
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             }
         }
     }
+    ring_drain(ring);
+}
+
+// ---------------------------------------------------------------------------
+// Standalone matvec y = W x (kernel-level entry points): the same streaming
+// and epilogue machinery as one op of the decode kernel.
+// ---------------------------------------------------------------------------
+struct StandaloneArgs {
+    OpDesc op;
+    const float* x;
+    float* y;
+    float* split_part;
+    int* split_cnt;
+    int P, slot_bytes, xbytes, xs_off;
+    int* error;
+};
+
+struct StoreEpi {
+    float* y;
+    int d;
+    __device__ __forceinline__ void operator()(int r0, const float* v) {
+        for (int r = 0; r < kRB; r++)
+            if (r0 + r < d) y[r0 + r] = v[r];
+    }
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1) k_matvec(StandaloneArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t bars[kWarps * 8];
+    __shared__ OpSmem os;
+    __shared__ OpDesc s_op;
+    unsigned char* xf = smem;
+    float* xs = reinterpret_cast<float*>(smem + a.xs_off);
+    unsigned char* ring_base = smem + a.xbytes;
+    if (threadIdx.x == 0) s_op = a.op;
+    __syncthreads();
+    Ring ring;
+    ring_init(ring, ring_base, bars, a.P, a.slot_bytes);
+    Seq seq;
+    seq_enter(seq, &s_op, 1, 1, MODE, 0, 0);
+    for (int i = 0; i < a.P; i++) seq_issue_next(seq, ring, &s_op, 1, 1, MODE);
+    pdl_launch_dependents();
+    pdl_wait();
+    VecSrc src;
+    src.p = a.x;
+    src.tok = 0;
+    src.emb = a.op.m;
+    src_build_digits<MODE>(xf, xs, src, a.op.m.n, nullptr, 1.0f);
+    __syncthreads();
+    StoreEpi epi{a.y, a.op.m.d};
+    if (!run_op<MODE>(s_op.m, ring, ring_base, seq, &s_op, 1, 1, xf, xs, os, a.split_part, a.split_cnt, epi))
+        if (threadIdx.x == 0) atomicCAS(a.error, 0, DEV_COPY_TIMEOUT);
     ring_drain(ring);
 }
 
