@@ -399,11 +399,12 @@ static aion_status validate_config(const aion_config& c, std::string* err) {
         return AION_ERR_SHAPE;
     }
     const long long hs = c.dim / c.n_heads, kv = (long long)c.dim * c.n_kv_heads / c.n_heads;
-    if (hs % 4 || hs > kMaxHead || c.dim % 32 || c.hidden_dim % 32 || kv % 32) {
+    if (hs % 16 || hs > kMaxHead || c.dim % 32 || c.hidden_dim % 32 || kv % 32 ||
+        c.dim > kMaxNormVec * 4 * kThreads || c.hidden_dim > kMaxVec * 4 * kThreads) {
         set_err(err,
-                "unsupported shape: head_size %lld, dim %d, hidden %d, kv_dim %lld (need head_size a multiple of 4, "
-                "<= %d; dim, hidden, kv_dim multiples of 32)",
-                hs, c.dim, c.hidden_dim, kv, kMaxHead);
+                "unsupported shape: head_size %lld, dim %d, hidden %d, kv_dim %lld (need head_size a multiple of 16, "
+                "<= %d; dim, hidden, kv_dim multiples of 32, dim <= %d, hidden <= %d)",
+                hs, c.dim, c.hidden_dim, kv, kMaxHead, kMaxNormVec * 4 * kThreads, kMaxVec * 4 * kThreads);
         return AION_ERR_SHAPE;
     }
     return AION_OK;
@@ -470,8 +471,9 @@ static aion_status setup_decode_kernel(aion_ctx* c, int max_n, int max_chunk) {
     const DevInfo& di = dev_info(c->dev);
     cudaFuncAttributes fa;
     CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode<MODE>));
-    // W4A8 runs the reference-order attention, whose scores use the digit area.
-    c->plan = plan_smem(max_n, max_chunk, di.smem_optin, (int)fa.sharedSizeBytes, MODE == MODE_W4A8 ? c->max_pos * 4 : 0);
+    // W4A8 stages the RMSNorm input (dim floats) and the reference-order
+    // attention scores (max_pos floats) in the digit area.
+    c->plan = plan_smem(max_n, max_chunk, di.smem_optin, (int)fa.sharedSizeBytes, MODE == MODE_W4A8 ? std::max(c->max_pos, (int)c->dim) * 4 : 0);
     if (c->plan.P < 2) {
         set_err(&c->err, "shared memory too small for the decode rings (P = %d)", c->plan.P);
         return AION_ERR_SHAPE;
@@ -508,7 +510,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             s = AION_ERR_ARG;
             break;
         }
-        c->max_chunks = (c->max_pos + kAttnLen - 1) / kAttnLen;
+        c->max_chunks = (c->max_pos + kAttnUnit - 1) / kAttnUnit;
         const long long dim = c->dim, hid = c->hidden, L = c->L, kv = c->kv_dim;
 
         // Matrix layouts (pointers filled below).
@@ -522,7 +524,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         bytes += align256(L * dim * 4) * 2 + align256(dim * 4) + 2 * align256(c->seq * (c->hs / 2) * 4);
         bytes += 2 * align256((size_t)L * c->max_pos * kv * 4);
         bytes += 3 * align256(dim * 4) + align256(hid * 4) + align256(c->vocab * 4);
-        bytes += align256((size_t)c->nh * c->max_chunks * (c->hs + 2) * 4) + align256(c->nh * 4);
+        bytes += align256((size_t)c->nh * c->max_chunks * (c->hs + 4) * 4) + align256(c->nh * 4);
         bytes += align256(sizeof(StepState)) + align256(8) + align256((size_t)c->max_pos * 4);
         bytes += align256((size_t)(4 * L + 1) * sizeof(OpDesc));
         c->max_tiles = std::max({c->emb.ntiles, dq.ntiles, dwo.ntiles, d13.ntiles, d2.ntiles});
@@ -551,7 +553,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         c->att = (float*)arena_take(c, dim * 4);
         c->hb = (float*)arena_take(c, hid * 4);
         c->logits = (float*)arena_take(c, c->vocab * 4);
-        c->attn_part = (float*)arena_take(c, (size_t)c->nh * c->max_chunks * (c->hs + 2) * 4);
+        c->attn_part = (float*)arena_take(c, (size_t)c->nh * c->max_chunks * (c->hs + 4) * 4);
         c->attn_cnt = (int*)arena_take(c, c->nh * 4);
         c->step = (StepState*)arena_take(c, sizeof(StepState));
         c->argmax = (unsigned long long*)arena_take(c, 8);

@@ -143,19 +143,20 @@ __device__ __forceinline__ bool grid_barrier(StepState* st, uint32_t& k, uint32_
     __shared__ int s_ok;
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
+        // bar.sync orders the CTA's writes before this release, and the
+        // release is cumulative, so no separate fence is needed; likewise
+        // the acquire below orders every later read of the CTA.
         red_release_add(&st->barrier, 1u);
         const uint32_t target = (k + 1) * gridDim.x;
         int ok = 1;
         uint32_t i = 0;
         while (ld_acquire_u32(&st->barrier) < target) {
-            if (++i > limit || ld_relaxed_i32(&st->error) != 0) {
+            if (++i > limit || ((i & 1023u) == 0 && ld_relaxed_i32(&st->error) != 0)) {
                 ok = 0;
                 break;
             }
         }
         if (!ok) set_error(st, DEV_BARRIER_TIMEOUT);
-        __threadfence();
         s_ok = ok;
     }
     __syncthreads();

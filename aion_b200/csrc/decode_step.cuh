@@ -31,8 +31,7 @@ struct OpDesc {
     int kind, layer;
 };
 
-constexpr int kAttnLen = 64;       // positions per attention unit
-constexpr int kMaxHead = 256;
+constexpr int kMaxHead = 128;
 
 struct DecodeArgs {
     const OpDesc* ops;             // [nops]: QKV, WO, W13, W2 per layer, then CLS
@@ -85,63 +84,137 @@ __device__ __forceinline__ float4 src_load4(const VecSrc& s, int i) {
     return v;
 }
 
-__device__ __forceinline__ float src_rms_scale(const VecSrc& s, int n, float* red) {
-    float acc = 0.0f;
-    for (int i = threadIdx.x; i < n / 4; i += blockDim.x) {
-        const float4 v = src_load4(s, i);
-        acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    }
-    acc = block_sum(acc, red);
-    return 1.0f / sqrtf(__fdiv_rn(acc, (float)n) + 1e-5f);
-}
-
-// The rmsnorm scale in the reference's own order (src/kernel_simd.c:793-803):
-// four lane sums of x[4m + l]^2 (product rounded, then added), reduced
-// pairwise, then mean, + 1e-5, 1 / sqrtf.  A sequential chain of n/4 adds
-// per lane: used where bit-exact parity with the reference is the contract.
-__device__ __forceinline__ float src_rms_scale_exact(const VecSrc& s, int n, float* red) {
-    if (threadIdx.x < 4) {
-        float acc = 0.0f;
-        for (int i = 0; i < n / 4; i++) {
-            const float4 v = src_load4(s, i);
-            const float e = threadIdx.x == 0 ? v.x : threadIdx.x == 1 ? v.y : threadIdx.x == 2 ? v.z : v.w;
-            acc = __fadd_rn(acc, __fmul_rn(e, e));
-        }
-        red[threadIdx.x] = acc;
-    }
-    __syncthreads();
-    const float sum = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
-    __syncthreads();
-    return 1.0f / sqrtf(__fdiv_rn(sum, (float)n) + 1e-5f);
-}
-
 // e^x rounded once to float: the double-precision exponential rounded to
 // the nearest float (CUDA exp() is accurate to < 1 double ulp, so only
 // inputs within ~1e-16 relative of a float rounding boundary can differ
 // from the correctly rounded value).
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
 
-// Activation digits of an op's input (optionally RMS-normalised as
-// (x * ss) * w, src/kernel_simd.c:805-813).  Thread per group.
-template <int MODE>
-__device__ __forceinline__ void src_build_digits(unsigned char* xf, float* xs, const VecSrc& s, int n,
-                                                 const float* norm_w, float ss) {
-    for (int g = threadIdx.x; g < n / 32; g += blockDim.x) {
-        float v[32];
+constexpr int kMaxVec = 14;       // float4 per thread of an op input: n <= 14 * 4 * kThreads
+constexpr int kMaxNormVec = 5;    // float4 per thread of a normed input: dim <= 5 * 4 * kThreads
+
+// Packs four signed values (the low bytes) into one word.
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) | ((uint32_t)(d & 0xFF) << 24);
+}
+
+// Builds the activation digits of an op's input in one pass: thread j of
+// the input holds float4 j (elements 4j..4j+3) in registers; the optional
+// RMSNorm (src/kernel_simd.c:793-813: 1 / sqrtf(sum(x^2)/n + 1e-5), then
+// (x * ss) * w) reduces over the CTA; the 8 threads of a 32-element group
+// find its maximum with shuffles and each writes its own fragment words.
+// W4A8 sums the squares in the reference's order (four lane sums of
+// x[4m + l]^2, pairwise) from a copy of x staged in the digit area.
+template <int MODE, int NV, bool NORM>
+__device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const VecSrc& s, int n,
+                                             const float* norm_w, float* red) {
+    const int tid = threadIdx.x;
+    const int nv = n / 4;
+    float4 v[NV], w[NORM ? NV : 1];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            float4 t = src_load4(s, g * 8 + j);
-            if (norm_w) {
-                const float4 w = __ldg(reinterpret_cast<const float4*>(norm_w) + g * 8 + j);
-                t.x = __fmul_rn(__fmul_rn(t.x, ss), w.x);
-                t.y = __fmul_rn(__fmul_rn(t.y, ss), w.y);
-                t.z = __fmul_rn(__fmul_rn(t.z, ss), w.z);
-                t.w = __fmul_rn(__fmul_rn(t.w, ss), w.w);
-            }
-            v[4 * j] = t.x; v[4 * j + 1] = t.y; v[4 * j + 2] = t.z; v[4 * j + 3] = t.w;
-        }
-        group_digits<MODE>(xf, xs, g, v);
+    for (int i = 0; i < NV; i++) {
+        const int j = tid + i * kThreads;
+        v[i] = j < nv ? src_load4(s, j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (NORM) w[i] = j < nv ? __ldg(reinterpret_cast<const float4*>(norm_w) + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
+    if (NORM) {
+        float ss;
+        if (MODE == MODE_W4A8) {
+            float4* stage = reinterpret_cast<float4*>(xf);
+#pragma unroll
+            for (int i = 0; i < NV; i++) {
+                const int j = tid + i * kThreads;
+                if (j < nv) stage[j] = v[i];
+            }
+            __syncthreads();
+            if (tid < 4) {
+                const float* sx = reinterpret_cast<const float*>(xf);
+                float acc = 0.0f;
+                for (int m = 0; m < nv; m++) {
+                    const float e = sx[4 * m + tid];
+                    acc = __fadd_rn(acc, __fmul_rn(e, e));
+                }
+                red[tid] = acc;
+            }
+            __syncthreads();
+            const float sum = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
+            ss = 1.0f / sqrtf(__fdiv_rn(sum, (float)n) + 1e-5f);
+            __syncthreads();
+        } else {
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV; i++) acc += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+            acc = block_sum(acc, red);
+            ss = 1.0f / sqrtf(__fdiv_rn(acc, (float)n) + 1e-5f);
+        }
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            v[i].x = __fmul_rn(__fmul_rn(v[i].x, ss), w[i].x);
+            v[i].y = __fmul_rn(__fmul_rn(v[i].y, ss), w[i].y);
+            v[i].z = __fmul_rn(__fmul_rn(v[i].z, ss), w[i].z);
+            v[i].w = __fmul_rn(__fmul_rn(v[i].w, ss), w[i].w);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+        if (i * kThreads >= nv) break;                      // uniform across the CTA
+        const int j = tid + i * kThreads;
+        const bool valid = j < nv;                          // same for the 8 threads of a group
+        const int g = j >> 3, q = j & 7;
+        float m = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        if (!valid) continue;
+        // element 4q + b sits in fragment lane t = q & 3, word (q >> 2)
+        unsigned char* dst = xf + (size_t)g * kXF + (q & 3) * 8 + (q >> 2) * 4;
+        const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        if (MODE == MODE_W4A16) {
+            const int ebits = (int)((__float_as_uint(m) >> 23) & 0xFF);
+            int d0[4], d1[4], d2[4];
+            float factor = 0.0f;
+            if (ebits > 127 - 60) {       // max |x| >= 2^-60; smaller groups count as zero
+                const int E = 22 - (ebits - 126);                // m * 2^E in [2^21, 2^22)
+                const float sa = __int_as_float((127 + E / 2) << 23), sb = __int_as_float((127 + E - E / 2) << 23);
+#pragma unroll
+                for (int b = 0; b < 4; b++) {
+                    const int X = __float2int_rn(__fmul_rn(__fmul_rn(e[b], sa), sb));
+                    d0[b] = ((X + 128) & 255) - 128;
+                    const int r = (X - d0[b]) >> 8;
+                    d1[b] = ((r + 128) & 255) - 128;
+                    d2[b] = (r - d1[b]) >> 8;
+                }
+                factor = __int_as_float((127 - E - 4) << 23);   // 2^-E / 16
+            } else {
+#pragma unroll
+                for (int b = 0; b < 4; b++) d0[b] = d1[b] = d2[b] = 0;
+            }
+            *reinterpret_cast<uint32_t*>(dst) = pack4(d0[0], d0[1], d0[2], d0[3]);
+            *reinterpret_cast<uint32_t*>(dst + 32) = pack4(d1[0], d1[1], d1[2], d1[3]);
+            *reinterpret_cast<uint32_t*>(dst + 64) = pack4(d2[0], d2[1], d2[2], d2[3]);
+            if (q == 0) xs[g] = factor;
+        } else {
+            // quantize_activations_neon (src/kernel_simd.c:186-227), bit-exact
+            const bool big = m > 1e-9f;
+            const float scale = big ? __fdiv_rn(127.0f, m) : 1.0f;
+            int qv[4];
+#pragma unroll
+            for (int b = 0; b < 4; b++) qv[b] = (int)roundf(__fmul_rn(e[b], scale));
+            *reinterpret_cast<uint32_t*>(dst) = pack4(qv[0], qv[1], qv[2], qv[3]);
+            *reinterpret_cast<uint32_t*>(dst + 32) = 0u;
+            *reinterpret_cast<uint32_t*>(dst + 64) = 0u;
+            if (q == 0) xs[g] = big ? __fdiv_rn(m, 127.0f) : 1.0f;
+        }
+    }
+}
+
+// Norm inputs (the model dimension) take at most kMaxNormVec float4 per
+// thread, with their RMSNorm weights loaded alongside; other inputs up to
+// kMaxVec.
+template <int MODE>
+__device__ void build_input(unsigned char* xf, float* xs, const VecSrc& s, int n, const float* norm_w, float* red) {
+    if (norm_w) build_digits<MODE, kMaxNormVec, true>(xf, xs, s, n, norm_w, red);
+    else build_digits<MODE, kMaxVec, false>(xf, xs, s, n, nullptr, red);
 }
 
 // ---------------------------------------------------------------------------
@@ -151,13 +224,15 @@ struct Seq {
     int step, op;                  // op == nops: end of the sequence
     OpWork w;
     OpCursor cu;
+    MatDesc m;                     // copy of ops[op].m, kept in registers
 };
 
 __device__ __forceinline__ void seq_enter(Seq& s, const OpDesc* ops, int nops, int steps, int mode, int step, int op) {
     while (step < steps) {
         while (op < nops) {
-            s.w = op_work(ops[op].m, mode);
-            if (cursor_begin(s.cu, s.w)) {
+            s.m = ops[op].m;
+            s.w = op_work(s.m, mode);
+            if (cursor_begin(s.cu, s.w, s.m)) {
                 s.step = step;
                 s.op = op;
                 return;
@@ -173,12 +248,10 @@ __device__ __forceinline__ void seq_enter(Seq& s, const OpDesc* ops, int nops, i
 
 __device__ __forceinline__ void seq_issue_next(Seq& s, Ring& r, const OpDesc* ops, int nops, int steps, int mode) {
     if (s.step >= steps) return;
-    const MatDesc& m = ops[s.op].m;
-    int tile, c, bytes;
-    cursor_tc(s.cu, s.w, m, tile, c);
-    const uint8_t* src = chunk_src(m, tile, c, bytes);
+    int bytes;
+    const uint8_t* src = chunk_src(s.m, s.cu.tile, s.cu.c, bytes);
     ring_issue(r, src, bytes);
-    if (!cursor_next(s.cu, s.w, m)) seq_enter(s, ops, nops, steps, mode, s.step, s.op + 1);
+    if (!cursor_next(s.cu, s.w, s.m)) seq_enter(s, ops, nops, steps, mode, s.step, s.op + 1);
 }
 
 // ---------------------------------------------------------------------------
@@ -201,7 +274,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
     const OpWork w = op_work(m, MODE);
     bool ok = true;
     OpCursor cu;
-    bool more = cursor_begin(cu, w);
+    bool more = cursor_begin(cu, w, m);
     if (w.split) {
         const int tf = w.u0 / m.nch, tl = (w.u1 - 1) / m.nch, ntl = tl - tf + 1;
         for (int i = tid; i < ntl * kWarps * kTR; i += blockDim.x) os.part[i] = 0.0f;
@@ -209,8 +282,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
         float a0 = 0.0f, a1 = 0.0f;
         int cur = -1;
         while (more) {
-            int tile, c;
-            cursor_tc(cu, w, m, tile, c);
+            const int tile = cu.tile, c = cu.c;
             if (tile != cur) {
                 if (cur >= 0) {
                     quad_reduce<MODE>(a0, a1);
@@ -228,7 +300,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
             chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, lf, a0, a1);
             __syncwarp();
-            ring.consumed++;
+            ring_release(ring);
             seq_issue_next(seq, ring, ops, nops, steps, MODE);
             more = cursor_next(cu, w, m);
         }
@@ -250,49 +322,55 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
         __syncthreads();
         // Tiles cut by a CTA boundary: local tile 0 when u0 is inside a tile
         // (this CTA has the tile's second part), the last local tile when u1
-        // is (this CTA has the first part).  The CTA arriving second adds
-        // first + second and finishes the tile.
-        int finish[2] = {1, 1};
-        for (int k = 0; k < 2; k++) {
-            const bool cut = k == 0 ? (w.u0 % m.nch) != 0 : (w.u1 % m.nch) != 0;
-            if (!cut) continue;
-            const int lt = k == 0 ? 0 : ntl - 1, partno = k == 0 ? 1 : 0, tile = tf + lt;
-            if (tid < kTR) __stcg(split_part + ((size_t)tile * 2 + partno) * kTR + tid, os.vals[lt * kTR + tid]);
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) os.state[k] = atomicAdd(split_cnt + tile, 1);
-            __syncthreads();
-            if (os.state[k] == 1) {
+        // is (this CTA has the first part).  Each part is published with one
+        // fence; the CTA arriving second adds first + second and finishes
+        // the tile.
+        const bool cut0 = (w.u0 % m.nch) != 0, cut1 = (w.u1 % m.nch) != 0;
+        const int tile0 = tf, tile1 = tl;
+        if (cut0 || cut1) {
+            if (cut0 && tid < kTR) {
+                __stcg(split_part + ((size_t)tile0 * 2 + 1) * kTR + tid, os.vals[tid]);
                 __threadfence();
-                if (tid < kTR) {
-                    const float mine = os.vals[lt * kTR + tid];
-                    const float other = __ldcg(split_part + ((size_t)tile * 2 + (1 - partno)) * kTR + tid);
-                    os.vals[lt * kTR + tid] = partno == 0 ? mine + other : other + mine;
-                }
-                if (tid == 0) split_cnt[tile] = 0;
-            } else {
-                finish[k] = 0;
+            }
+            if (cut1 && tid >= 32 && tid < 32 + kTR) {
+                __stcg(split_part + ((size_t)tile1 * 2 + 0) * kTR + (tid - 32), os.vals[(ntl - 1) * kTR + tid - 32]);
+                __threadfence();
+            }
+            __syncthreads();
+            if (cut0 && tid == 0) os.state[0] = atomicAdd(split_cnt + tile0, 1);
+            if (cut1 && tid == 32) os.state[1] = atomicAdd(split_cnt + tile1, 1);
+            __syncthreads();
+            if (cut0 && os.state[0] == 1 && tid < kTR) {
+                __threadfence();
+                const float first = __ldcg(split_part + ((size_t)tile0 * 2 + 0) * kTR + tid);
+                os.vals[tid] = first + os.vals[tid];
+                if (tid == 0) split_cnt[tile0] = 0;
+            }
+            if (cut1 && os.state[1] == 1 && tid >= 32 && tid < 32 + kTR) {
+                __threadfence();
+                const float second = __ldcg(split_part + ((size_t)tile1 * 2 + 1) * kTR + tid - 32);
+                os.vals[(ntl - 1) * kTR + tid - 32] = os.vals[(ntl - 1) * kTR + tid - 32] + second;
+                if (tid == 32) split_cnt[tile1] = 0;
             }
             __syncthreads();
         }
+        const bool skip0 = cut0 && os.state[0] != 1, skip1 = cut1 && os.state[1] != 1;
         for (int i = tid; i < ntl * (kTR / kRB); i += blockDim.x) {
             const int lt = i / (kTR / kRB), q = i % (kTR / kRB);
-            if (lt == 0 && (w.u0 % m.nch) != 0 && !finish[0]) continue;
-            if (lt == ntl - 1 && (w.u1 % m.nch) != 0 && !finish[1]) continue;
+            if ((lt == 0 && skip0) || (lt == ntl - 1 && skip1)) continue;
             epi((tf + lt) * kTR + q * kRB, os.vals + lt * kTR + q * kRB);
         }
     } else {
         float a0 = 0.0f, a1 = 0.0f;
         float* stage = os.part + warp * kTR;
         while (more) {
-            int tile, c;
-            cursor_tc(cu, w, m, tile, c);
+            const int tile = cu.tile, c = cu.c;
             const unsigned char* ch = ring_wait(ring, ring_base);
             if (!ch) { ok = false; break; }
             const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
             chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, lf, a0, a1);
             __syncwarp();
-            ring.consumed++;
+            ring_release(ring);
             seq_issue_next(seq, ring, ops, nops, steps, MODE);
             if (c == m.nch - 1) {
                 quad_reduce<MODE>(a0, a1);
@@ -382,112 +460,148 @@ struct DecodeEpi {
 };
 
 // ---------------------------------------------------------------------------
-// Attention of one layer (CTA-wide).  Unit (head h, chunk k) covers
-// positions [64k, 64k+64) ∩ [0, pos]: scores (q . k_t) / sqrtf(head_size)
-// (src/kernel_simd.c:1099-1117), local max, e^(s - max), their sum and the
-// weighted V sum are written as a partial; the last CTA to finish a head
-// merges the partials in chunk order into att[h].
+// Attention of one layer, split into warp units: unit (head h, chunk k)
+// covers positions [16k, 16k+16) ∩ [0, pos], one warp each, spread over every
+// warp of the grid.  Scores (q . k_t) / sqrtf(head_size) (src/kernel_simd.c:
+// 1099-1117), local max, e^(s - max), their sum and the weighted V sum; with
+// a single chunk the warp writes att[h] directly, otherwise it writes a
+// partial and the last warp to finish a head merges the partials in chunk
+// order.  Unit u runs on CTA u mod G, warp u div G, so short contexts put one
+// unit on each SM.  A unit makes two dependent trips to memory: q with all
+// of its K rows (4 lanes per position, a quarter of the head each, 8
+// positions per pass), then all of its V rows (4 consecutive elements of the
+// head per lane).
+// Partial layout per (head, chunk): [max, sum, -, -, o[0..hs)].
 // ---------------------------------------------------------------------------
-struct AttnSmem {
-    float q[kMaxHead];
-    float s[kAttnLen];
-    float o[kThreads];             // groups * head_size <= kThreads
-    float red[32];
-    int last;
-};
+constexpr int kAttnUnit = 16;
+constexpr int kQ4 = kMaxHead / 16;     // float4 of K per lane per position
 
-__device__ void attention_layer(const DecodeArgs& a, int layer, int pos, AttnSmem& sm) {
-    const int hs = a.head_size, tid = threadIdx.x;
-    const int nch = (pos + kAttnLen) / kAttnLen;
+__device__ void attention_layer(const DecodeArgs& a, int layer, int pos) {
+    const int hs = a.head_size, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hq = hs / 4, sub = lane & 3, pg = lane >> 2;
+    const int nch = pos / kAttnUnit + 1;
     const int units = a.n_heads * nch;
     const size_t lkv = (size_t)layer * a.max_pos * a.kv_dim;
     const float* kc = a.kcache + lkv;
     const float* vc = a.vcache + lkv;
     const float rs = sqrtf((float)hs);
-    const int groups = blockDim.x / hs;           // position groups for the V sum (>= 1)
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        const int h = u / nch, k = u % nch;
+    const int pstride = hs + 4;
+    const int nw = gridDim.x * kWarps;
+    const bool vl = 4 * lane < hs;
+    const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int u = warp * gridDim.x + blockIdx.x; u < units; u += nw) {
+        const int h = u / nch, k = u - (u / nch) * nch;
         const int kvh = h / a.kv_mul;
-        const int t0 = k * kAttnLen, n = min(kAttnLen, pos + 1 - t0);
-        for (int i = tid; i < hs; i += blockDim.x) sm.q[i] = __ldcg(a.q + h * hs + i);
-        __syncthreads();
-        // scores: 4 threads per position, each a quarter of the head
-        {
-            const int p = tid >> 2, part = tid & 3;
-            float dot = 0.0f;
-            if (p < n) {
-                const float* kr = kc + (size_t)(t0 + p) * a.kv_dim + kvh * hs;
-                const int q4 = hs / 4;
-                if ((q4 & 3) == 0) {
-                    for (int i = part * q4; i < (part + 1) * q4; i += 4) {
-                        const float4 kv4 = __ldcg(reinterpret_cast<const float4*>(kr + i));
-                        dot = fmaf(sm.q[i], kv4.x, dot);
-                        dot = fmaf(sm.q[i + 1], kv4.y, dot);
-                        dot = fmaf(sm.q[i + 2], kv4.z, dot);
-                        dot = fmaf(sm.q[i + 3], kv4.w, dot);
-                    }
-                } else {
-                    for (int i = part; i < hs; i += 4) dot = fmaf(sm.q[i], __ldcg(kr + i), dot);
-                }
-            }
-            dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-            dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-            if (part == 0 && p < kAttnLen) sm.s[p] = p < n ? __fdiv_rn(dot, rs) : -INFINITY;
+        const int t0 = k * kAttnUnit, n = min(kAttnUnit, pos + 1 - t0);
+        const float* qp = a.q + h * hs + sub * hq;
+        const float* kr0 = kc + (size_t)(t0 + pg) * a.kv_dim + kvh * hs + sub * hq;
+        const float* kr1 = kr0 + (size_t)8 * a.kv_dim;
+        float4 qv[kQ4], k0[kQ4], k1[kQ4];
+#pragma unroll
+        for (int j = 0; j < kQ4; j++) {
+            const bool in = 4 * j < hq;
+            qv[j] = in ? __ldcg(reinterpret_cast<const float4*>(qp + 4 * j)) : z4;
+            k0[j] = (in && pg < n) ? __ldcg(reinterpret_cast<const float4*>(kr0 + 4 * j)) : z4;
+            k1[j] = (in && pg + 8 < n) ? __ldcg(reinterpret_cast<const float4*>(kr1 + 4 * j)) : z4;
         }
-        __syncthreads();
-        float m = tid < n ? sm.s[tid] : -INFINITY;
-        m = block_max(m, sm.red);
-        float e = 0.0f;
-        if (tid < n) {
-            e = expf_cr(sm.s[tid] - m);
-            sm.s[tid] = e;
+        float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kQ4; j++) {
+            d0 = fmaf(qv[j].x, k0[j].x, d0);
+            d0 = fmaf(qv[j].y, k0[j].y, d0);
+            d0 = fmaf(qv[j].z, k0[j].z, d0);
+            d0 = fmaf(qv[j].w, k0[j].w, d0);
+            d1 = fmaf(qv[j].x, k1[j].x, d1);
+            d1 = fmaf(qv[j].y, k1[j].y, d1);
+            d1 = fmaf(qv[j].z, k1[j].z, d1);
+            d1 = fmaf(qv[j].w, k1[j].w, d1);
         }
-        const float l = block_sum(e, sm.red);
-        __syncthreads();
-        // V: thread (group gi, dim i) sums positions gi, gi + groups, ...;
-        // the group sums are added in group order.
-        {
-            const int gi = tid / hs, i = tid % hs;
-            if (gi < groups) {
-                float o = 0.0f;
-                for (int p = gi; p < n; p += groups)
-                    o = fmaf(sm.s[p], __ldcg(vc + (size_t)(t0 + p) * a.kv_dim + kvh * hs + i), o);
-                sm.o[gi * hs + i] = o;
-            }
+        d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+        d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+        d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
+        d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+        float sc[kAttnUnit];
+#pragma unroll
+        for (int pp = 0; pp < 8; pp++) {
+            sc[pp] = __shfl_sync(0xffffffffu, d0, pp * 4);
+            sc[8 + pp] = __shfl_sync(0xffffffffu, d1, pp * 4);
         }
-        __syncthreads();
-        float* part = a.attn_part + ((size_t)h * a.max_chunks + k) * (hs + 2);
-        for (int i = tid; i < hs; i += blockDim.x) {
-            float o = sm.o[i];
-            for (int g = 1; g < groups; g++) o += sm.o[g * hs + i];
-            __stcg(part + 2 + i, o);
+        const float* vr = vc + (size_t)t0 * a.kv_dim + kvh * hs + 4 * lane;
+        float4 vv[kAttnUnit];
+#pragma unroll
+        for (int p = 0; p < kAttnUnit; p++)
+            vv[p] = (p < n && vl) ? __ldcg(reinterpret_cast<const float4*>(vr + (size_t)p * a.kv_dim)) : z4;
+        float m = -INFINITY;
+#pragma unroll
+        for (int p = 0; p < kAttnUnit; p++) {
+            sc[p] = p < n ? __fdiv_rn(sc[p], rs) : -INFINITY;
+            m = fmaxf(m, sc[p]);
         }
-        if (tid == 0) {
+        float l = 0.0f;
+#pragma unroll
+        for (int p = 0; p < kAttnUnit; p++) {
+            sc[p] = p < n ? expf(sc[p] - m) : 0.0f;
+            l += sc[p];
+        }
+        float4 o = z4;
+#pragma unroll
+        for (int p = 0; p < kAttnUnit; p++) {
+            o.x = fmaf(sc[p], vv[p].x, o.x);
+            o.y = fmaf(sc[p], vv[p].y, o.y);
+            o.z = fmaf(sc[p], vv[p].z, o.z);
+            o.w = fmaf(sc[p], vv[p].w, o.w);
+        }
+        if (nch == 1) {
+            const float inv = 1.0f / l;
+            if (vl) __stcg(reinterpret_cast<float4*>(a.att + h * hs + 4 * lane),
+                           make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv));
+            continue;
+        }
+        float* part = a.attn_part + ((size_t)h * a.max_chunks + k) * pstride;
+        if (vl) __stcg(reinterpret_cast<float4*>(part + 4 + 4 * lane), o);
+        if (lane == 0) {
             __stcg(part, m);
             __stcg(part + 1, l);
         }
         __threadfence();
-        __syncthreads();
-        if (tid == 0) sm.last = (atomicAdd(a.attn_cnt + h, 1) == nch - 1);
-        __syncthreads();
-        if (sm.last) {
-            __threadfence();
-            const float* ph = a.attn_part + (size_t)h * a.max_chunks * (hs + 2);
-            float M = -INFINITY;
-            for (int c = 0; c < nch; c++) M = fmaxf(M, __ldcg(ph + (size_t)c * (hs + 2)));
-            float L = 0.0f;
-            for (int c = 0; c < nch; c++)
-                L = fmaf(__ldcg(ph + (size_t)c * (hs + 2) + 1), expf_cr(__ldcg(ph + (size_t)c * (hs + 2)) - M), L);
-            const float inv = 1.0f / L;
-            for (int i = tid; i < hs; i += blockDim.x) {
-                float o = 0.0f;
-                for (int c = 0; c < nch; c++)
-                    o = fmaf(__ldcg(ph + (size_t)c * (hs + 2) + 2 + i), expf_cr(__ldcg(ph + (size_t)c * (hs + 2)) - M), o);
-                __stcg(a.att + h * hs + i, o * inv);
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(a.attn_cnt + h, 1) == nch - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        // Merge: lane c holds chunk c's max and sum (32 chunks per pass).
+        const float* ph = a.attn_part + (size_t)h * a.max_chunks * pstride;
+        float M = -INFINITY;
+        for (int c0 = 0; c0 < nch; c0 += 32)
+            if (c0 + lane < nch) M = fmaxf(M, __ldcg(ph + (size_t)(c0 + lane) * pstride));
+        M = warp_max(M);
+        float L = 0.0f;
+        float4 acc = z4;
+        for (int c0 = 0; c0 < nch; c0 += 32) {
+            const int cn = min(32, nch - c0);
+            float wl = 0.0f, ll = 0.0f;
+            if (lane < cn) {
+                wl = expf(__ldcg(ph + (size_t)(c0 + lane) * pstride) - M);
+                ll = __ldcg(ph + (size_t)(c0 + lane) * pstride + 1);
             }
-            if (tid == 0) a.attn_cnt[h] = 0;
+            for (int c = 0; c < cn; c++) {
+                const float wgt = __shfl_sync(0xffffffffu, wl, c);
+                const float lc = __shfl_sync(0xffffffffu, ll, c);
+                L = fmaf(lc, wgt, L);
+                if (vl) {
+                    const float4 oc = __ldcg(reinterpret_cast<const float4*>(ph + (size_t)(c0 + c) * pstride + 4 + 4 * lane));
+                    acc.x = fmaf(oc.x, wgt, acc.x);
+                    acc.y = fmaf(oc.y, wgt, acc.y);
+                    acc.z = fmaf(oc.z, wgt, acc.z);
+                    acc.w = fmaf(oc.w, wgt, acc.w);
+                }
+            }
         }
-        __syncthreads();
+        const float inv = 1.0f / L;
+        if (vl) __stcg(reinterpret_cast<float4*>(a.att + h * hs + 4 * lane),
+                       make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+        if (lane == 0) a.attn_cnt[h] = 0;
     }
 }
 
@@ -575,9 +689,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
     __shared__ __align__(8) uint64_t bars[kWarps * 8];
     __shared__ float red[32];
     __shared__ unsigned long long red64[kWarps];
-    __shared__ AttnSmem attn;
     __shared__ OpSmem os;
     __shared__ int s_tok, s_pos, s_bad;
+    __shared__ __align__(16) OpDesc s_ops[2];   // current op, and the next one being fetched
     unsigned char* xf = smem;
     float* xs = reinterpret_cast<float*>(smem + a.xs_off);
     unsigned char* ring_base = smem + a.xbytes;
@@ -588,6 +702,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
     seq_enter(seq, a.ops, a.nops, a.steps, MODE, 0, 0);
     for (int i = 0; i < a.P; i++) seq_issue_next(seq, ring, a.ops, a.nops, a.steps, MODE);
 
+    constexpr int kOpWords = sizeof(OpDesc) / 4;
+    static_assert(sizeof(OpDesc) % 4 == 0 && kOpWords <= kThreads, "OpDesc copy");
+    if (threadIdx.x < kOpWords)
+        reinterpret_cast<int*>(&s_ops[0])[threadIdx.x] = __ldg(reinterpret_cast<const int*>(a.ops) + threadIdx.x);
+    int oslot = 0;
     uint32_t nbar = 0;
     bool ok = true;
     for (int step = 0; step < a.steps && ok; step++) {
@@ -615,8 +734,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
             for (int i = threadIdx.x; i < a.dim / 4; i += blockDim.x)
                 __stcg(reinterpret_cast<float4*>(a.x) + i, src_load4(emb_src, i));
 
-        for (int oi = 0; oi < a.nops && ok; oi++) {
-            const OpDesc op = a.ops[oi];
+        for (int oi = 0; oi < a.nops && ok; oi++, oslot ^= 1) {
+            const OpDesc op = s_ops[oslot];
             VecSrc src;
             src.emb = a.emb;
             src.tok = tok;
@@ -634,10 +753,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
             } else {
                 src.p = op.kind == OP_WO ? a.att : a.hb;
             }
-            const float ss = !nw ? 1.0f
-                             : (MODE == MODE_W4A8 ? src_rms_scale_exact(src, op.m.n, red) : src_rms_scale(src, op.m.n, red));
-            src_build_digits<MODE>(xf, xs, src, op.m.n, nw, ss);
+            build_input<MODE>(xf, xs, src, op.m.n, nw, red);
             __syncthreads();
+            if (threadIdx.x < kOpWords) {   // next op (op 0 of the next step after the classifier)
+                const int nx = oi + 1 < a.nops ? oi + 1 : 0;
+                reinterpret_cast<int*>(&s_ops[oslot ^ 1])[threadIdx.x] =
+                    __ldg(reinterpret_cast<const int*>(a.ops + nx) + threadIdx.x);
+            }
             DecodeEpi epi{&a, &op, pos, -1e9f, 0u};
             if (!run_op<MODE>(op.m, ring, ring_base, seq, a.ops, a.nops, a.steps, xf, xs, os, a.split_part, a.split_cnt,
                               epi)) {
@@ -663,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
                 if (MODE == MODE_W4A8)
                     attention_layer_exact(a, op.layer, pos, reinterpret_cast<float*>(xf), red);
                 else
-                    attention_layer(a, op.layer, pos, attn);
+                    attention_layer(a, op.layer, pos);
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             }
         }
@@ -716,7 +838,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_matvec(StandaloneArgs a) {
     src.p = a.x;
     src.tok = 0;
     src.emb = a.op.m;
-    src_build_digits<MODE>(xf, xs, src, a.op.m.n, nullptr, 1.0f);
+    __shared__ float red[32];
+    build_input<MODE>(xf, xs, src, s_op.m.n, nullptr, red);
     __syncthreads();
     StoreEpi epi{a.y, a.op.m.d};
     if (!run_op<MODE>(s_op.m, ring, ring_base, seq, &s_op, 1, 1, xf, xs, os, a.split_part, a.split_cnt, epi))

@@ -47,6 +47,7 @@ struct MatDesc {
     const uint8_t* w;
     long long tile_bytes;          // G * 320
     int n, G, nch;                 // columns, groups per row, chunks per tile
+    int cg, cr;                    // chunk c spans cg groups, one more for c < cr
     int ntiles, d;                 // tiles, logical rows
 };
 
@@ -59,14 +60,16 @@ __host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, i
     m.nch = (int)((m.tile_bytes + kTargetChunk - 1) / kTargetChunk);
     if (m.nch < 1) m.nch = 1;
     if (m.nch > m.G) m.nch = m.G;
+    m.cg = m.G / m.nch;
+    m.cr = m.G % m.nch;
     m.ntiles = (int)((rows + kTR - 1) / kTR);
     m.d = (int)rows;
     return m;
 }
 
 __host__ __device__ inline long long desc_bytes(const MatDesc& m) { return m.tile_bytes * m.ntiles; }
-__host__ __device__ inline int chunk_g0(const MatDesc& m, int c) { return (int)(((long long)c * m.G) / m.nch); }
-__host__ __device__ inline int max_chunk_bytes(const MatDesc& m) { return (m.G + m.nch - 1) / m.nch * kGB; }
+__host__ __device__ inline int chunk_g0(const MatDesc& m, int c) { return c * m.cg + (c < m.cr ? c : m.cr); }
+__host__ __device__ inline int max_chunk_bytes(const MatDesc& m) { return (m.cg + (m.cr ? 1 : 0)) * kGB; }
 
 // ---------------------------------------------------------------------------
 // Activation digits in shared memory: group g at g*96: digit column p (0..2),
@@ -157,8 +160,7 @@ __device__ __forceinline__ void group_digits(unsigned char* xf, float* xs, int g
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
@@ -176,31 +178,73 @@ __device__ __forceinline__ float w4a16_lane_factor() {
 
 // Accumulates groups [0, ng) of one chunk of one tile held in shared memory
 // (group k of the chunk at chunk + k*320; g0 = its first group in the row).
-// acc0 / acc1 belong to rows r and r + 8 of the tile (r = lane / 4).
+// acc0 / acc1 belong to rows r and r + 8 of the tile (r = lane / 4).  Four
+// groups per step: their operand loads and MMAs are independent, only the
+// final accumulation is a chain.
+template <int MODE>
+__device__ __forceinline__ void group_accumulate(const int (&d)[4], float2 sw, float f, float lane_factor, float& acc0,
+                                                 float& acc1) {
+    if (MODE == MODE_W4A16) {
+        const float xsf = f * lane_factor;
+        acc0 = fmaf(sw.x * xsf, (float)(d[0] + 256 * d[1]), acc0);
+        acc1 = fmaf(sw.y * xsf, (float)(d[2] + 256 * d[3]), acc1);
+    } else {
+        acc0 = __fadd_rn(acc0, __fmul_rn((float)(d[0] >> 4), __fmul_rn(sw.x, f)));
+        acc1 = __fadd_rn(acc1, __fmul_rn((float)(d[2] >> 4), __fmul_rn(sw.y, f)));
+    }
+}
+
 template <int MODE>
 __device__ __forceinline__ void chunk_mma(const unsigned char* chunk, int ng, int g0, const unsigned char* xf,
                                           const float* xs, float lane_factor, float& acc0, float& acc1) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2;
-#pragma unroll 2
-    for (int k = 0; k < ng; k++) {
-        const unsigned char* gp = chunk + k * kGB;
-        const uint2 wv = *reinterpret_cast<const uint2*>(gp + 8 * lane);
-        const float2 sw = *reinterpret_cast<const float2*>(gp + 256 + 8 * r);
-        const int g = g0 + k;
-        uint2 xv = make_uint2(0u, 0u);
-        if (lane < 12) xv = *reinterpret_cast<const uint2*>(xf + (size_t)g * kXF + 8 * lane);
-        int d[4];
-        mma_s8(d, lo16(wv.x), lo16(wv.y), hi16(wv.x), hi16(wv.y), xv.x, xv.y);
-        const float f = xs[g];
-        if (MODE == MODE_W4A16) {
-            const float xsf = f * lane_factor;
-            acc0 = fmaf(sw.x * xsf, (float)(d[0] + 256 * d[1]), acc0);
-            acc1 = fmaf(sw.y * xsf, (float)(d[2] + 256 * d[3]), acc1);
-        } else {
-            acc0 = __fadd_rn(acc0, __fmul_rn((float)(d[0] >> 4), __fmul_rn(sw.x, f)));
-            acc1 = __fadd_rn(acc1, __fmul_rn((float)(d[2] >> 4), __fmul_rn(sw.y, f)));
+    const bool xl = lane < 12;
+    const unsigned char* wp = chunk + 8 * lane;
+    const unsigned char* sp = chunk + 256 + 8 * r;
+    const unsigned char* xp = xf + (size_t)g0 * kXF + 8 * lane;
+    const float* fp = xs + g0;
+    int k = 0;
+    for (; k + 4 <= ng; k += 4) {
+        uint2 wv[4], xv[4];
+        float2 sw[4];
+        float f[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            wv[j] = *reinterpret_cast<const uint2*>(wp + (k + j) * kGB);
+            sw[j] = *reinterpret_cast<const float2*>(sp + (k + j) * kGB);
+            xv[j] = xl ? *reinterpret_cast<const uint2*>(xp + (k + j) * kXF) : make_uint2(0u, 0u);
+            f[j] = fp[k + j];
         }
+        int d[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            mma_s8(d[j], lo16(wv[j].x), lo16(wv[j].y), hi16(wv[j].x), hi16(wv[j].y), xv[j].x, xv[j].y);
+#pragma unroll
+        for (int j = 0; j < 4; j++) group_accumulate<MODE>(d[j], sw[j], f[j], lane_factor, acc0, acc1);
+    }
+    if (k < ng) {
+        // Last 1-3 groups as one step of four; the missing groups read the
+        // chunk's last group with all-zero weights (nibbles 8), whose
+        // products add exactly zero.
+        uint2 wv[4], xv[4];
+        float2 sw[4];
+        float f[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int kk = min(k + j, ng - 1);
+            wv[j] = *reinterpret_cast<const uint2*>(wp + kk * kGB);
+            if (k + j >= ng) wv[j] = make_uint2(0x88888888u, 0x88888888u);
+            sw[j] = *reinterpret_cast<const float2*>(sp + kk * kGB);
+            xv[j] = xl ? *reinterpret_cast<const uint2*>(xp + kk * kXF) : make_uint2(0u, 0u);
+            f[j] = fp[kk];
+        }
+        int d[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            mma_s8(d[j], lo16(wv[j].x), lo16(wv[j].y), hi16(wv[j].x), hi16(wv[j].y), xv[j].x, xv[j].y);
+#pragma unroll
+        for (int j = 0; j < 4; j++) group_accumulate<MODE>(d[j], sw[j], f[j], lane_factor, acc0, acc1);
     }
 }
 
@@ -228,6 +272,8 @@ struct Ring {
     uint32_t bars;       // shared address of this warp's mbarrier 0
     int P, slot_bytes;
     uint32_t issued, consumed;
+    int islot, cslot;    // issued % P, consumed % P
+    uint32_t cphase;     // (consumed / P) & 1
 };
 
 __device__ __forceinline__ void ring_init(Ring& r, unsigned char* ring_base, uint64_t* bar_base, int P, int slot_bytes) {
@@ -237,6 +283,8 @@ __device__ __forceinline__ void ring_init(Ring& r, unsigned char* ring_base, uin
     r.slots = smem_addr(ring_base + (size_t)warp * P * slot_bytes);
     r.bars = smem_addr(bar_base + warp * P);
     r.issued = r.consumed = 0;
+    r.islot = r.cslot = 0;
+    r.cphase = 0;
     if (lane == 0)
         for (int i = 0; i < P; i++) mbar_init(r.bars + 8 * i, 1);
     fence_mbar_init();
@@ -244,31 +292,36 @@ __device__ __forceinline__ void ring_init(Ring& r, unsigned char* ring_base, uin
 }
 
 __device__ __forceinline__ void ring_issue(Ring& r, const uint8_t* src, int bytes) {
-    const int slot = r.issued % r.P;
+    const int slot = r.islot;
     if ((threadIdx.x & 31) == 0) {
         const uint32_t bar = r.bars + 8 * slot;
         mbar_arrive_expect_tx(bar, (uint32_t)bytes);
         bulk_g2s(r.slots + slot * r.slot_bytes, src, (uint32_t)bytes, bar);
     }
     r.issued++;
+    r.islot = slot + 1 == r.P ? 0 : slot + 1;
 }
 
 // Waits for the oldest issued chunk; returns its generic shared pointer, or
-// nullptr on timeout.
+// nullptr on timeout.  ring_release() then frees the slot.
 __device__ __forceinline__ const unsigned char* ring_wait(Ring& r, unsigned char* ring_base) {
-    const int slot = r.consumed % r.P;
-    const uint32_t parity = (r.consumed / r.P) & 1;
-    if (!mbar_wait(r.bars + 8 * slot, parity)) return nullptr;
+    if (!mbar_wait(r.bars + 8 * r.cslot, r.cphase)) return nullptr;
     const int warp = threadIdx.x >> 5;
-    return ring_base + ((size_t)warp * r.P + slot) * r.slot_bytes;
+    return ring_base + ((size_t)warp * r.P + r.cslot) * r.slot_bytes;
+}
+__device__ __forceinline__ void ring_release(Ring& r) {
+    r.consumed++;
+    if (++r.cslot == r.P) {
+        r.cslot = 0;
+        r.cphase ^= 1u;
+    }
 }
 
 // Drains every chunk still in flight (bounded), so the CTA may exit safely.
 __device__ __forceinline__ void ring_drain(Ring& r) {
     while (r.consumed < r.issued) {
-        const int slot = r.consumed % r.P;
-        mbar_wait(r.bars + 8 * slot, (r.consumed / r.P) & 1, 1u << 20);
-        r.consumed++;
+        mbar_wait(r.bars + 8 * r.cslot, r.cphase, 1u << 20);
+        ring_release(r);
     }
 }
 
@@ -298,31 +351,35 @@ __device__ __forceinline__ OpWork op_work(const MatDesc& m, int mode) {
     return w;
 }
 
-// Position in a warp's chunk sequence of one op.
+// Position in a warp's chunk sequence of one op: unit index a (split) or
+// tile index (whole), and the tile / chunk it stands for.
 struct OpCursor {
-    int a, b;            // split: unit index, -; whole: tile, chunk
+    int a, tile, c;
 };
 
-__device__ __forceinline__ bool cursor_begin(OpCursor& cu, const OpWork& w) {
+__device__ __forceinline__ bool cursor_begin(OpCursor& cu, const OpWork& w, const MatDesc& m) {
     cu.a = w.u0 + (int)(threadIdx.x >> 5);
-    cu.b = 0;
-    return cu.a < w.u1;
-}
-__device__ __forceinline__ void cursor_tc(const OpCursor& cu, const OpWork& w, const MatDesc& m, int& tile, int& c) {
     if (w.split) {
-        tile = cu.a / m.nch;
-        c = cu.a % m.nch;
+        cu.tile = cu.a / m.nch;
+        cu.c = cu.a - cu.tile * m.nch;
     } else {
-        tile = cu.a;
-        c = cu.b;
+        cu.tile = cu.a;
+        cu.c = 0;
     }
+    return cu.a < w.u1;
 }
 __device__ __forceinline__ bool cursor_next(OpCursor& cu, const OpWork& w, const MatDesc& m) {
     if (w.split) {
         cu.a += kWarps;
-    } else if (++cu.b == m.nch) {
-        cu.b = 0;
+        cu.c += kWarps;
+        while (cu.c >= m.nch) {
+            cu.c -= m.nch;
+            cu.tile++;
+        }
+    } else if (++cu.c == m.nch) {
+        cu.c = 0;
         cu.a += kWarps;
+        cu.tile = cu.a;
     }
     return cu.a < w.u1;
 }
