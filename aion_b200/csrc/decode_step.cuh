@@ -155,45 +155,56 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
             v[i].w = __fmul_rn(__fmul_rn(v[i].w, ss), w[i].w);
         }
     }
+    // W4A16: one exponent for the vector, from its largest magnitude M;
+    // vectors with M < 2^-93 count as zero.
+    int E = 0;
+    bool live = false;
+    float sa = 0.0f, sb = 0.0f;
+    if (MODE == MODE_W4A16) {
+        float mx = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; i++)
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        mx = block_max(mx, red);
+        const int ebits = (int)((__float_as_uint(mx) >> 23) & 0xFF);
+        live = ebits >= 34;
+        E = 156 - ebits;                                   // M * 2^E in [2^29, 2^30)
+        sa = __int_as_float((127 + E / 2) << 23);
+        sb = __int_as_float((127 + E - E / 2) << 23);
+        if (tid == 0) xs[0] = live ? __int_as_float((127 - E - 4) << 23) : 0.0f;   // 2^-E / 16
+    }
 #pragma unroll
     for (int i = 0; i < NV; i++) {
         if (i * kThreads >= nv) break;                      // uniform across the CTA
         const int j = tid + i * kThreads;
         const bool valid = j < nv;                          // same for the 8 threads of a group
         const int g = j >> 3, q = j & 7;
-        float m = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        if (!valid) continue;
         // element 4q + b sits in fragment lane t = q & 3, word (q >> 2)
         unsigned char* dst = xf + (size_t)g * kXF + (q & 3) * 8 + (q >> 2) * 4;
         const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
         if (MODE == MODE_W4A16) {
-            const int ebits = (int)((__float_as_uint(m) >> 23) & 0xFF);
-            int d0[4], d1[4], d2[4];
-            float factor = 0.0f;
-            if (ebits > 127 - 60) {       // max |x| >= 2^-60; smaller groups count as zero
-                const int E = 22 - (ebits - 126);                // m * 2^E in [2^21, 2^22)
-                const float sa = __int_as_float((127 + E / 2) << 23), sb = __int_as_float((127 + E - E / 2) << 23);
+            if (!valid) continue;
+            int d0[4], d1[4], d2[4], d3[4];
 #pragma unroll
-                for (int b = 0; b < 4; b++) {
-                    const int X = __float2int_rn(__fmul_rn(__fmul_rn(e[b], sa), sb));
-                    d0[b] = ((X + 128) & 255) - 128;
-                    const int r = (X - d0[b]) >> 8;
-                    d1[b] = ((r + 128) & 255) - 128;
-                    d2[b] = (r - d1[b]) >> 8;
-                }
-                factor = __int_as_float((127 - E - 4) << 23);   // 2^-E / 16
-            } else {
-#pragma unroll
-                for (int b = 0; b < 4; b++) d0[b] = d1[b] = d2[b] = 0;
+            for (int b = 0; b < 4; b++) {
+                const int X = live ? __float2int_rn(__fmul_rn(__fmul_rn(e[b], sa), sb)) : 0;
+                d0[b] = ((X + 128) & 255) - 128;
+                const int r1 = (X - d0[b]) >> 8;
+                d1[b] = ((r1 + 128) & 255) - 128;
+                const int r2 = (r1 - d1[b]) >> 8;
+                d2[b] = ((r2 + 128) & 255) - 128;
+                d3[b] = (r2 - d2[b]) >> 8;
             }
             *reinterpret_cast<uint32_t*>(dst) = pack4(d0[0], d0[1], d0[2], d0[3]);
             *reinterpret_cast<uint32_t*>(dst + 32) = pack4(d1[0], d1[1], d1[2], d1[3]);
             *reinterpret_cast<uint32_t*>(dst + 64) = pack4(d2[0], d2[1], d2[2], d2[3]);
-            if (q == 0) xs[g] = factor;
+            *reinterpret_cast<uint32_t*>(dst + 96) = pack4(d3[0], d3[1], d3[2], d3[3]);
         } else {
+            float m = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+            if (!valid) continue;
             // quantize_activations_neon (src/kernel_simd.c:186-227), bit-exact
             const bool big = m > 1e-9f;
             const float scale = big ? __fdiv_rn(127.0f, m) : 1.0f;
@@ -201,8 +212,6 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
 #pragma unroll
             for (int b = 0; b < 4; b++) qv[b] = (int)roundf(__fmul_rn(e[b], scale));
             *reinterpret_cast<uint32_t*>(dst) = pack4(qv[0], qv[1], qv[2], qv[3]);
-            *reinterpret_cast<uint32_t*>(dst + 32) = 0u;
-            *reinterpret_cast<uint32_t*>(dst + 64) = 0u;
             if (q == 0) xs[g] = big ? __fdiv_rn(m, 127.0f) : 1.0f;
         }
     }
@@ -270,7 +279,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
                        int steps, const unsigned char* xf, const float* xs, OpSmem& os, float* split_part,
                        int* split_cnt, Epi& epi) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    const float lf = MODE == MODE_W4A16 ? w4a16_lane_factor() : 0.0f;
+    const float xfac = MODE == MODE_W4A16 ? xs[0] : 0.0f;
     const OpWork w = op_work(m, MODE);
     bool ok = true;
     OpCursor cu;
@@ -285,7 +294,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             const int tile = cu.tile, c = cu.c;
             if (tile != cur) {
                 if (cur >= 0) {
-                    quad_reduce<MODE>(a0, a1);
+                    quad_reduce<MODE>(a0, a1, xfac);
                     if ((lane & 3) == 0) {
                         float* p = os.part + ((cur - tf) * kWarps + warp) * kTR;
                         p[lane >> 2] = a0;
@@ -298,14 +307,14 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             const unsigned char* ch = ring_wait(ring, ring_base);
             if (!ch) { ok = false; break; }
             const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
-            chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, lf, a0, a1);
+            chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, a0, a1);
             __syncwarp();
             ring_release(ring);
             seq_issue_next(seq, ring, ops, nops, steps, MODE);
             more = cursor_next(cu, w, m);
         }
         if (ok && cur >= 0) {
-            quad_reduce<MODE>(a0, a1);
+            quad_reduce<MODE>(a0, a1, xfac);
             if ((lane & 3) == 0) {
                 float* p = os.part + ((cur - tf) * kWarps + warp) * kTR;
                 p[lane >> 2] = a0;
@@ -368,12 +377,12 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             const unsigned char* ch = ring_wait(ring, ring_base);
             if (!ch) { ok = false; break; }
             const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
-            chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, lf, a0, a1);
+            chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, a0, a1);
             __syncwarp();
             ring_release(ring);
             seq_issue_next(seq, ring, ops, nops, steps, MODE);
             if (c == m.nch - 1) {
-                quad_reduce<MODE>(a0, a1);
+                quad_reduce<MODE>(a0, a1, xfac);
                 if ((lane & 3) == 0) {
                     stage[lane >> 2] = a0;
                     stage[(lane >> 2) + 8] = a1;

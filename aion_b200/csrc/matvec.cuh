@@ -38,7 +38,7 @@ constexpr int kGB = 320;             // bytes per (tile, group)
 constexpr int kWarps = 8;            // warps per CTA
 constexpr int kThreads = kWarps * 32;
 constexpr int kTargetChunk = 6400;   // bytes per bulk copy, about
-constexpr int kXF = 96;              // bytes of activation digits per group
+constexpr int kXF = 128;             // bytes of activation digits per group (4 columns)
 constexpr int kMaxLocalTiles = 24;   // tiles of one op per CTA (split mode)
 
 enum Mode { MODE_W4A16 = 0, MODE_W4A8 = 1 };
@@ -72,88 +72,19 @@ __host__ __device__ inline int chunk_g0(const MatDesc& m, int c) { return c * m.
 __host__ __device__ inline int max_chunk_bytes(const MatDesc& m) { return (m.cg + (m.cr ? 1 : 0)) * kGB; }
 
 // ---------------------------------------------------------------------------
-// Activation digits in shared memory: group g at g*96: digit column p (0..2),
-// lane t (0..3): 8 bytes = the B-fragment words (elements 4t..4t+3 and
-// 16+4t..16+4t+3), so lane l < 12 of a warp loads its fragment at
-// g*96 + 8l.  Then G fp32 group factors (2^-E / 16 for W4A16, the activation
-// scale for W4A8).
+// Activation digits in shared memory: group g at g*128: digit column p
+// (0..3), lane t (0..3): 8 bytes = the B-fragment words (elements 4t..4t+3
+// and 16+4t..16+4t+3), so lane l of a warp loads its fragment at
+// g*128 + 8*(l % 16) (lanes 16..31 repeat columns 0..3 as columns 4..7,
+// whose products no lane uses).  Then G fp32 group factors: W4A8's
+// activation scales; W4A16 keeps one factor for the whole vector in xs[0].
+//   W4A16: X = round(x * 2^E) with one E per vector (max |x| * 2^E in
+//     [2^29, 2^30)), written as four signed bytes X = d0 + 2^8 d1 + 2^16 d2
+//     + 2^24 d3; factor 2^-E / 16 (the weight bytes carry 16 * q).
+//   W4A8: column 0 holds the reference's int8 activations; the other
+//     columns are not read for any output.
 // ---------------------------------------------------------------------------
 __host__ __device__ inline int xbuf_bytes(int n) { return (n / 32) * (kXF + 4); }
-
-// Packs 32 signed values (one digit column) into its 4 lanes' fragment words.
-__device__ __forceinline__ void store_digits(unsigned char* dst, const int* v) {
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-        uint32_t b0 = 0, b1 = 0;
-#pragma unroll
-        for (int b = 0; b < 4; b++) {
-            b0 |= (uint32_t)(v[4 * t + b] & 0xFF) << (8 * b);
-            b1 |= (uint32_t)(v[16 + 4 * t + b] & 0xFF) << (8 * b);
-        }
-        reinterpret_cast<uint2*>(dst)[t] = make_uint2(b0, b1);
-    }
-}
-
-// W4A16 digits of one group of 32 fp32 values.
-__device__ __forceinline__ void group_digits_w4a16(unsigned char* xf, float* xs, int g, const float* v) {
-    float m = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 32; k++) m = fmaxf(m, fabsf(v[k]));
-    const int ebits = (int)((__float_as_uint(m) >> 23) & 0xFF);
-    int X0[32], X1[32], X2[32];
-    float factor = 0.0f;
-    if (ebits > 127 - 60) {      // max |x| >= 2^-60; smaller groups count as zero
-        const int E = 22 - (ebits - 126);                 // m * 2^E in [2^21, 2^22)
-        const float sa = __int_as_float((127 + E / 2) << 23), sb = __int_as_float((127 + E - E / 2) << 23);
-#pragma unroll
-        for (int k = 0; k < 32; k++) {
-            const int X = __float2int_rn(__fmul_rn(__fmul_rn(v[k], sa), sb));
-            const int d0 = ((X + 128) & 255) - 128;
-            const int r = (X - d0) >> 8;
-            const int d1 = ((r + 128) & 255) - 128;
-            X0[k] = d0;
-            X1[k] = d1;
-            X2[k] = (r - d1) >> 8;
-        }
-        factor = __int_as_float((127 - E - 4) << 23);     // 2^-E / 16
-    } else {
-#pragma unroll
-        for (int k = 0; k < 32; k++) X0[k] = X1[k] = X2[k] = 0;
-    }
-    unsigned char* dst = xf + (size_t)g * kXF;
-    store_digits(dst, X0);
-    store_digits(dst + 32, X1);
-    store_digits(dst + 64, X2);
-    xs[g] = factor;
-}
-
-// W4A8 digits: the per-32 int8 quantization of quantize_activations_neon
-// (src/kernel_simd.c:186-227), bit-exact: amax; scale 127/amax if amax >
-// 1e-9 else 1; stored scale amax/127 (else 1); q = round-half-away(x*scale).
-__device__ __forceinline__ void group_digits_w4a8(unsigned char* xf, float* xs, int g, const float* v) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
-    const bool big = amax > 1e-9f;
-    const float scale = big ? __fdiv_rn(127.0f, amax) : 1.0f;
-    int q[32], z[32];
-#pragma unroll
-    for (int k = 0; k < 32; k++) {
-        q[k] = (int)roundf(__fmul_rn(v[k], scale));
-        z[k] = 0;
-    }
-    unsigned char* dst = xf + (size_t)g * kXF;
-    store_digits(dst, q);
-    store_digits(dst + 32, z);
-    store_digits(dst + 64, z);
-    xs[g] = big ? __fdiv_rn(amax, 127.0f) : 1.0f;
-}
-
-template <int MODE>
-__device__ __forceinline__ void group_digits(unsigned char* xf, float* xs, int g, const float* v) {
-    if (MODE == MODE_W4A16) group_digits_w4a16(xf, xs, g, v);
-    else group_digits_w4a8(xf, xs, g, v);
-}
 
 // ---------------------------------------------------------------------------
 // Tensor-pipe group dot.
@@ -169,25 +100,20 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, ui
 __device__ __forceinline__ uint32_t lo16(uint32_t w) { return ((w << 4) & 0xF0F0F0F0u) ^ 0x80808080u; }
 __device__ __forceinline__ uint32_t hi16(uint32_t w) { return (w & 0xF0F0F0F0u) ^ 0x80808080u; }
 
-// Lane factor of the W4A16 digit recombination: quad lane t = 0 holds digit
-// 0 + 256 * digit 1, t = 1 holds digit 2 (x 65536); t = 2, 3 see zero columns.
-__device__ __forceinline__ float w4a16_lane_factor() {
-    const int t = threadIdx.x & 3;
-    return t == 0 ? 1.0f : (t == 1 ? 65536.0f : 0.0f);
-}
-
 // Accumulates groups [0, ng) of one chunk of one tile held in shared memory
 // (group k of the chunk at chunk + k*320; g0 = its first group in the row).
 // acc0 / acc1 belong to rows r and r + 8 of the tile (r = lane / 4).  Four
 // groups per step: their operand loads and MMAs are independent, only the
 // final accumulation is a chain.
+//   W4A16: quad lane t = 0 holds columns 0, 1 (digits d0 + 2^8 d1), t = 1
+//     columns 2, 3 (d2 + 2^8 d3); each adds weight scale * that integer.
+//   W4A8: lane t = 0 adds (column 0 / 16) * (weight scale * activation
+//     scale) in the reference's order.
 template <int MODE>
-__device__ __forceinline__ void group_accumulate(const int (&d)[4], float2 sw, float f, float lane_factor, float& acc0,
-                                                 float& acc1) {
+__device__ __forceinline__ void group_accumulate(const int (&d)[4], float2 sw, float f, float& acc0, float& acc1) {
     if (MODE == MODE_W4A16) {
-        const float xsf = f * lane_factor;
-        acc0 = fmaf(sw.x * xsf, (float)(d[0] + 256 * d[1]), acc0);
-        acc1 = fmaf(sw.y * xsf, (float)(d[2] + 256 * d[3]), acc1);
+        acc0 = fmaf(sw.x, (float)(d[0] + 256 * d[1]), acc0);
+        acc1 = fmaf(sw.y, (float)(d[2] + 256 * d[3]), acc1);
     } else {
         acc0 = __fadd_rn(acc0, __fmul_rn((float)(d[0] >> 4), __fmul_rn(sw.x, f)));
         acc1 = __fadd_rn(acc1, __fmul_rn((float)(d[2] >> 4), __fmul_rn(sw.y, f)));
@@ -196,13 +122,12 @@ __device__ __forceinline__ void group_accumulate(const int (&d)[4], float2 sw, f
 
 template <int MODE>
 __device__ __forceinline__ void chunk_mma(const unsigned char* chunk, int ng, int g0, const unsigned char* xf,
-                                          const float* xs, float lane_factor, float& acc0, float& acc1) {
+                                          const float* xs, float& acc0, float& acc1) {
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2;
-    const bool xl = lane < 12;
     const unsigned char* wp = chunk + 8 * lane;
     const unsigned char* sp = chunk + 256 + 8 * r;
-    const unsigned char* xp = xf + (size_t)g0 * kXF + 8 * lane;
+    const unsigned char* xp = xf + (size_t)g0 * kXF + 8 * (lane & 15);
     const float* fp = xs + g0;
     int k = 0;
     for (; k + 4 <= ng; k += 4) {
@@ -213,15 +138,15 @@ __device__ __forceinline__ void chunk_mma(const unsigned char* chunk, int ng, in
         for (int j = 0; j < 4; j++) {
             wv[j] = *reinterpret_cast<const uint2*>(wp + (k + j) * kGB);
             sw[j] = *reinterpret_cast<const float2*>(sp + (k + j) * kGB);
-            xv[j] = xl ? *reinterpret_cast<const uint2*>(xp + (k + j) * kXF) : make_uint2(0u, 0u);
-            f[j] = fp[k + j];
+            xv[j] = *reinterpret_cast<const uint2*>(xp + (k + j) * kXF);
+            f[j] = MODE == MODE_W4A8 ? fp[k + j] : 0.0f;
         }
         int d[4][4];
 #pragma unroll
         for (int j = 0; j < 4; j++)
             mma_s8(d[j], lo16(wv[j].x), lo16(wv[j].y), hi16(wv[j].x), hi16(wv[j].y), xv[j].x, xv[j].y);
 #pragma unroll
-        for (int j = 0; j < 4; j++) group_accumulate<MODE>(d[j], sw[j], f[j], lane_factor, acc0, acc1);
+        for (int j = 0; j < 4; j++) group_accumulate<MODE>(d[j], sw[j], f[j], acc0, acc1);
     }
     if (k < ng) {
         // Last 1-3 groups as one step of four; the missing groups read the
@@ -236,28 +161,29 @@ __device__ __forceinline__ void chunk_mma(const unsigned char* chunk, int ng, in
             wv[j] = *reinterpret_cast<const uint2*>(wp + kk * kGB);
             if (k + j >= ng) wv[j] = make_uint2(0x88888888u, 0x88888888u);
             sw[j] = *reinterpret_cast<const float2*>(sp + kk * kGB);
-            xv[j] = xl ? *reinterpret_cast<const uint2*>(xp + kk * kXF) : make_uint2(0u, 0u);
-            f[j] = fp[kk];
+            xv[j] = *reinterpret_cast<const uint2*>(xp + kk * kXF);
+            f[j] = MODE == MODE_W4A8 ? fp[kk] : 0.0f;
         }
         int d[4][4];
 #pragma unroll
         for (int j = 0; j < 4; j++)
             mma_s8(d[j], lo16(wv[j].x), lo16(wv[j].y), hi16(wv[j].x), hi16(wv[j].y), xv[j].x, xv[j].y);
 #pragma unroll
-        for (int j = 0; j < 4; j++) group_accumulate<MODE>(d[j], sw[j], f[j], lane_factor, acc0, acc1);
+        for (int j = 0; j < 4; j++) group_accumulate<MODE>(d[j], sw[j], f[j], acc0, acc1);
     }
 }
 
 // Finishes a tile's lane accumulators: afterwards lane 4r (t = 0) holds rows
-// r (acc0) and r + 8 (acc1).  W4A16 adds the quad's digit partial sums;
-// W4A8 rows are complete in lane t = 0 already.
+// r (acc0) and r + 8 (acc1).  W4A16 joins the quad's low and high digit
+// halves and applies the vector factor; W4A8 rows are complete in lane t = 0
+// already.
 template <int MODE>
-__device__ __forceinline__ void quad_reduce(float& acc0, float& acc1) {
+__device__ __forceinline__ void quad_reduce(float& acc0, float& acc1, float xfactor) {
     if (MODE == MODE_W4A16) {
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+        const float h0 = __shfl_xor_sync(0xffffffffu, acc0, 1);
+        const float h1 = __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc0 = fmaf(h0, 65536.0f, acc0) * xfactor;
+        acc1 = fmaf(h1, 65536.0f, acc1) * xfactor;
     }
 }
 
