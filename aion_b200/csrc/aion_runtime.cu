@@ -81,21 +81,23 @@ static const DevInfo& dev_info(int dev) {
 static int round128(int b) { return (b + 127) & ~127; }
 
 // Dynamic shared memory plan of the streaming kernels: activation digits
-// (G * 96 bytes) and group factors (G * 4), then the per-warp rings of P
-// slots.
+// (G * 128 bytes) and group factors (G * 4), the op table (decode kernel),
+// then the per-warp rings of P slots.
 struct SmemPlan {
-    int xbytes = 0, xs_off = 0, slot_bytes = 0, P = 0, total = 0;
+    int xbytes = 0, xs_off = 0, ring_off = 0, slot_bytes = 0, P = 0, total = 0;
 };
 
-static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int smem_optin, int static_bytes, int min_xbytes = 0) {
+static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int smem_optin, int static_bytes, int min_xbytes = 0,
+                          int ops_bytes = 0) {
     SmemPlan p;
     const int G = max_n / 32;
     p.xs_off = G * kXF;
     p.xbytes = round128(std::max(xbuf_bytes(max_n), min_xbytes));
+    p.ring_off = p.xbytes + round128(ops_bytes);
     p.slot_bytes = round128(max_chunk_bytes);
-    const int avail = smem_optin - static_bytes - 1024 - p.xbytes;
+    const int avail = smem_optin - static_bytes - 1024 - p.ring_off;
     p.P = std::min(8, avail / (kWarps * p.slot_bytes));
-    p.total = p.xbytes + kWarps * std::max(p.P, 0) * p.slot_bytes;
+    p.total = p.ring_off + kWarps * std::max(p.P, 0) * p.slot_bytes;
     return p;
 }
 
@@ -184,7 +186,7 @@ static cudaError_t launch_standalone(const MatDesc& m, const Scratch& sc, const 
     a.error = sc.error;
     a.P = p.P;
     a.slot_bytes = p.slot_bytes;
-    a.xbytes = p.xbytes;
+    a.xbytes = p.ring_off;
     a.xs_off = p.xs_off;
     return launch_ex(k_matvec<MODE>, dim3(di.sms), dim3(kThreads), (size_t)p.total, st, true, false, a);
 }
@@ -329,12 +331,13 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.steps = steps;
     a.P = c->plan.P;
     a.slot_bytes = c->plan.slot_bytes;
-    a.xbytes = c->plan.xbytes;
+    a.xbytes = c->plan.ring_off;
     a.xs_off = c->plan.xs_off;
+    a.ops_off = c->plan.xbytes;
     // The grid-barrier counter starts from zero in every launch.
     cudaError_t e = cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream);
     if (e != cudaSuccess) return e;
-    return launch_ex(k_decode<MODE>, dim3(c->grid), dim3(kThreads), (size_t)c->plan.total, c->stream, false, true, a);
+    return launch_ex(k_decode<MODE>, dim3(c->grid), dim3(kDecodeThreads), (size_t)c->plan.total, c->stream, false, true, a);
 }
 
 static cudaError_t launch_decode(aion_ctx* c, int steps) {
@@ -473,14 +476,15 @@ static aion_status setup_decode_kernel(aion_ctx* c, int max_n, int max_chunk) {
     CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode<MODE>));
     // W4A8 stages the RMSNorm input (dim floats) and the reference-order
     // attention scores (max_pos floats) in the digit area.
-    c->plan = plan_smem(max_n, max_chunk, di.smem_optin, (int)fa.sharedSizeBytes, MODE == MODE_W4A8 ? std::max(c->max_pos, (int)c->dim) * 4 : 0);
+    c->plan = plan_smem(max_n, max_chunk, di.smem_optin, (int)fa.sharedSizeBytes,
+                        MODE == MODE_W4A8 ? std::max(c->max_pos, (int)c->dim) * 4 : 0, (int)(c->nops * sizeof(OpDesc)));
     if (c->plan.P < 2) {
         set_err(&c->err, "shared memory too small for the decode rings (P = %d)", c->plan.P);
         return AION_ERR_SHAPE;
     }
     CK_RET(&c->err, cudaFuncSetAttribute(k_decode<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->plan.total));
     int nb = 0;
-    CK_RET(&c->err, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_decode<MODE>, kThreads, c->plan.total));
+    CK_RET(&c->err, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_decode<MODE>, kDecodeThreads, c->plan.total));
     if (nb < 1) {
         set_err(&c->err, "decode kernel cannot be resident (smem %d)", c->plan.total);
         return AION_ERR_CUDA;

@@ -77,6 +77,13 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only), and the wait for
+// all of this thread's copies.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---------------------------------------------------------------------------
 // mbarrier + bulk copy (global -> shared, completion counted in bytes).
 // ---------------------------------------------------------------------------
@@ -95,6 +102,9 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
@@ -116,6 +126,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
 }
 
 // ---------------------------------------------------------------------------
+// CTA barrier of the compute threads: named barrier 1 over the first
+// kComputeThreads threads, so a kernel may run extra (producer) warps that
+// never join it.
+// ---------------------------------------------------------------------------
+constexpr int kComputeThreads = 352;
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kComputeThreads) : "memory"); }
+__device__ __forceinline__ int csync_or(int pred) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.s32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, %2, p;\n\t"
+        "selp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred), "n"(kComputeThreads)
+        : "memory");
+    return r;
+}
+
+// ---------------------------------------------------------------------------
 // Grid barrier for a kernel whose CTAs are all co-resident (cooperative
 // launch).  The counter only grows within a launch; barrier k (0-based)
 // completes when it reaches (k + 1) * gridDim.x.  Bounded: after `limit`
@@ -129,6 +159,9 @@ __device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
 __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ int32_t ld_relaxed_i32(const int32_t* p) {
     int32_t v;
     asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -141,7 +174,7 @@ __device__ __forceinline__ void set_error(StepState* st, int32_t code) { atomicC
 // when another CTA already recorded an error.
 __device__ __forceinline__ bool grid_barrier(StepState* st, uint32_t& k, uint32_t limit = (1u << 24)) {
     __shared__ int s_ok;
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
         // bar.sync orders the CTA's writes before this release, and the
         // release is cumulative, so no separate fence is needed; likewise
@@ -159,7 +192,7 @@ __device__ __forceinline__ bool grid_barrier(StepState* st, uint32_t& k, uint32_
         if (!ok) set_error(st, DEV_BARRIER_TIMEOUT);
         s_ok = ok;
     }
-    __syncthreads();
+    csync();
     k++;
     return s_ok != 0;
 }
@@ -181,19 +214,19 @@ __device__ __forceinline__ float warp_max(float v) {
 __device__ __forceinline__ float block_sum(float v, float* red) {
     v = warp_sum(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
+    csync();
     if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = (lane < (int)(blockDim.x >> 5)) ? red[lane] : 0.0f;
+    csync();
+    float t = (lane < kComputeThreads / 32) ? red[lane] : 0.0f;
     return warp_sum(t);
 }
 __device__ __forceinline__ float block_max(float v, float* red) {
     v = warp_max(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __syncthreads();
+    csync();
     if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = (lane < (int)(blockDim.x >> 5)) ? red[lane] : -INFINITY;
+    csync();
+    float t = (lane < kComputeThreads / 32) ? red[lane] : -INFINITY;
     return warp_max(t);
 }
 

@@ -51,6 +51,7 @@ struct DecodeArgs {
     int32_t* history;              // [max_pos]
     int steps;
     int P, slot_bytes, xbytes, xs_off;
+    int ops_off;                   // shared-memory copy of ops[] (xbytes = ring offset)
 };
 
 // ---------------------------------------------------------------------------
@@ -90,8 +91,8 @@ __device__ __forceinline__ float4 src_load4(const VecSrc& s, int i) {
 // from the correctly rounded value).
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
 
-constexpr int kMaxVec = 14;       // float4 per thread of an op input: n <= 14 * 4 * kThreads
-constexpr int kMaxNormVec = 5;    // float4 per thread of a normed input: dim <= 5 * 4 * kThreads
+constexpr int kMaxVec = 10;       // float4 per thread of an op input: n <= 10 * 4 * kThreads
+constexpr int kMaxNormVec = 4;    // float4 per thread of a normed input: dim <= 4 * 4 * kThreads
 
 // Packs four signed values (the low bytes) into one word.
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
@@ -126,7 +127,7 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
                 const int j = tid + i * kThreads;
                 if (j < nv) stage[j] = v[i];
             }
-            __syncthreads();
+            csync();
             if (tid < 4) {
                 const float* sx = reinterpret_cast<const float*>(xf);
                 float acc = 0.0f;
@@ -136,10 +137,10 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
                 }
                 red[tid] = acc;
             }
-            __syncthreads();
+            csync();
             const float sum = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
             ss = 1.0f / sqrtf(__fdiv_rn(sum, (float)n) + 1e-5f);
-            __syncthreads();
+            csync();
         } else {
             float acc = 0.0f;
 #pragma unroll
@@ -184,21 +185,22 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
         const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
         if (MODE == MODE_W4A16) {
             if (!valid) continue;
-            int d0[4], d1[4], d2[4], d3[4];
+            // Balanced base-256 digits d0..d2 in [-128, 127] and d3: the bytes
+            // of Z = (X + 0x808080) ^ 0x808080 are d0, d1, d2, d3 as signed
+            // bytes (adding 128 per digit makes every digit a plain byte).
+            // A 4x4 byte transpose then gives each digit column its word.
+            uint32_t Z[4];
 #pragma unroll
             for (int b = 0; b < 4; b++) {
                 const int X = live ? __float2int_rn(__fmul_rn(__fmul_rn(e[b], sa), sb)) : 0;
-                d0[b] = ((X + 128) & 255) - 128;
-                const int r1 = (X - d0[b]) >> 8;
-                d1[b] = ((r1 + 128) & 255) - 128;
-                const int r2 = (r1 - d1[b]) >> 8;
-                d2[b] = ((r2 + 128) & 255) - 128;
-                d3[b] = (r2 - d2[b]) >> 8;
+                Z[b] = ((uint32_t)X + 0x808080u) ^ 0x808080u;
             }
-            *reinterpret_cast<uint32_t*>(dst) = pack4(d0[0], d0[1], d0[2], d0[3]);
-            *reinterpret_cast<uint32_t*>(dst + 32) = pack4(d1[0], d1[1], d1[2], d1[3]);
-            *reinterpret_cast<uint32_t*>(dst + 64) = pack4(d2[0], d2[1], d2[2], d2[3]);
-            *reinterpret_cast<uint32_t*>(dst + 96) = pack4(d3[0], d3[1], d3[2], d3[3]);
+            const uint32_t t0 = __byte_perm(Z[0], Z[1], 0x5140), t1 = __byte_perm(Z[0], Z[1], 0x7362);
+            const uint32_t t2 = __byte_perm(Z[2], Z[3], 0x5140), t3 = __byte_perm(Z[2], Z[3], 0x7362);
+            *reinterpret_cast<uint32_t*>(dst) = __byte_perm(t0, t2, 0x5410);
+            *reinterpret_cast<uint32_t*>(dst + 32) = __byte_perm(t0, t2, 0x7632);
+            *reinterpret_cast<uint32_t*>(dst + 64) = __byte_perm(t1, t3, 0x5410);
+            *reinterpret_cast<uint32_t*>(dst + 96) = __byte_perm(t1, t3, 0x7632);
         } else {
             float m = fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w)));
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
@@ -236,12 +238,13 @@ struct Seq {
     MatDesc m;                     // copy of ops[op].m, kept in registers
 };
 
-__device__ __forceinline__ void seq_enter(Seq& s, const OpDesc* ops, int nops, int steps, int mode, int step, int op) {
+__device__ __forceinline__ void seq_enter(Seq& s, const OpDesc* ops, int nops, int steps, int mode, int step, int op,
+                                          int warp) {
     while (step < steps) {
         while (op < nops) {
             s.m = ops[op].m;
             s.w = op_work(s.m, mode);
-            if (cursor_begin(s.cu, s.w, s.m)) {
+            if (cursor_begin(s.cu, s.w, s.m, warp)) {
                 s.step = step;
                 s.op = op;
                 return;
@@ -260,7 +263,7 @@ __device__ __forceinline__ void seq_issue_next(Seq& s, Ring& r, const OpDesc* op
     int bytes;
     const uint8_t* src = chunk_src(s.m, s.cu.tile, s.cu.c, bytes);
     ring_issue(r, src, bytes);
-    if (!cursor_next(s.cu, s.w, s.m)) seq_enter(s, ops, nops, steps, mode, s.step, s.op + 1);
+    if (!cursor_next(s.cu, s.w, s.m)) seq_enter(s, ops, nops, steps, mode, s.step, s.op + 1, threadIdx.x >> 5);
 }
 
 // ---------------------------------------------------------------------------
@@ -271,10 +274,11 @@ __device__ __forceinline__ void seq_issue_next(Seq& s, Ring& r, const OpDesc* op
 struct OpSmem {
     float part[kMaxLocalTiles * kWarps * kTR];   // split: warp partials per local tile
     float vals[kMaxLocalTiles * kTR];            // split: finished rows per local tile
+    float pre[kMaxLocalTiles * kTR];             // split: epilogue operands fetched ahead
     int state[2];
 };
 
-template <int MODE, class Epi>
+template <int MODE, bool PROD, class Epi>
 __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, Seq& seq, const OpDesc* ops, int nops,
                        int steps, const unsigned char* xf, const float* xs, OpSmem& os, float* split_part,
                        int* split_cnt, Epi& epi) {
@@ -283,11 +287,13 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
     const OpWork w = op_work(m, MODE);
     bool ok = true;
     OpCursor cu;
-    bool more = cursor_begin(cu, w, m);
+    bool more = cursor_begin(cu, w, m, warp);
     if (w.split) {
         const int tf = w.u0 / m.nch, tl = (w.u1 - 1) / m.nch, ntl = tl - tf + 1;
-        for (int i = tid; i < ntl * kWarps * kTR; i += blockDim.x) os.part[i] = 0.0f;
-        __syncthreads();
+        for (int i = tid; i < ntl * kWarps * kTR; i += kThreads) os.part[i] = 0.0f;
+        if (tid == 0) os.state[0] = 0;
+        epi.prefetch(tf * kTR, ntl * kTR, os.pre);
+        csync();
         float a0 = 0.0f, a1 = 0.0f;
         int cur = -1;
         while (more) {
@@ -309,8 +315,12 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
             chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, a0, a1);
             __syncwarp();
-            ring_release(ring);
-            seq_issue_next(seq, ring, ops, nops, steps, MODE);
+            if (PROD) {
+                ring_release(ring, true);
+            } else {
+                ring_release(ring);
+                seq_issue_next(seq, ring, ops, nops, steps, MODE);
+            }
             more = cursor_next(cu, w, m);
         }
         if (ok && cur >= 0) {
@@ -321,52 +331,50 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
                 p[(lane >> 2) + 8] = a1;
             }
         }
-        if (__syncthreads_or(!ok)) return false;
-        for (int i = tid; i < ntl * kTR; i += blockDim.x) {
+        cp_async_wait_all();
+        if (csync_or(!ok)) return false;
+        for (int i = tid; i < ntl * kTR; i += kThreads) {
             const int lt = i / kTR, r = i % kTR;
             float v = 0.0f;
             for (int k = 0; k < kWarps; k++) v += os.part[(lt * kWarps + k) * kTR + r];
             os.vals[i] = v;
         }
-        __syncthreads();
+        csync();
         // Tiles cut by a CTA boundary: local tile 0 when u0 is inside a tile
         // (this CTA has the tile's second part), the last local tile when u1
-        // is (this CTA has the first part).  Each part is published with one
-        // fence; the CTA arriving second adds first + second and finishes
-        // the tile.
+        // is (this CTA has the first part).  The CTA with the second part
+        // publishes it and raises the tile's flag; the CTA with the first
+        // part waits for the flag, adds first + second, lowers the flag and
+        // finishes the tile.  Publishing never waits, so the waits form a
+        // chain towards higher CTAs and always end.
         const bool cut0 = (w.u0 % m.nch) != 0, cut1 = (w.u1 % m.nch) != 0;
-        const int tile0 = tf, tile1 = tl;
-        if (cut0 || cut1) {
-            if (cut0 && tid < kTR) {
-                __stcg(split_part + ((size_t)tile0 * 2 + 1) * kTR + tid, os.vals[tid]);
-                __threadfence();
-            }
-            if (cut1 && tid >= 32 && tid < 32 + kTR) {
-                __stcg(split_part + ((size_t)tile1 * 2 + 0) * kTR + (tid - 32), os.vals[(ntl - 1) * kTR + tid - 32]);
-                __threadfence();
-            }
-            __syncthreads();
-            if (cut0 && tid == 0) os.state[0] = atomicAdd(split_cnt + tile0, 1);
-            if (cut1 && tid == 32) os.state[1] = atomicAdd(split_cnt + tile1, 1);
-            __syncthreads();
-            if (cut0 && os.state[0] == 1 && tid < kTR) {
-                __threadfence();
-                const float first = __ldcg(split_part + ((size_t)tile0 * 2 + 0) * kTR + tid);
-                os.vals[tid] = first + os.vals[tid];
-                if (tid == 0) split_cnt[tile0] = 0;
-            }
-            if (cut1 && os.state[1] == 1 && tid >= 32 && tid < 32 + kTR) {
-                __threadfence();
-                const float second = __ldcg(split_part + ((size_t)tile1 * 2 + 1) * kTR + tid - 32);
-                os.vals[(ntl - 1) * kTR + tid - 32] = os.vals[(ntl - 1) * kTR + tid - 32] + second;
-                if (tid == 32) split_cnt[tile1] = 0;
-            }
-            __syncthreads();
+        if (cut0 && tid < kTR) {
+            __stcg(split_part + (size_t)tf * kTR + tid, os.vals[tid]);
+            __syncwarp(0xFFFFu);
+            if (tid == 0) st_release_u32(reinterpret_cast<uint32_t*>(split_cnt) + tf, 1u);
         }
-        const bool skip0 = cut0 && os.state[0] != 1, skip1 = cut1 && os.state[1] != 1;
-        for (int i = tid; i < ntl * (kTR / kRB); i += blockDim.x) {
+        if (cut1 && tid >= 32 && tid < 32 + kTR) {
+            int ok1 = 1;
+            if (tid == 32) {
+                uint32_t i = 0;
+                while (ld_acquire_u32(reinterpret_cast<const uint32_t*>(split_cnt) + tl) == 0u)
+                    if (++i > (1u << 24)) { ok1 = 0; break; }
+            }
+            ok1 = __shfl_sync(0xFFFFu, ok1, 0);
+            __syncwarp(0xFFFFu);
+            if (ok1) {
+                const float second = __ldcg(split_part + (size_t)tl * kTR + tid - 32);
+                os.vals[(ntl - 1) * kTR + tid - 32] = os.vals[(ntl - 1) * kTR + tid - 32] + second;
+                if (tid == 32) split_cnt[tl] = 0;
+            } else if (tid == 32) {
+                os.state[0] = 1;
+            }
+        }
+        if (cut1 && csync_or(os.state[0] != 0)) return false;
+        const bool skip0 = cut0;
+        for (int i = tid; i < ntl * (kTR / kRB); i += kThreads) {
             const int lt = i / (kTR / kRB), q = i % (kTR / kRB);
-            if ((lt == 0 && skip0) || (lt == ntl - 1 && skip1)) continue;
+            if (lt == 0 && skip0) continue;
             epi((tf + lt) * kTR + q * kRB, os.vals + lt * kTR + q * kRB);
         }
     } else {
@@ -379,8 +387,12 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
             chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, a0, a1);
             __syncwarp();
-            ring_release(ring);
-            seq_issue_next(seq, ring, ops, nops, steps, MODE);
+            if (PROD) {
+                ring_release(ring, true);
+            } else {
+                ring_release(ring);
+                seq_issue_next(seq, ring, ops, nops, steps, MODE);
+            }
             if (c == m.nch - 1) {
                 quad_reduce<MODE>(a0, a1, xfac);
                 if ((lane & 3) == 0) {
@@ -394,7 +406,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             }
             more = cursor_next(cu, w, m);
         }
-        if (__syncthreads_or(!ok)) return false;
+        if (csync_or(!ok)) return false;
     }
     return true;
 }
@@ -406,8 +418,21 @@ struct DecodeEpi {
     const DecodeArgs* a;
     const OpDesc* op;
     int pos;
+    const float* freq;             // shared: this position's RoPE cos[hs/2], sin[hs/2]
     float best;
     uint32_t best_i;
+    const float* pre = nullptr;    // shared: residual rows [pre_row0, ...) fetched ahead
+    int pre_row0 = 0;
+
+    // Split mode: rows [row0, row0 + rows) end on this CTA; WO / W2 fetch
+    // their residual rows into shared memory while the op streams.
+    __device__ __forceinline__ void prefetch(int row0, int rows, float* dst) {
+        if (op->kind != OP_WO && op->kind != OP_W2) return;
+        const int tid = threadIdx.x;
+        if (4 * tid < rows) cp_async16(dst + 4 * tid, a->x + row0 + 4 * tid);
+        pre = dst;
+        pre_row0 = row0;
+    }
 
     __device__ __forceinline__ void operator()(int r0, const float* v) {
         const DecodeArgs& A = *a;
@@ -424,8 +449,8 @@ struct DecodeEpi {
                 float out[kRB];
                 for (int r = 0; r < kRB; r += 2) {
                     const int hd = (base + r) % hs;
-                    const float fr = __ldg(A.freq_re + pos * (hs / 2) + hd / 2);
-                    const float fi = __ldg(A.freq_im + pos * (hs / 2) + hd / 2);
+                    const float fr = freq[hd / 2];
+                    const float fi = freq[hs / 2 + hd / 2];
                     out[r] = __fsub_rn(__fmul_rn(v[r], fr), __fmul_rn(v[r + 1], fi));
                     out[r + 1] = __fadd_rn(__fmul_rn(v[r], fi), __fmul_rn(v[r + 1], fr));
                 }
@@ -441,7 +466,10 @@ struct DecodeEpi {
         case OP_WO:
         case OP_W2:
             for (int r = 0; r < kRB; r++)
-                if (r0 + r < d) __stcg(A.x + r0 + r, __ldcg(A.x + r0 + r) + v[r]);
+                if (r0 + r < d) {
+                    const float xr = pre ? pre[r0 + r - pre_row0] : __ldcg(A.x + r0 + r);
+                    __stcg(A.x + r0 + r, xr + v[r]);
+                }
             break;
         case OP_W13: {
             // rows w1[2j], w1[2j+1], w3[2j], w3[2j+1]; swiglu (src/kernel_simd.c:836-841)
@@ -629,10 +657,10 @@ __device__ void attention_layer_exact(const DecodeArgs& a, int layer, int pos, f
     __shared__ float s_sum;
     for (int h = blockIdx.x; h < a.n_heads; h += gridDim.x) {
         const int kvh = h / a.kv_mul;
-        for (int i = tid; i < hs; i += blockDim.x) s_q[i] = __ldcg(a.q + h * hs + i);
-        __syncthreads();
+        for (int i = tid; i < hs; i += kThreads) s_q[i] = __ldcg(a.q + h * hs + i);
+        csync();
         float m = -INFINITY;
-        for (int t = tid; t <= pos; t += blockDim.x) {
+        for (int t = tid; t <= pos; t += kThreads) {
             const float* kr = kc + (size_t)t * a.kv_dim + kvh * hs;
             float d = 0.0f;
             for (int j = 0; j < hs; j++) d = __fadd_rn(d, __fmul_rn(s_q[j], __ldcg(kr + j)));
@@ -641,24 +669,24 @@ __device__ void attention_layer_exact(const DecodeArgs& a, int layer, int pos, f
             m = fmaxf(m, d);
         }
         m = block_max(m, red);
-        for (int t = tid; t <= pos; t += blockDim.x) sc[t] = expf_cr(__fsub_rn(sc[t], m));
-        __syncthreads();
+        for (int t = tid; t <= pos; t += kThreads) sc[t] = expf_cr(__fsub_rn(sc[t], m));
+        csync();
         if (tid == 0) {
             float sum = 0.0f;
             for (int t = 0; t <= pos; t++) sum = __fadd_rn(sum, sc[t]);
             s_sum = sum;
         }
-        __syncthreads();
+        csync();
         const float scale = __fdiv_rn(1.0f, s_sum);
-        for (int t = tid; t <= pos; t += blockDim.x) sc[t] = __fmul_rn(sc[t], scale);
-        __syncthreads();
-        for (int j = tid; j < hs; j += blockDim.x) {
+        for (int t = tid; t <= pos; t += kThreads) sc[t] = __fmul_rn(sc[t], scale);
+        csync();
+        for (int j = tid; j < hs; j += kThreads) {
             float o = 0.0f;
             for (int t = 0; t <= pos; t++)
                 o = __fadd_rn(o, __fmul_rn(sc[t], __ldcg(vc + (size_t)t * a.kv_dim + kvh * hs + j)));
             __stcg(a.att + h * hs + j, o);
         }
-        __syncthreads();
+        csync();
     }
 }
 
@@ -680,42 +708,75 @@ __device__ __forceinline__ void cta_argmax(unsigned long long* dst, float best, 
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) red64[warp] = k;
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) {
         unsigned long long m = 0;
-        for (int i = 0; i < (int)(blockDim.x >> 5); i++) m = red64[i] > m ? red64[i] : m;
+        for (int i = 0; i < kWarps; i++) m = red64[i] > m ? red64[i] : m;
         if (m) atomicMax(dst, m);
     }
-    __syncthreads();
+    csync();
 }
 
 // ---------------------------------------------------------------------------
 // The persistent decode kernel.
 // ---------------------------------------------------------------------------
+// Warps 0..kWarps-1 compute; warp kWarps is the producer: its lane w walks compute warp
+// w's chunk sequence and issues each chunk's bulk copy as soon as the slot
+// it goes to is free, so the compute warps only wait, compute and release.
+constexpr int kDecodeThreads = kThreads + 32;
+
+// Producer lane `w` (bounded: gives up when a slot stays busy for 2^24 polls
+// or a compute warp has recorded an error), then waits for its copies.
+__device__ __forceinline__ void produce(const DecodeArgs& a, const OpDesc* ops, unsigned char* ring_base,
+                                       uint64_t* bars, int w, int mode) {
+    ProdRing pr;
+    ring_init(pr.r, ring_base, bars, a.P, a.slot_bytes, w, false);
+    pr.round = 0;
+    Seq seq;
+    seq_enter(seq, ops, a.nops, a.steps, mode, 0, 0, w);
+    uint32_t spins = 0;
+    while (seq.step < a.steps) {
+        int bytes;
+        const uint8_t* src = chunk_src(seq.m, seq.cu.tile, seq.cu.c, bytes);
+        if (prod_try_issue(pr, src, bytes)) {
+            spins = 0;
+            if (!cursor_next(seq.cu, seq.w, seq.m)) seq_enter(seq, ops, a.nops, a.steps, mode, seq.step, seq.op + 1, w);
+        } else if (++spins > (1u << 24) || ((spins & 4095u) == 0 && ld_relaxed_i32(&a.step->error) != 0)) {
+            break;
+        }
+    }
+    prod_drain(pr);
+}
+
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
+__global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t bars[kWarps * 8];
+    __shared__ __align__(8) uint64_t bars[kWarps * 2 * 8];
     __shared__ float red[32];
     __shared__ unsigned long long red64[kWarps];
-    __shared__ OpSmem os;
+    __shared__ __align__(16) OpSmem os;
     __shared__ int s_tok, s_pos, s_bad;
-    __shared__ __align__(16) OpDesc s_ops[2];   // current op, and the next one being fetched
+    __shared__ float s_freq[kMaxHead];          // RoPE cos / sin of this step's position
     unsigned char* xf = smem;
     float* xs = reinterpret_cast<float*>(smem + a.xs_off);
     unsigned char* ring_base = smem + a.xbytes;
 
+    // The op table lives in shared memory for the whole launch.
+    OpDesc* ops = reinterpret_cast<OpDesc*>(smem + a.ops_off);
+    static_assert(sizeof(OpDesc) % 4 == 0, "OpDesc copy");
+    for (int i = threadIdx.x; i < a.nops * (int)(sizeof(OpDesc) / 4); i += kDecodeThreads)
+        reinterpret_cast<int*>(ops)[i] = __ldg(reinterpret_cast<const int*>(a.ops) + i);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     Ring ring;
-    ring_init(ring, ring_base, bars, a.P, a.slot_bytes);
-    Seq seq;
-    seq_enter(seq, a.ops, a.nops, a.steps, MODE, 0, 0);
-    for (int i = 0; i < a.P; i++) seq_issue_next(seq, ring, a.ops, a.nops, a.steps, MODE);
+    if (warp < kWarps) ring_init(ring, ring_base, bars, a.P, a.slot_bytes, warp, lane == 0);
+    fence_mbar_init();
+    __syncthreads();   // all kDecodeThreads: the op table and the barriers are ready
+    if (warp == kWarps) {
+        if (lane < kWarps) produce(a, ops, ring_base, bars, lane, MODE);
+        return;
+    }
+    Seq seq;   // unused: the producer warp issues every chunk
 
-    constexpr int kOpWords = sizeof(OpDesc) / 4;
-    static_assert(sizeof(OpDesc) % 4 == 0 && kOpWords <= kThreads, "OpDesc copy");
-    if (threadIdx.x < kOpWords)
-        reinterpret_cast<int*>(&s_ops[0])[threadIdx.x] = __ldg(reinterpret_cast<const int*>(a.ops) + threadIdx.x);
-    int oslot = 0;
     uint32_t nbar = 0;
     bool ok = true;
     for (int step = 0; step < a.steps && ok; step++) {
@@ -729,22 +790,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
             s_tok = tok;
             s_pos = pos;
         }
-        __syncthreads();
+        csync();
         if (s_bad) {
             if (blockIdx.x == 0 && threadIdx.x == 0) set_error(a.step, DEV_BAD_INPUT);
             break;
         }
         const int pos = s_pos, tok = s_tok;
+        {
+            const int h2 = a.head_size / 2;
+            if (threadIdx.x < 2 * h2)
+                s_freq[threadIdx.x] = threadIdx.x < h2 ? __ldg(a.freq_re + (size_t)pos * h2 + threadIdx.x)
+                                                       : __ldg(a.freq_im + (size_t)pos * h2 + threadIdx.x - h2);
+        }
         VecSrc emb_src;
         emb_src.p = nullptr;
         emb_src.emb = a.emb;
         emb_src.tok = tok;
         if (blockIdx.x == 0)   // x = embedding row, for the residual stream
-            for (int i = threadIdx.x; i < a.dim / 4; i += blockDim.x)
+            for (int i = threadIdx.x; i < a.dim / 4; i += kThreads)
                 __stcg(reinterpret_cast<float4*>(a.x) + i, src_load4(emb_src, i));
 
-        for (int oi = 0; oi < a.nops && ok; oi++, oslot ^= 1) {
-            const OpDesc op = s_ops[oslot];
+        for (int oi = 0; oi < a.nops && ok; oi++) {
+            const OpDesc op = ops[oi];
             VecSrc src;
             src.emb = a.emb;
             src.tok = tok;
@@ -763,14 +830,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
                 src.p = op.kind == OP_WO ? a.att : a.hb;
             }
             build_input<MODE>(xf, xs, src, op.m.n, nw, red);
-            __syncthreads();
-            if (threadIdx.x < kOpWords) {   // next op (op 0 of the next step after the classifier)
-                const int nx = oi + 1 < a.nops ? oi + 1 : 0;
-                reinterpret_cast<int*>(&s_ops[oslot ^ 1])[threadIdx.x] =
-                    __ldg(reinterpret_cast<const int*>(a.ops + nx) + threadIdx.x);
-            }
-            DecodeEpi epi{&a, &op, pos, -1e9f, 0u};
-            if (!run_op<MODE>(op.m, ring, ring_base, seq, a.ops, a.nops, a.steps, xf, xs, os, a.split_part, a.split_cnt,
+            csync();
+            DecodeEpi epi{&a, &op, pos, s_freq, -1e9f, 0u};
+            if (!run_op<MODE, true>(op.m, ring, ring_base, seq, ops, a.nops, a.steps, xf, xs, os, a.split_part, a.split_cnt,
                               epi)) {
                 set_error(a.step, DEV_COPY_TIMEOUT);
                 ok = false;
@@ -799,7 +861,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(DecodeArgs a) {
             }
         }
     }
-    ring_drain(ring);
 }
 
 // ---------------------------------------------------------------------------
@@ -819,6 +880,7 @@ struct StandaloneArgs {
 struct StoreEpi {
     float* y;
     int d;
+    __device__ __forceinline__ void prefetch(int, int, float*) {}
     __device__ __forceinline__ void operator()(int r0, const float* v) {
         for (int r = 0; r < kRB; r++)
             if (r0 + r < d) y[r0 + r] = v[r];
@@ -828,18 +890,19 @@ struct StoreEpi {
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) k_matvec(StandaloneArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t bars[kWarps * 8];
-    __shared__ OpSmem os;
+    __shared__ __align__(8) uint64_t bars[kWarps * 2 * 8];
+    __shared__ __align__(16) OpSmem os;
     __shared__ OpDesc s_op;
     unsigned char* xf = smem;
     float* xs = reinterpret_cast<float*>(smem + a.xs_off);
     unsigned char* ring_base = smem + a.xbytes;
     if (threadIdx.x == 0) s_op = a.op;
-    __syncthreads();
     Ring ring;
-    ring_init(ring, ring_base, bars, a.P, a.slot_bytes);
+    ring_init(ring, ring_base, bars, a.P, a.slot_bytes, threadIdx.x >> 5, (threadIdx.x & 31) == 0);
+    fence_mbar_init();
+    csync();
     Seq seq;
-    seq_enter(seq, &s_op, 1, 1, MODE, 0, 0);
+    seq_enter(seq, &s_op, 1, 1, MODE, 0, 0, threadIdx.x >> 5);
     for (int i = 0; i < a.P; i++) seq_issue_next(seq, ring, &s_op, 1, 1, MODE);
     pdl_launch_dependents();
     pdl_wait();
@@ -849,9 +912,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_matvec(StandaloneArgs a) {
     src.emb = a.op.m;
     __shared__ float red[32];
     build_input<MODE>(xf, xs, src, s_op.m.n, nullptr, red);
-    __syncthreads();
+    csync();
     StoreEpi epi{a.y, a.op.m.d};
-    if (!run_op<MODE>(s_op.m, ring, ring_base, seq, &s_op, 1, 1, xf, xs, os, a.split_part, a.split_cnt, epi))
+    if (!run_op<MODE, false>(s_op.m, ring, ring_base, seq, &s_op, 1, 1, xf, xs, os, a.split_part, a.split_cnt, epi))
         if (threadIdx.x == 0) atomicCAS(a.error, 0, DEV_COPY_TIMEOUT);
     ring_drain(ring);
 }

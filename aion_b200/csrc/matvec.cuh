@@ -35,8 +35,9 @@ namespace aion {
 constexpr int kTR = 16;              // rows per tile (MMA M)
 constexpr int kRB = 4;               // rows per epilogue quad
 constexpr int kGB = 320;             // bytes per (tile, group)
-constexpr int kWarps = 8;            // warps per CTA
+constexpr int kWarps = 11;           // compute warps per CTA
 constexpr int kThreads = kWarps * 32;
+static_assert(kThreads == kComputeThreads, "compute threads");
 constexpr int kTargetChunk = 6400;   // bytes per bulk copy, about
 constexpr int kXF = 128;             // bytes of activation digits per group (4 columns)
 constexpr int kMaxLocalTiles = 24;   // tiles of one op per CTA (split mode)
@@ -188,35 +189,42 @@ __device__ __forceinline__ void quad_reduce(float& acc0, float& acc1, float xfac
 }
 
 // ---------------------------------------------------------------------------
-// Per-warp bulk-copy ring.  Each warp streams its own chunk sequence through
-// P slots: lane 0 issues one bulk copy per slot (mbarrier expect_tx), the
-// warp waits on the slot's mbarrier, computes, and lane 0 refills the slot
-// with the chunk P positions further on.  No cross-warp coordination.
+// Per-warp bulk-copy ring of P slots.  Slot s has a "full" mbarrier (armed
+// with the chunk's byte count, completed by the bulk copy) and an "empty"
+// mbarrier (one arrival when the consuming warp is done with the slot).
+// The chunks are issued either by the consuming warp's lane 0 right after it
+// frees a slot (ring_issue), or by a producer lane that waits for the slot's
+// empty barrier (ProdRing).
 // ---------------------------------------------------------------------------
 struct Ring {
     uint32_t slots;      // shared address of this warp's slot 0
-    uint32_t bars;       // shared address of this warp's mbarrier 0
+    uint32_t bars;       // shared address of this warp's full mbarrier 0
+    uint32_t ebars;      // shared address of this warp's empty mbarrier 0
     int P, slot_bytes;
     uint32_t issued, consumed;
     int islot, cslot;    // issued % P, consumed % P
     uint32_t cphase;     // (consumed / P) & 1
 };
 
-__device__ __forceinline__ void ring_init(Ring& r, unsigned char* ring_base, uint64_t* bar_base, int P, int slot_bytes) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Ring of warp `warp`; its lane 0 initialises the barriers when init is set.
+__device__ __forceinline__ void ring_init(Ring& r, unsigned char* ring_base, uint64_t* bar_base, int P, int slot_bytes,
+                                          int warp, bool init) {
     r.P = P;
     r.slot_bytes = slot_bytes;
     r.slots = smem_addr(ring_base + (size_t)warp * P * slot_bytes);
-    r.bars = smem_addr(bar_base + warp * P);
+    r.bars = smem_addr(bar_base + warp * 2 * P);
+    r.ebars = r.bars + 8 * P;
     r.issued = r.consumed = 0;
     r.islot = r.cslot = 0;
     r.cphase = 0;
-    if (lane == 0)
-        for (int i = 0; i < P; i++) mbar_init(r.bars + 8 * i, 1);
-    fence_mbar_init();
-    __syncwarp();
+    if (init)
+        for (int i = 0; i < P; i++) {
+            mbar_init(r.bars + 8 * i, 1);
+            mbar_init(r.ebars + 8 * i, 1);
+        }
 }
 
+// Consumer-issued chunk (lane 0 of the consuming warp).
 __device__ __forceinline__ void ring_issue(Ring& r, const uint8_t* src, int bytes) {
     const int slot = r.islot;
     if ((threadIdx.x & 31) == 0) {
@@ -235,7 +243,13 @@ __device__ __forceinline__ const unsigned char* ring_wait(Ring& r, unsigned char
     const int warp = threadIdx.x >> 5;
     return ring_base + ((size_t)warp * r.P + r.cslot) * r.slot_bytes;
 }
-__device__ __forceinline__ void ring_release(Ring& r) {
+// Frees the oldest slot; with a producer, tells it so through the slot's
+// empty barrier (after every lane of the warp is done reading).
+__device__ __forceinline__ void ring_release(Ring& r, bool producer = false) {
+    if (producer) {
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive(r.ebars + 8 * r.cslot);
+    }
     r.consumed++;
     if (++r.cslot == r.P) {
         r.cslot = 0;
@@ -248,6 +262,38 @@ __device__ __forceinline__ void ring_drain(Ring& r) {
     while (r.consumed < r.issued) {
         mbar_wait(r.bars + 8 * r.cslot, r.cphase, 1u << 20);
         ring_release(r);
+    }
+}
+
+// Producer side of one warp's ring, run by a single producer lane: issue k
+// goes to slot k % P after the consumer has released issue k - P there.
+struct ProdRing {
+    Ring r;
+    uint32_t round;      // issued / P
+};
+
+// Non-blocking: issues the chunk if its slot is free; false otherwise.
+__device__ __forceinline__ bool prod_try_issue(ProdRing& p, const uint8_t* src, int bytes) {
+    const int slot = p.r.islot;
+    if (p.round > 0 && !mbar_try_wait(p.r.ebars + 8 * slot, (p.round - 1) & 1)) return false;
+    const uint32_t bar = p.r.bars + 8 * slot;
+    mbar_arrive_expect_tx(bar, (uint32_t)bytes);
+    bulk_g2s(p.r.slots + slot * p.r.slot_bytes, src, (uint32_t)bytes, bar);
+    p.r.issued++;
+    if (++p.r.islot == p.r.P) {
+        p.r.islot = 0;
+        p.round++;
+    }
+    return true;
+}
+
+// Waits (bounded) until every chunk this producer issued has landed.
+__device__ __forceinline__ void prod_drain(ProdRing& p) {
+    const uint32_t n = p.r.issued < (uint32_t)p.r.P ? p.r.issued : (uint32_t)p.r.P;
+    for (uint32_t i = 0; i < n; i++) {
+        // the last issue into slot s was number issued - 1 - i
+        const uint32_t k = p.r.issued - 1 - i;
+        mbar_wait(p.r.bars + 8 * (k % p.r.P), (k / p.r.P) & 1, 1u << 20);
     }
 }
 
@@ -269,11 +315,17 @@ struct OpWork {
 
 __device__ __forceinline__ OpWork op_work(const MatDesc& m, int mode) {
     OpWork w;
-    const long long G = gridDim.x, c = blockIdx.x;
-    w.split = (mode == MODE_W4A16 && m.ntiles >= (int)G && m.ntiles <= (kMaxLocalTiles - 2) * (int)G) ? 1 : 0;
+    const int G = gridDim.x, c = blockIdx.x;
+    w.split = (mode == MODE_W4A16 && m.ntiles >= G && m.ntiles <= (kMaxLocalTiles - 2) * G) ? 1 : 0;
     const long long U = w.split ? (long long)m.ntiles * m.nch : m.ntiles;
-    w.u0 = (int)((c * U) / G);
-    w.u1 = (int)(((c + 1) * U) / G);
+    if (U * G < (1LL << 31)) {   // 32-bit division when the products fit
+        const uint32_t u = (uint32_t)U;
+        w.u0 = (int)(((uint32_t)c * u) / (uint32_t)G);
+        w.u1 = (int)(((uint32_t)(c + 1) * u) / (uint32_t)G);
+    } else {
+        w.u0 = (int)(((long long)c * U) / G);
+        w.u1 = (int)(((long long)(c + 1) * U) / G);
+    }
     return w;
 }
 
@@ -283,8 +335,8 @@ struct OpCursor {
     int a, tile, c;
 };
 
-__device__ __forceinline__ bool cursor_begin(OpCursor& cu, const OpWork& w, const MatDesc& m) {
-    cu.a = w.u0 + (int)(threadIdx.x >> 5);
+__device__ __forceinline__ bool cursor_begin(OpCursor& cu, const OpWork& w, const MatDesc& m, int warp) {
+    cu.a = w.u0 + warp;
     if (w.split) {
         cu.tile = cu.a / m.nch;
         cu.c = cu.a - cu.tile * m.nch;
