@@ -21,6 +21,9 @@ N > 1: independent replicas, one per GPU (the 7B path does not shard;
 built from the reference's src/kernel_simd.c; scalar int4 kernel, host
 thread pool) on the same workload, bounded to a few minutes.
 --matvec times the isolated matvec shapes only (for profiling).
+--profile-layers L runs the same path on a 7B-shape checkpoint truncated to
+L layers (same seed and shapes; for ncu captures that must stay small, never
+for the reported metric).
 """
 from __future__ import annotations
 
@@ -44,8 +47,20 @@ SEED_7B = 1
 BOS = 1
 WORKLOAD_TOKENS = 512
 WEIGHT_BYTES_PER_TOKEN = 4_129_423_360          # 0.625 B x 6,607,077,376 weights
+
+
+def weight_bytes_per_token(layers: int) -> int:
+    """int4 weight bytes one token streams (0.625 B per weight: nibble +
+    1/32 fp32 scale): per layer wq, wk, wv, wo, w1, w2, w3; plus the
+    classifier (the tied embedding)."""
+    dim, hid, vocab = CFG_7B[0], CFG_7B[1], CFG_7B[5]
+    return int(0.625 * (layers * (4 * dim * dim + 3 * dim * hid) + vocab * dim))
 MATVEC_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes per token of the decode kernel's weight stream, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum of an 8-step 7B
+# launch, minus its K/V reads; profiles/k_decode_7b_dram.md).
+DRAM_WEIGHT_BYTES_PER_TOKEN = 4.1296e9
 
 
 def matvec_bytes(d: int, n: int) -> int:
@@ -69,14 +84,17 @@ def ckpt_dir() -> Path:
     return d
 
 
-def ensure_7b(rank: int) -> Path:
-    """Writes the seeded 7B int4 checkpoint once per host (rank 0)."""
+def ensure_7b(rank: int, layers: int = 0) -> Path:
+    """Writes the seeded 7B int4 checkpoint once per host (rank 0); with
+    layers > 0, the same shapes truncated to that many layers."""
     import aion_b200 as A
-    path = ckpt_dir() / "llama2_7b_seed1.int4"
+    cfg = CFG_7B if layers <= 0 else (CFG_7B[0], CFG_7B[1], layers) + CFG_7B[3:]
+    name = "llama2_7b_seed1.int4" if layers <= 0 else f"llama2_7b_shape_{layers}l_seed1.int4"
+    path = ckpt_dir() / name
     done = path.with_suffix(".done")
     if rank == 0 and not done.exists():
         tmp = path.with_suffix(".tmp")
-        A.synth_checkpoint(tmp, CFG_7B, SEED_7B, int4=True)
+        A.synth_checkpoint(tmp, cfg, SEED_7B, int4=True)
         tmp.rename(path)
         done.write_text("ok")
     while not done.exists():
@@ -229,6 +247,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the isolated matvec shapes")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
+    ap.add_argument("--profile-layers", type=int, default=0,
+                    help="profiling only: 7B shapes truncated to this many layers")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -267,7 +287,7 @@ def main() -> None:
             print(json.dumps({"metric": "int4 matvec HBM GB/s (isolated 7B shapes)", "matvec": res}), flush=True)
         return
 
-    path = ensure_7b(rank)
+    path = ensure_7b(rank, args.profile_layers)
     model = A.Model(path, device=local)
     L = model.config.n_layers
     stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{local}")
@@ -313,7 +333,7 @@ def main() -> None:
     # Parity sanity: the stream against the reference's 7B stream, where recorded.
     parity = None
     gold = ROOT / "tests" / "golden" / "7b.json"
-    if gold.exists():
+    if gold.exists() and args.profile_layers <= 0:
         want = json.loads(gold.read_text())["w4a16_tokens"]
         k = min(len(want), len(stream_tokens))
         parity = {"tokens_compared": k, "identical": stream_tokens[:k] == want[:k]}
@@ -329,13 +349,17 @@ def main() -> None:
             pos = 0
         kv_bytes += 2 * L * dim * 4 * (pos + 1)
         pos += 1
-    weights_gbs = WEIGHT_BYTES_PER_TOKEN * args.steps / (ms_local * 1e-3) / 1e9
+    wbytes = weight_bytes_per_token(L)
+    weights_gbs = wbytes * args.steps / (ms_local * 1e-3) / 1e9
     peak, peak_kind = hbm_peak()
+    traffic = (DRAM_WEIGHT_BYTES_PER_TOKEN * args.steps + kv_bytes
+               if args.profile_layers <= 0 else None)
     roofline = {"kernel": "k_decode<W4A16> (persistent decode, all steps)", "bound": "hbm",
                 "achieved": weights_gbs, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                "frac": weights_gbs / peak, "traffic": None,
-                "bytes_per_token": WEIGHT_BYTES_PER_TOKEN,
-                "with_kv_GBps": (WEIGHT_BYTES_PER_TOKEN * args.steps + kv_bytes) / (ms_local * 1e-3) / 1e9}
+                "frac": weights_gbs / peak, "traffic": traffic, "traffic_unit": "bytes per launch",
+                "algorithmic_bytes": wbytes * args.steps,
+                "bytes_per_token": wbytes,
+                "with_kv_GBps": (wbytes * args.steps + kv_bytes) / (ms_local * 1e-3) / 1e9}
     matvec = isolated_matvecs(local, reps=5) if (rank == 0 and not args.no_matvec) else None
 
     # End-to-end: the reference-facing call transformer(token, pos) per token
@@ -358,7 +382,7 @@ def main() -> None:
     barrier()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and args.profile_layers <= 0:
         cb = cpu_reference_decode(path, 2, 1000, budget_s=20.0)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
@@ -367,7 +391,8 @@ def main() -> None:
             "metric": "Llama-2-7B int4 decode tok/s (batch 1)",
             "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int4 weights (W4A16), fp32 activations/accumulate", "data": "synthetic",
+            "dtype": "s4 weights x s8 activation digits (int32 tensor-core dot), fp32 accumulate",
+            "data": "synthetic",
             "config": {"workload": "llama2-7b-shape W4A16 greedy decode, batch 1, 512-token workload",
                        "dim": dim, "hidden": hid, "layers": L, "heads": 32, "vocab": vocab, "seed": SEED_7B,
                        "parallelism": f"replicas x{world}", "l2": "weights 4.13 GB/token > L2 (no flush needed)"},
