@@ -17,7 +17,10 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <cmath>
+#include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/aion.h"
@@ -199,6 +202,9 @@ struct aion_ctx {
     aion_opts opts;
     aion_config cfg;
     int dev = 0, mode = 0;
+    uint32_t* exp_tab = nullptr;   // W4A8: inputs where the host expf is not correctly rounded
+    int exp_n = 0;
+    double exp_delta = 0.0;
     long long dim = 0, hidden = 0, L = 0, nh = 0, nkv = 0, vocab = 0, seq = 0, hs = 0, kv_dim = 0, kv_mul = 0;
     int max_pos = 0;
     cudaStream_t stream = nullptr;
@@ -250,6 +256,93 @@ extern "C" AION_API const char* aion_last_error(const aion_ctx* ctx) {
     return g_thread_err.c_str();
 }
 
+// ---------------------------------------------------------------------------
+// The host C library's expf, tabulated.  The reference's softmax and SwiGLU
+// call expf; its results are correctly rounded except on a small set of
+// inputs.  Calling it on every float x with a finite non-zero result and
+// comparing with the correctly rounded e^x finds that set once per process
+// (about 2^31 calls, spread over the host's cores).  The device keeps the
+// sorted list and the largest distance of e^x from a rounding midpoint over
+// the listed inputs (see expf_host).  If the library ever returned a value
+// other than one of the two floats around e^x, the table could not express
+// it and is not used.
+// ---------------------------------------------------------------------------
+struct HostExpTable {
+    std::vector<uint32_t> x;
+    double delta = 0.0;
+    bool usable = false;
+};
+
+// Correctly rounded e^x: the double exponential rounded to float, or, when
+// that lands within 1e-6 result ulp of a midpoint, the long double one.
+static float cr_expf_host(float x) {
+    const double d = std::exp((double)x);
+    const float f = (float)d;
+    if (!std::isfinite(f)) return f;
+    const float o = (double)f < d ? std::nextafterf(f, INFINITY) : std::nextafterf(f, 0.0f);
+    const double mid = 0.5 * ((double)f + (double)o), ulp = std::fabs((double)o - (double)f);
+    if (ulp > 0.0 && std::fabs(d - mid) > 1e-6 * ulp) return f;
+    return (float)expl((long double)x);
+}
+
+static const HostExpTable& host_exp_table() {
+    static HostExpTable t;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        // x in [0, 88.75) and (-104, -0]: every float whose e^x is a finite,
+        // non-zero float lies in these bit ranges.
+        const uint64_t ranges[2][2] = {{0x00000000u, 0x42B20000u}, {0x80000000u, 0xC2D00000u}};
+        const int nt = std::max(1u, std::thread::hardware_concurrency());
+        std::vector<std::vector<uint32_t>> found(nt);
+        std::vector<double> dmax(nt, 0.0);
+        std::vector<int> bad(nt, 0);
+        std::vector<std::thread> th;
+        for (int k = 0; k < nt; k++)
+            th.emplace_back([&, k] {
+                for (const auto& r : ranges) {
+                    const uint64_t len = r[1] - r[0], b0 = r[0] + len * k / nt, b1 = r[0] + len * (k + 1) / nt;
+                    for (uint64_t b = b0; b < b1; b++) {
+                        float x;
+                        const uint32_t u = (uint32_t)b;
+                        memcpy(&x, &u, 4);
+                        const float g = expf(x);
+                        const double d = std::exp((double)x);
+                        const float f = (float)d;
+                        if (g == f) {
+                            // f may still be off when d sits on a midpoint;
+                            // then the long double value decides.
+                            const float o = (double)f < d ? std::nextafterf(f, INFINITY) : std::nextafterf(f, 0.0f);
+                            const double ulp = std::fabs((double)o - (double)f);
+                            if (!(ulp > 0.0) || std::fabs(d - 0.5 * ((double)f + (double)o)) > 1e-6 * ulp) continue;
+                        }
+                        const float c = cr_expf_host(x);
+                        if (g == c) continue;
+                        if (std::nextafterf(c, g) != g) {
+                            bad[k]++;
+                            continue;
+                        }
+                        const long double e = expl((long double)x);
+                        const long double mid = 0.5L * ((long double)c + (long double)g);
+                        const long double ulp = fabsl((long double)g - (long double)c);
+                        dmax[k] = std::max(dmax[k], (double)(fabsl(e - mid) / ulp));
+                        found[k].push_back(u);
+                    }
+                }
+            });
+        for (auto& h : th) h.join();
+        int nbad = 0;
+        for (int k = 0; k < nt; k++) {
+            t.x.insert(t.x.end(), found[k].begin(), found[k].end());
+            t.delta = std::max(t.delta, dmax[k]);
+            nbad += bad[k];
+        }
+        std::sort(t.x.begin(), t.x.end());
+        t.delta += 1e-6;   // room for the device's double exponential
+        t.usable = nbad == 0 && t.x.size() < (1u << 30);
+    });
+    return t;
+}
+
 static void ctx_destroy(aion_ctx* c) {
     if (!c) return;
     int prev = 0;
@@ -259,6 +352,7 @@ static void ctx_destroy(aion_ctx* c) {
     if (c->gexec) cudaGraphExecDestroy(c->gexec);
     if (c->graph) cudaGraphDestroy(c->graph);
     if (c->arena) cudaFree(c->arena);
+    if (c->exp_tab) cudaFree(c->exp_tab);
     if (c->h_step) cudaFreeHost(c->h_step);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaSetDevice(prev);
@@ -334,6 +428,9 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.xbytes = c->plan.ring_off;
     a.xs_off = c->plan.xs_off;
     a.ops_off = c->plan.xbytes;
+    a.exp_host.x = c->exp_tab;
+    a.exp_host.n = c->exp_n;
+    a.exp_host.delta = c->exp_delta;
     // The grid-barrier counter starts from zero in every launch.
     cudaError_t e = cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream);
     if (e != cudaSuccess) return e;
@@ -658,6 +755,16 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         s = c->mode == MODE_W4A8 ? setup_decode_kernel<MODE_W4A8>(c, max_n, max_chunk)
                                  : setup_decode_kernel<MODE_W4A16>(c, max_n, max_chunk);
         if (s != AION_OK) break;
+        if (c->mode == MODE_W4A8) {   // the bit-exact mode follows the host expf
+            const HostExpTable& t = host_exp_table();
+            if (t.usable && !t.x.empty()) {
+                CK_RET(&c->err, cudaMalloc(&c->exp_tab, t.x.size() * 4));
+                CK_RET(&c->err, cudaMemcpyAsync(c->exp_tab, t.x.data(), t.x.size() * 4, cudaMemcpyHostToDevice,
+                                                c->stream));
+                c->exp_n = (int)t.x.size();
+                c->exp_delta = t.delta;
+            }
+        }
 
         // Step state: pos 0, no forced token, argmax key at its initial value.
         StepState init = {};

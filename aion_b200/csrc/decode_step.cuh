@@ -33,6 +33,14 @@ struct OpDesc {
 
 constexpr int kMaxHead = 128;
 
+// Inputs on which the host C library's expf differs from the correctly
+// rounded e^x (see expf_host).
+struct ExpTable {
+    const uint32_t* x = nullptr;
+    int n = 0;
+    double delta = 0.0;
+};
+
 struct DecodeArgs {
     const OpDesc* ops;             // [nops]: QKV, WO, W13, W2 per layer, then CLS
     int nops;
@@ -52,6 +60,7 @@ struct DecodeArgs {
     int steps;
     int P, slot_bytes, xbytes, xs_off;
     int ops_off;                   // shared-memory copy of ops[] (xbytes = ring offset)
+    ExpTable exp_host;             // the host expf's deviations (W4A8), or empty
 };
 
 // ---------------------------------------------------------------------------
@@ -90,6 +99,32 @@ __device__ __forceinline__ float4 src_load4(const VecSrc& s, int i) {
 // inputs within ~1e-16 relative of a float rounding boundary can differ
 // from the correctly rounded value).
 __device__ __forceinline__ float expf_cr(float x) { return (float)exp((double)x); }
+
+// The host C library's expf, which the reference calls, is not correctly
+// rounded: on a small set of inputs it returns the other float neighbour
+// of e^x.  ExpTable lists those inputs (ascending bit patterns), found on
+// the host by calling that expf on every float with a finite non-zero
+// result; delta bounds how far (in result ulps) from a rounding midpoint
+// e^x lies for any listed input.  expf_host() returns the correctly
+// rounded value unless e^x is that close to a midpoint, and then looks the
+// input up.  With no table it is expf_cr().
+__device__ __forceinline__ float expf_host(float x, const ExpTable& t) {
+    const double yd = exp((double)x);
+    const float f = (float)yd;
+    if (!t.x || !(f < INFINITY)) return f;
+    const float other = (double)f < yd ? nextafterf(f, INFINITY) : nextafterf(f, 0.0f);
+    const double mid = 0.5 * ((double)f + (double)other);
+    const double ulp = fabs((double)other - (double)f);
+    if (!(ulp > 0.0) || fabs(yd - mid) > t.delta * ulp) return f;
+    const uint32_t key = __float_as_uint(x);
+    int lo = 0, hi = t.n;
+    while (lo < hi) {
+        const int m = (lo + hi) >> 1;
+        if (t.x[m] < key) lo = m + 1;
+        else hi = m;
+    }
+    return (lo < t.n && t.x[lo] == key) ? other : f;
+}
 
 constexpr int kMaxVec = 10;       // float4 per thread of an op input: n <= 10 * 4 * kThreads
 constexpr int kMaxNormVec = 4;    // float4 per thread of a normed input: dim <= 4 * 4 * kThreads
@@ -477,7 +512,7 @@ struct DecodeEpi {
             for (int r = 0; r < 2; r++)
                 if (h0 + r < A.hidden) {
                     const float g = v[r];
-                    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g)));
+                    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf_host(-g, A.exp_host)));
                     __stcg(A.hb + h0 + r, __fmul_rn(s, v[2 + r]));
                 }
             break;
@@ -669,7 +704,7 @@ __device__ void attention_layer_exact(const DecodeArgs& a, int layer, int pos, f
             m = fmaxf(m, d);
         }
         m = block_max(m, red);
-        for (int t = tid; t <= pos; t += kThreads) sc[t] = expf_cr(__fsub_rn(sc[t], m));
+        for (int t = tid; t <= pos; t += kThreads) sc[t] = expf_host(__fsub_rn(sc[t], m), a.exp_host);
         csync();
         if (tid == 0) {
             float sum = 0.0f;

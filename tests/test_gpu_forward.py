@@ -6,7 +6,9 @@ Tolerances:
     accumulate; the reorderings of the GPU sums stay near 1e-6);
   - greedy token streams: identical to the reference's own streams
     (tests/golden/tiny.json, from src/kernel_simd.c), all 256 steps;
-  - W4A8 logits: within 1e-6 relative, >= 99.9% bit-identical.
+  - W4A8 logits: bit-identical to the reference order (the exponentials
+    follow the host C library's expf, tabulated where it is not correctly
+    rounded).
 """
 from __future__ import annotations
 
@@ -70,8 +72,7 @@ def test_w4a8_generate_matches_reference_stream(model_w4a8, golden_tiny):
 def test_w4a8_logits_match_oracle(model_w4a8, oracle, tiny_path, golden_tiny):
     """W4A8 follows the reference's operation order end to end (integer group
     dots, sequential epilogues, 4-lane RMSNorm sums, sequential attention and
-    softmax sums, correctly rounded exp): logits agree to 1e-6 relative and
-    nearly all of them bit for bit."""
+    softmax sums, the host's expf): every logit agrees bit for bit."""
     om = oracle.open(tiny_path)
     toks = golden_tiny["w4a8_tokens"]
     equal = total = 0
@@ -81,7 +82,7 @@ def test_w4a8_logits_match_oracle(model_w4a8, oracle, tiny_path, golden_tiny):
         assert rel_err(got, want) <= 1e-6
         equal += int((got.view(np.uint32) == want.view(np.uint32)).sum())
         total += got.size
-    assert equal >= 0.999 * total
+    assert equal == total
     om.close()
 
 
