@@ -1028,6 +1028,84 @@ extern "C" AION_API aion_status aion_matvec_w4a8(const aion_qmatrix* w, const fl
     return matvec_api(MODE_W4A8, w, x_dev, y_dev, stream);
 }
 
+// ---------------------------------------------------------------------------
+// W4A16 matvec on scratch that exists from module load (no counterpart in
+// the reference).  aion_matvec_w4a16 uses the scratch aion_qmatrix_upload
+// allocated next to the weights.  This variant runs the same kernel on a
+// fixed file-scope device array instead, and calls no allocating function.
+// It is for callers that cannot allocate device memory on the call path:
+// a serving loop that has budgeted all device memory at start-up and treats
+// any later allocation as an error, or code that must not trigger the
+// implicit device-wide synchronisation that cudaMalloc / cudaFree can cause
+// while other streams are busy.
+//
+// Limits: matrices of at most kStaticScratchTiles * 16 = 32768 rows (larger
+// ones are rejected with AION_ERR_SHAPE).  The scratch is one array per
+// device shared by every call, so calls that overlap in time (on different
+// streams or threads) race on it and must be serialised by the caller.  The
+// first call on a device looks the array's address up (cudaGetSymbolAddress);
+// make that first call before any stream capture on that device.
+// ---------------------------------------------------------------------------
+constexpr int kStaticScratchTiles = 2048;
+constexpr size_t kStaticPartBytes = (size_t)kStaticScratchTiles * kTR * 4;   // second parts of cut tiles
+constexpr size_t kStaticFlagBytes = (size_t)kStaticScratchTiles * 4;         // cut-tile flags: start at zero
+constexpr size_t kStaticScratchBytes = kStaticPartBytes + kStaticFlagBytes + 256;   // + error word: starts at zero
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxStaticDevices = 64;
+static std::mutex g_static_mu;
+static unsigned char* g_static_addr[kMaxStaticDevices];
+
+// Address of this device's g_static_scratch; the device must be current.
+static aion_status static_scratch_addr(int dev, unsigned char** out) {
+    if (dev < 0 || dev >= kMaxStaticDevices) {
+        set_err(nullptr, "aion_matvec_w4a16_static: device %d out of range", dev);
+        return AION_ERR_ARG;
+    }
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) {
+            set_err(nullptr, "aion_matvec_w4a16_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+            return cuda_status(e);
+        }
+        g_static_addr[dev] = static_cast<unsigned char*>(p);
+    }
+    *out = g_static_addr[dev];
+    return AION_OK;
+}
+
+extern "C" AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, const float* x_dev, float* y_dev,
+                                                         void* stream) {
+    if (!w || !x_dev || !y_dev) {
+        set_err(nullptr, "aion_matvec_w4a16_static: null argument");
+        return AION_ERR_ARG;
+    }
+    if (((uintptr_t)x_dev & 15) || ((uintptr_t)y_dev & 3)) {
+        set_err(nullptr, "aion_matvec_w4a16_static: x must be 16-byte aligned, y 4-byte aligned");
+        return AION_ERR_ARG;
+    }
+    if (w->m.ntiles > kStaticScratchTiles) {
+        set_err(nullptr, "aion_matvec_w4a16_static: %d rows exceed the static scratch limit of %d rows", w->m.d,
+                kStaticScratchTiles * kTR);
+        return AION_ERR_SHAPE;
+    }
+    CK_RET(nullptr, cudaSetDevice(w->device));
+    unsigned char* base = nullptr;
+    const aion_status st = static_scratch_addr(w->device, &base);
+    if (st != AION_OK) return st;
+    Scratch sc;
+    sc.split_part = reinterpret_cast<float*>(base);
+    sc.split_cnt = reinterpret_cast<int*>(base + kStaticPartBytes);
+    sc.error = reinterpret_cast<int*>(base + kStaticPartBytes + kStaticFlagBytes);
+    // The flags and the error word must start at zero (a call that gave up
+    // may have left a flag raised); the partials need no initial value.
+    CK_RET(nullptr, cudaMemsetAsync(sc.split_cnt, 0, kStaticFlagBytes + sizeof(int), (cudaStream_t)stream));
+    CK_RET(nullptr, launch_standalone<MODE_W4A16>(w->m, sc, x_dev, y_dev, w->device, (cudaStream_t)stream));
+    return AION_OK;
+}
+
 extern "C" AION_API aion_status aion_quantize_activations(const float* x, int8_t* qx, float* xs, int64_t n, void* stream) {
     if (!x || !qx || !xs || n <= 0 || n % 32) {
         set_err(nullptr, "aion_quantize_activations: invalid arguments (n must be a positive multiple of 32)");

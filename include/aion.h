@@ -142,6 +142,15 @@ AION_API aion_status aion_matvec_w4a16(const aion_qmatrix* w, const float* x_dev
  * dispatch_matmul_w4a8 (:771) would run them.  Bit-exact with them. */
 AION_API aion_status aion_matvec_w4a8(const aion_qmatrix* w, const float* x_dev, float* y_dev, void* stream);
 
+/* The W4A16 matvec of aion_matvec_w4a16 with its scratch in a fixed device
+ * array instead of the matrix's own scratch; it calls no allocating
+ * function.  No counterpart in the reference.  At most 32768 rows
+ * (AION_ERR_SHAPE beyond).  One scratch array per device is shared by all
+ * calls: calls that overlap in time race and must be serialised by the
+ * caller.  The first call on a device resolves the array's address; make it
+ * before any stream capture on that device. */
+AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, const float* x_dev, float* y_dev, void* stream);
+
 /* Per-32 symmetric int8 activation quantization (quantize_activations_neon,
  * src/kernel_simd.c:186-227): qx[n] int8, xs[n/32] fp32.  Bit-exact. */
 AION_API aion_status aion_quantize_activations(const float* x_dev, int8_t* qx_dev, float* xs_dev, int64_t n,
