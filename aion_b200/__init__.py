@@ -93,6 +93,7 @@ def lib() -> ctypes.CDLL:
         "aion_matvec_w4a16": (I32, [VP, VP, VP, VP]),
         "aion_matvec_w4a8": (I32, [VP, VP, VP, VP]),
         "aion_matvec_w4a16_static": (I32, [VP, VP, VP, VP]),
+        "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
         "aion_quantize_activations": (I32, [VP, VP, VP, I64, VP]),
         "aion_quantize_buffer": (None, [VP, VP, VP, I64]),
         "aion_checkpoint_bytes": (I64, [P(I32), ctypes.c_int]),

@@ -23,8 +23,11 @@
 #include <thread>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/aion.h"
 #include "decode_step.cuh"
+#include "gemm_tc.cuh"
 
 using namespace aion;
 
@@ -1104,6 +1107,95 @@ extern "C" AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, 
     CK_RET(nullptr, cudaMemsetAsync(sc.split_cnt, 0, kStaticFlagBytes + sizeof(int), (cudaStream_t)stream));
     CK_RET(nullptr, launch_standalone<MODE_W4A16>(w->m, sc, x_dev, y_dev, w->device, (cudaStream_t)stream));
     return AION_OK;
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05 bf16 GEMM (prefill building block)
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D tensor map of a row-major bf16 [rows][cols] matrix, box (64 cols x
+// box_rows rows), 128-byte swizzle (the UMMA K-major canonical layout).
+static bool bf16_tensor_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int* g_gemm_err_dev[kMaxStaticDevices];
+static __device__ int g_gemm_err_word;
+
+// C[M][ldc] (fp32) = A[M][K] * B[N][K]^T, bf16 A and B with K contiguous.
+static aion_status launch_gemm_bf16(const void* a, const void* b, float* c, int64_t m, int64_t n, int64_t k,
+                                    int64_t ldc, int dev, cudaStream_t st, int* err_dev, std::string* err) {
+    if (m <= 0 || n <= 0 || k <= 0 || m % kGemmBM || n % kGemmBN || k % kGemmBK || ldc < n || ldc % 4 ||
+        m / kGemmBM > 0x7FFFFFFF || n / kGemmBN > 65535) {
+        set_err(err, "gemm: M, N, K must be positive multiples of %d, %d, %d (got %lld, %lld, %lld)", kGemmBM,
+                kGemmBN, kGemmBK, (long long)m, (long long)n, (long long)k);
+        return AION_ERR_SHAPE;
+    }
+    if (((uintptr_t)a & 15) || ((uintptr_t)b & 15) || ((uintptr_t)c & 15)) {
+        set_err(err, "gemm: A, B and C must be 16-byte aligned");
+        return AION_ERR_ARG;
+    }
+    CUtensorMap ma, mb;
+    if (!bf16_tensor_map(&ma, a, m, k, kGemmBM) || !bf16_tensor_map(&mb, b, n, k, kGemmBN)) {
+        set_err(err, "gemm: cuTensorMapEncodeTiled is unavailable or rejected the operands");
+        return AION_ERR_CUDA;
+    }
+    static bool attr_done[kMaxStaticDevices] = {};
+    if (dev >= 0 && dev < kMaxStaticDevices && !attr_done[dev]) {
+        CK_RET(err, cudaFuncSetAttribute(k_gemm_bf16_tn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+        attr_done[dev] = true;
+    }
+    GemmArgs g;
+    g.C = c;
+    g.M = (int)m;
+    g.N = (int)n;
+    g.K = (int)k;
+    g.ldc = (int)ldc;
+    g.err = err_dev;
+    k_gemm_bf16_tn<<<dim3((unsigned)(m / kGemmBM), (unsigned)(n / kGemmBN)), kGemmThreads, kGemmSmem, st>>>(ma, mb, g);
+    CK_RET(err, cudaGetLastError());
+    return AION_OK;
+}
+
+extern "C" AION_API aion_status aion_gemm_bf16_tn(const void* a_dev, const void* b_dev, float* c_dev, int64_t m,
+                                                  int64_t n, int64_t k, void* stream) {
+    if (!a_dev || !b_dev || !c_dev) {
+        set_err(nullptr, "aion_gemm_bf16_tn: null argument");
+        return AION_ERR_ARG;
+    }
+    int dev = 0;
+    CK_RET(nullptr, cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxStaticDevices) return AION_ERR_ARG;
+    if (!g_gemm_err_dev[dev]) {
+        void* p = nullptr;
+        CK_RET(nullptr, cudaGetSymbolAddress(&p, g_gemm_err_word));
+        g_gemm_err_dev[dev] = static_cast<int*>(p);
+    }
+    std::string err;
+    const aion_status s = launch_gemm_bf16(a_dev, b_dev, c_dev, m, n, k, n, dev, (cudaStream_t)stream,
+                                           g_gemm_err_dev[dev], &err);
+    if (s != AION_OK) set_err(nullptr, "%s", err.c_str());
+    return s;
 }
 
 extern "C" AION_API aion_status aion_quantize_activations(const float* x, int8_t* qx, float* xs, int64_t n, void* stream) {

@@ -1,0 +1,191 @@
+// Dense bf16 GEMM on the 5th-generation tensor cores (sm_100a), for the
+// batched prefill: C[M][N] (fp32) = A[M][K] * B[N][K]^T, A and B bf16 with K
+// contiguous.  The int4 weights reach it as bf16 tiles written by
+// k_dequant_bf16 (decode_prefill.cuh); the activations as bf16 rows.
+//
+// One CTA computes one 128 x 256 tile of C:
+//   warp 0     TMA producer: 128 x 64 tile of A and 256 x 64 tile of B per
+//              K block into a ring of kStages shared-memory stages (128-byte
+//              swizzle), completion counted on the stage's full mbarrier;
+//   warp 1     allocates 256 TMEM columns, then one thread issues
+//              tcgen05.mma (M 128, N 256, K 16; bf16 x bf16 -> fp32 in TMEM)
+//              four times per K block and commits each stage back to its
+//              empty mbarrier, and the whole tile to the done mbarrier;
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator (each warp its TMEM
+//              lane quarter, 16 columns at a time) and fp32 stores to C.
+// Every wait is bounded; a wait that gives up records an error code in
+// *err and the CTA finishes without further work.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace aion {
+
+constexpr int kGemmBM = 128, kGemmBN = 256, kGemmBK = 64;
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;   // 16 KB
+constexpr int kGemmBBytes = kGemmBN * kGemmBK * 2;   // 32 KB
+constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
+constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 1024;   // + room to align to 1024
+constexpr uint32_t kGemmWaitLimit = 1u << 26;
+
+// UMMA shared-memory matrix descriptor, K-major with the 128-byte swizzle:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: bf16 A and B (K-major), fp32 D, M 128, N 256.
+constexpr uint32_t kGemmIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGemmBN >> 3) << 17) |
+                                ((uint32_t)(kGemmBM >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+struct GemmArgs {
+    float* C;          // [M][ldc]
+    int M, N, K;       // multiples of 128, 256 and 64
+    int ldc;
+    int* err;          // first error code of any CTA (0 = none)
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+k_gemm_bf16_tn(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs g) {
+    extern __shared__ __align__(1024) unsigned char gsm_raw[];
+    __shared__ __align__(8) uint64_t full_bar[kGemmStages], empty_bar[kGemmStages], done_bar;
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_fail;
+    unsigned char* gsm =
+        gsm_raw + ((1024u - (smem_addr(gsm_raw) & 1023u)) & 1023u);   // stages start 1024-aligned
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
+    const int nkb = g.K / kGemmBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGemmStages; s++) {
+            mbar_init(smem_addr(&full_bar[s]), 1);
+            mbar_init(smem_addr(&empty_bar[s]), 1);
+        }
+        mbar_init(smem_addr(&done_bar), 1);
+        s_fail = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
+                     "r"(kGemmBN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == 0 && lane == 0) {
+        // Producer.  Stage s is reused after the MMAs that read it commit.
+        for (int kb = 0; kb < nkb; kb++) {
+            const int s = kb % kGemmStages;
+            const uint32_t round = kb / kGemmStages;
+            if (round > 0 && !mbar_wait(smem_addr(&empty_bar[s]), (round - 1) & 1, kGemmWaitLimit)) {
+                s_fail = 1;
+                break;
+            }
+            const uint32_t sa = smem_addr(gsm + s * kGemmStageBytes);
+            mbar_arrive_expect_tx(smem_addr(&full_bar[s]), kGemmStageBytes);
+            tma_load_2d(sa, &map_a, kb * kGemmBK, m0, smem_addr(&full_bar[s]));
+            tma_load_2d(sa + kGemmABytes, &map_b, kb * kGemmBK, n0, smem_addr(&full_bar[s]));
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer.
+        bool ok = true;
+        for (int kb = 0; kb < nkb && ok; kb++) {
+            const int s = kb % kGemmStages;
+            if (!mbar_wait(smem_addr(&full_bar[s]), (kb / kGemmStages) & 1, kGemmWaitLimit)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_addr(gsm + s * kGemmStageBytes);
+            const uint64_t adesc = umma_desc_sw128(sa), bdesc = umma_desc_sw128(sa + kGemmABytes);
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 16; k++)   // 32 bytes of K per step inside the swizzle atom
+                umma_bf16(tmem, adesc + 2 * k, bdesc + 2 * k, kGemmIdesc, (kb | k) != 0);
+            umma_commit(smem_addr(&empty_bar[s]));
+        }
+        if (!ok) s_fail = 1;
+        umma_commit(smem_addr(&done_bar));   // arrives once the issued MMAs are complete
+    } else if (warp >= 2) {
+        // Epilogue: TMEM lane quarter q = warp % 4 holds rows m0 + 32q ..
+        const int q = warp & 3;
+        const bool done = mbar_wait(smem_addr(&done_bar), 0, kGemmWaitLimit);
+        tc_fence_after();
+        if (done) {
+            const int row = m0 + 32 * q + lane;
+            float* crow = g.C + (size_t)row * g.ldc + n0;
+#pragma unroll 1
+            for (int c = 0; c < kGemmBN; c += 16) {
+                float v[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<float4*>(crow + c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            }
+        } else if (lane == 0) {
+            s_fail = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0 && lane == 0) {
+        // Let every issued copy land before the CTA's shared memory goes.
+        for (int kb = (nkb > kGemmStages ? nkb - kGemmStages : 0); kb < nkb; kb++)
+            mbar_wait(smem_addr(&full_bar[kb % kGemmStages]), (kb / kGemmStages) & 1, 1u << 20);
+    }
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmBN) : "memory");
+    }
+    if (threadIdx.x == 0 && s_fail) atomicCAS(g.err, 0, DEV_COPY_TIMEOUT);
+}
+
+}  // namespace aion

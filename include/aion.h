@@ -151,6 +151,14 @@ AION_API aion_status aion_matvec_w4a8(const aion_qmatrix* w, const float* x_dev,
  * before any stream capture on that device. */
 AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, const float* x_dev, float* y_dev, void* stream);
 
+/* Dense GEMM on the tensor cores: C[m][n] (fp32) = A[m][k] * B[n][k]^T with
+ * A and B bf16 (K contiguous), all device memory, on the current device.
+ * The building block of the batched prefill, where B holds int4 weights
+ * dequantized to bf16; no counterpart in the reference.  m, n, k must be
+ * multiples of 128, 256 and 64; A, B and C 16-byte aligned. */
+AION_API aion_status aion_gemm_bf16_tn(const void* a_dev, const void* b_dev, float* c_dev, int64_t m, int64_t n,
+                                       int64_t k, void* stream);
+
 /* Per-32 symmetric int8 activation quantization (quantize_activations_neon,
  * src/kernel_simd.c:186-227): qx[n] int8, xs[n/32] fp32.  Bit-exact. */
 AION_API aion_status aion_quantize_activations(const float* x_dev, int8_t* qx_dev, float* xs_dev, int64_t n,
