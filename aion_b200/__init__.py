@@ -94,6 +94,8 @@ def lib() -> ctypes.CDLL:
         "aion_matvec_w4a8": (I32, [VP, VP, VP, VP]),
         "aion_matvec_w4a16_static": (I32, [VP, VP, VP, VP]),
         "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
+        "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
+        "aion_set_sequence": (I32, [VP, I32]),
         "aion_quantize_activations": (I32, [VP, VP, VP, I64, VP]),
         "aion_quantize_buffer": (None, [VP, VP, VP, I64]),
         "aion_checkpoint_bytes": (I64, [P(I32), ctypes.c_int]),
@@ -163,7 +165,8 @@ class Model:
     """A device-resident int4 model: load_checkpoint_int4 + RunState of the
     reference (src/kernel_simd.c:941-1008), on one B200."""
 
-    def __init__(self, path, device: int = 0, mode: str = "int4", max_pos: int = 0, use_graph: bool = True):
+    def __init__(self, path, device: int = 0, mode: str = "int4", max_pos: int = 0, use_graph: bool = True,
+                 max_batch: int = 1):
         L = lib()
         o = Opts()
         L.aion_default_opts(ctypes.byref(o))
@@ -171,6 +174,7 @@ class Model:
         o.mode = {"int4": MODE_W4A16, "w4a16": MODE_W4A16, "w4a8": MODE_W4A8}[mode]
         o.max_pos = max_pos
         o.use_graph = 1 if use_graph else 0
+        o.max_batch = max_batch
         h = ctypes.c_void_p()
         _check(L.aion_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)))
         self._h = h
@@ -203,6 +207,21 @@ class Model:
         return out
 
     forward = transformer
+
+    def prefill(self, tokens) -> np.ndarray:
+        """Runs tokens[n_seq][n_tok] through the model at positions 0..n_tok-1
+        of sequences 0..n_seq-1 (their KV caches) on the tensor cores;
+        returns the logits of each sequence's last position."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        if t.ndim == 1:
+            t = t[None, :]
+        out = np.empty((t.shape[0], self.config.vocab_size), np.float32)
+        _check(lib().aion_prefill(self._h, _ptr(t), t.shape[0], t.shape[1], _ptr(out)), self._h)
+        return out
+
+    def set_sequence(self, seq: int) -> None:
+        """Selects the sequence (KV cache) that forward / decode calls use."""
+        _check(lib().aion_set_sequence(self._h, seq), self._h)
 
     def generate(self, steps: int, bos: int = 1):
         """Greedy decode from `bos`; returns (input token of each step, seconds)."""

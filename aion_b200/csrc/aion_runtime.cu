@@ -28,6 +28,7 @@
 #include "../../include/aion.h"
 #include "decode_step.cuh"
 #include "gemm_tc.cuh"
+#include "prefill.cuh"
 
 using namespace aion;
 
@@ -205,6 +206,16 @@ struct aion_ctx {
     aion_opts opts;
     aion_config cfg;
     int dev = 0, mode = 0;
+    int nseq = 1;                  // sequences (KV caches) held; opts.max_batch
+    int cur_seq = 0;               // the sequence decode / forward calls run on
+    size_t kv_seq = 0;             // floats per sequence in kcache / vcache
+    struct PrefillBufs {           // grown on demand by aion_prefill
+        __nv_bfloat16 *a = nullptr, *b = nullptr;
+        float *c = nullptr, *x = nullptr, *q = nullptr;
+        int32_t* tok = nullptr;
+        int* map = nullptr;
+        size_t a_cap = 0, b_cap = 0, c_cap = 0, x_cap = 0, q_cap = 0, tok_cap = 0, map_cap = 0;
+    } pf;
     uint32_t* exp_tab = nullptr;   // W4A8: inputs where the host expf is not correctly rounded
     int exp_n = 0;
     double exp_delta = 0.0;
@@ -356,6 +367,9 @@ static void ctx_destroy(aion_ctx* c) {
     if (c->graph) cudaGraphDestroy(c->graph);
     if (c->arena) cudaFree(c->arena);
     if (c->exp_tab) cudaFree(c->exp_tab);
+    for (void* p : {(void*)c->pf.a, (void*)c->pf.b, (void*)c->pf.c, (void*)c->pf.x, (void*)c->pf.q,
+                    (void*)c->pf.tok, (void*)c->pf.map})
+        if (p) cudaFree(p);
     if (c->h_step) cudaFreeHost(c->h_step);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaSetDevice(prev);
@@ -415,8 +429,8 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.att = c->att;
     a.hb = c->hb;
     a.logits = c->logits;
-    a.kcache = c->kcache;
-    a.vcache = c->vcache;
+    a.kcache = c->kcache + (size_t)c->cur_seq * c->kv_seq;
+    a.vcache = c->vcache + (size_t)c->cur_seq * c->kv_seq;
     a.attn_part = c->attn_part;
     a.attn_cnt = c->attn_cnt;
     a.max_chunks = c->max_chunks;
@@ -626,7 +640,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         bytes += L * (align256(desc_bytes(dq)) + align256(desc_bytes(dwo)) + align256(desc_bytes(d13)) +
                       align256(desc_bytes(d2)));
         bytes += align256(L * dim * 4) * 2 + align256(dim * 4) + 2 * align256(c->seq * (c->hs / 2) * 4);
-        bytes += 2 * align256((size_t)L * c->max_pos * kv * 4);
+        bytes += 2 * align256((size_t)c->nseq * L * c->max_pos * kv * 4);
         bytes += 3 * align256(dim * 4) + align256(hid * 4) + align256(c->vocab * 4);
         bytes += align256((size_t)c->nh * c->max_chunks * (c->hs + 4) * 4) + align256(c->nh * 4);
         bytes += align256(sizeof(StepState)) + align256(8) + align256((size_t)c->max_pos * 4);
@@ -650,8 +664,9 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         c->rms_final = (float*)arena_take(c, dim * 4);
         c->freq_re = (float*)arena_take(c, c->seq * (c->hs / 2) * 4);
         c->freq_im = (float*)arena_take(c, c->seq * (c->hs / 2) * 4);
-        c->kcache = (float*)arena_take(c, (size_t)L * c->max_pos * kv * 4);
-        c->vcache = (float*)arena_take(c, (size_t)L * c->max_pos * kv * 4);
+        c->kv_seq = (size_t)L * c->max_pos * kv;
+        c->kcache = (float*)arena_take(c, (size_t)c->nseq * c->kv_seq * 4);
+        c->vcache = (float*)arena_take(c, (size_t)c->nseq * c->kv_seq * 4);
         c->x = (float*)arena_take(c, dim * 4);
         c->q = (float*)arena_take(c, dim * 4);
         c->att = (float*)arena_take(c, dim * 4);
@@ -799,11 +814,17 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
         delete c;
         return AION_ERR_ARG;
     }
-    if (c->opts.max_batch > 1 || c->opts.tp_size > 1) {
-        set_err(&c->err, "max_batch > 1 and tp_size > 1 are not available in this build");
+    if (c->opts.tp_size > 1) {
+        set_err(&c->err, "tp_size > 1 is not available in this build");
         delete c;
         return AION_ERR_ARG;
     }
+    if (c->opts.max_batch < 1 || c->opts.max_batch > 1024) {
+        set_err(&c->err, "max_batch %d out of range [1, 1024]", c->opts.max_batch);
+        delete c;
+        return AION_ERR_ARG;
+    }
+    c->nseq = c->opts.max_batch;
     c->mode = c->opts.mode == AION_MODE_W4A8 ? MODE_W4A8 : MODE_W4A16;
     c->dev = c->opts.device;
     aion_status hs = read_header(path, &c->cfg, &c->err);
@@ -904,14 +925,174 @@ extern "C" AION_API aion_status aion_tokens(aion_ctx* c, int32_t* out, int32_t n
 extern "C" AION_API aion_status aion_reset(aion_ctx* c) {
     if (!c) return AION_ERR_ARG;
     CK_RET(&c->err, cudaSetDevice(c->dev));
-    const size_t kvb = (size_t)c->L * c->max_pos * c->kv_dim * 4;
-    CK_RET(&c->err, cudaMemsetAsync(c->kcache, 0, kvb, c->stream));
-    CK_RET(&c->err, cudaMemsetAsync(c->vcache, 0, kvb, c->stream));
+    const size_t kvb = c->kv_seq * 4;
+    CK_RET(&c->err, cudaMemsetAsync(c->kcache + (size_t)c->cur_seq * c->kv_seq, 0, kvb, c->stream));
+    CK_RET(&c->err, cudaMemsetAsync(c->vcache + (size_t)c->cur_seq * c->kv_seq, 0, kvb, c->stream));
     CK_RET(&c->err, cudaMemsetAsync(&c->step->error, 0, sizeof(int32_t), c->stream));
     CK_RET(&c->err, cudaMemsetAsync(c->attn_cnt, 0, c->nh * 4, c->stream));
     CK_RET(&c->err, cudaMemsetAsync(c->split_cnt, 0, (size_t)c->max_tiles * 4, c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return AION_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Sequences and batched prefill (no counterpart in the reference, whose
+// transformer() takes one token of one sequence)
+// ---------------------------------------------------------------------------
+extern "C" AION_API aion_status aion_set_sequence(aion_ctx* c, int32_t seq) {
+    if (!c) return AION_ERR_ARG;
+    if (seq < 0 || seq >= c->nseq) {
+        set_err(&c->err, "aion_set_sequence: sequence %d out of range [0, %d)", seq, c->nseq);
+        return AION_ERR_ARG;
+    }
+    if (seq == c->cur_seq) return AION_OK;
+    CK_RET(&c->err, cudaSetDevice(c->dev));
+    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    c->cur_seq = seq;
+    // The per-token graph holds the previous sequence's cache pointers.
+    if (c->gexec) {
+        cudaGraphExecDestroy(c->gexec);
+        c->gexec = nullptr;
+    }
+    if (c->graph) {
+        cudaGraphDestroy(c->graph);
+        c->graph = nullptr;
+    }
+    return AION_OK;
+}
+
+static aion_status launch_gemm_bf16(const void* a, const void* b, float* c, int64_t m, int64_t n, int64_t k,
+                                    int64_t ldc, int dev, cudaStream_t st, int* err_dev, std::string* err);
+
+// Grows a prefill buffer to at least `bytes`.
+static cudaError_t pf_grow(void** p, size_t* cap, size_t bytes) {
+    if (*cap >= bytes) return cudaSuccess;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(p, bytes);
+    if (e == cudaSuccess) *cap = bytes;
+    return e;
+}
+
+static inline long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
+
+// One int4 matrix product of the prefill: C[mpad][np] = A(3*kp) * B(matrix)^T.
+static aion_status pf_matmul(aion_ctx* c, const MatDesc& w, long long mpad, long long kp, long long* np_out) {
+    const long long np = round_up(w.d, kGemmBN);
+    const long long tasks = np * (kp / 8);
+    const int blocks = (int)std::min<long long>((tasks + 255) / 256, 148LL * 32);
+    k_pf_dequant<<<blocks, 256, 0, c->stream>>>(w, (int)np, (int)kp, c->pf.b);
+    CK_RET(&c->err, cudaGetLastError());
+    const aion_status s = launch_gemm_bf16(c->pf.a, c->pf.b, c->pf.c, mpad, np, 3 * kp, np, c->dev, c->stream,
+                                           &c->step->error, &c->err);
+    *np_out = np;
+    return s;
+}
+
+extern "C" AION_API aion_status aion_prefill(aion_ctx* c, const int32_t* tokens, int32_t n_seq, int32_t n_tok,
+                                             float* logits_host) {
+    if (!c || !tokens || n_seq < 1 || n_tok < 1) return AION_ERR_ARG;
+    if (n_seq > c->nseq || n_tok > c->max_pos) {
+        set_err(&c->err, "aion_prefill: %d sequences x %d tokens exceed the context (%d sequences, %d positions)",
+                n_seq, n_tok, c->nseq, c->max_pos);
+        return AION_ERR_ARG;
+    }
+    for (long long i = 0; i < (long long)n_seq * n_tok; i++)
+        if (tokens[i] < 0 || tokens[i] >= c->vocab) {
+            set_err(&c->err, "aion_prefill: token %d at %lld out of range", tokens[i], i);
+            return AION_ERR_ARG;
+        }
+    CK_RET(&c->err, cudaSetDevice(c->dev));
+    const long long dim = c->dim, hid = c->hidden, kv = c->kv_dim, L = c->L;
+    const long long mrows = (long long)n_seq * n_tok, mpad = round_up(mrows, kGemmBM);
+    const long long kpd = round_up(dim, kGemmBK), kph = round_up(hid, kGemmBK);
+    const long long np_max = std::max({round_up(dim + 2 * kv, kGemmBN), round_up(2 * hid, kGemmBN),
+                                       round_up(dim, kGemmBN)});
+    const long long np_cls = round_up(c->vocab, kGemmBN), mcls = round_up(n_seq, kGemmBM);
+    const long long kmax = std::max(kpd, kph);
+    const size_t a_bytes = (size_t)std::max(mpad, mcls) * 3 * kmax * 2;
+    const size_t b_bytes = (size_t)std::max({np_max * 3 * kpd, round_up(dim, kGemmBN) * 3 * kph, np_cls * 3 * kpd}) * 2;
+    const size_t c_bytes = (size_t)std::max(mpad * np_max, mcls * np_cls) * 4;
+    auto& pf = c->pf;
+    CK_RET(&c->err, pf_grow((void**)&pf.a, &pf.a_cap, a_bytes));
+    CK_RET(&c->err, pf_grow((void**)&pf.b, &pf.b_cap, b_bytes));
+    CK_RET(&c->err, pf_grow((void**)&pf.c, &pf.c_cap, c_bytes));
+    CK_RET(&c->err, pf_grow((void**)&pf.x, &pf.x_cap, (size_t)mrows * dim * 4));
+    CK_RET(&c->err, pf_grow((void**)&pf.q, &pf.q_cap, (size_t)mrows * dim * 4));
+    CK_RET(&c->err, pf_grow((void**)&pf.tok, &pf.tok_cap, (size_t)mrows * 4));
+    CK_RET(&c->err, pf_grow((void**)&pf.map, &pf.map_cap, (size_t)mcls * 4));
+    CK_RET(&c->err, cudaMemcpyAsync(pf.tok, tokens, (size_t)mrows * 4, cudaMemcpyHostToDevice, c->stream));
+    std::vector<int> map(n_seq);
+    for (int s = 0; s < n_seq; s++) map[s] = s * n_tok + n_tok - 1;
+    CK_RET(&c->err, cudaMemcpyAsync(pf.map, map.data(), n_seq * 4, cudaMemcpyHostToDevice, c->stream));
+    CK_RET(&c->err, cudaFuncSetAttribute(k_pf_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfAttnSmem));
+
+    k_pf_embed<<<(unsigned)mrows, 256, 0, c->stream>>>(pf.tok, (int)mrows, c->emb, (int)dim, pf.x);
+    CK_RET(&c->err, cudaGetLastError());
+    for (long long l = 0; l < L; l++) {
+        long long np = 0;
+        // attention block
+        k_pf_norm_split<<<(unsigned)mpad, 256, 0, c->stream>>>(pf.x, nullptr, (int)mrows, (int)dim, (int)kpd,
+                                                                c->rms_att + l * dim, pf.a);
+        aion_status st = pf_matmul(c, c->qkv[l], mpad, kpd, &np);
+        if (st != AION_OK) return st;
+        PfRopeArgs ra;
+        ra.c = pf.c;
+        ra.ldc = (int)np;
+        ra.mrows = (int)mrows;
+        ra.T = n_tok;
+        ra.dim = (int)dim;
+        ra.kv_dim = (int)kv;
+        ra.hs = (int)c->hs;
+        ra.freq_re = c->freq_re;
+        ra.freq_im = c->freq_im;
+        ra.q = pf.q;
+        ra.kcache = c->kcache + (size_t)l * c->max_pos * kv;
+        ra.vcache = c->vcache + (size_t)l * c->max_pos * kv;
+        ra.seq_stride = c->kv_seq;
+        k_pf_rope_kv<<<(unsigned)mrows, 256, 0, c->stream>>>(ra);
+        PfAttnArgs aa;
+        aa.q = pf.q;
+        aa.kcache = ra.kcache;
+        aa.vcache = ra.vcache;
+        aa.seq_stride = c->kv_seq;
+        aa.T = n_tok;
+        aa.dim = (int)dim;
+        aa.kv_dim = (int)kv;
+        aa.hs = (int)c->hs;
+        aa.kv_mul = (int)c->kv_mul;
+        aa.kp = (int)kpd;
+        aa.out = pf.a;
+        k_pf_attention<<<dim3((unsigned)((n_tok + kPfQB - 1) / kPfQB), (unsigned)c->nh, (unsigned)n_seq), 256,
+                         kPfAttnSmem, c->stream>>>(aa);
+        CK_RET(&c->err, cudaGetLastError());
+        st = pf_matmul(c, c->wo[l], mpad, kpd, &np);
+        if (st != AION_OK) return st;
+        k_pf_residual<<<(unsigned)mrows, 256, 0, c->stream>>>(pf.x, pf.c, (int)np, (int)mrows, (int)dim);
+        // feed-forward block
+        k_pf_norm_split<<<(unsigned)mpad, 256, 0, c->stream>>>(pf.x, nullptr, (int)mrows, (int)dim, (int)kpd,
+                                                                c->rms_ffn + l * dim, pf.a);
+        st = pf_matmul(c, c->w13[l], mpad, kpd, &np);
+        if (st != AION_OK) return st;
+        k_pf_swiglu_split<<<(unsigned)mpad, 256, 0, c->stream>>>(pf.c, (int)np, (int)mrows, (int)hid, (int)kph,
+                                                                  pf.a);
+        st = pf_matmul(c, c->w2[l], mpad, kph, &np);
+        if (st != AION_OK) return st;
+        k_pf_residual<<<(unsigned)mrows, 256, 0, c->stream>>>(pf.x, pf.c, (int)np, (int)mrows, (int)dim);
+        CK_RET(&c->err, cudaGetLastError());
+    }
+    // Logits of each sequence's last position.
+    k_pf_norm_split<<<(unsigned)mcls, 256, 0, c->stream>>>(pf.x, pf.map, n_seq, (int)dim, (int)kpd, c->rms_final,
+                                                            pf.a);
+    long long np = 0;
+    aion_status st = pf_matmul(c, c->emb, mcls, kpd, &np);
+    if (st != AION_OK) return st;
+    if (logits_host)
+        CK_RET(&c->err, cudaMemcpy2DAsync(logits_host, (size_t)c->vocab * 4, pf.c, (size_t)np * 4,
+                                          (size_t)c->vocab * 4, (size_t)n_seq, cudaMemcpyDeviceToHost, c->stream));
+    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
 }
 
 // ---------------------------------------------------------------------------

@@ -69,9 +69,9 @@ struct DecodeArgs {
 // token (src/kernel_simd.c:1032-1040: x[i] = (int8)(nibble - 8) * scale).
 // ---------------------------------------------------------------------------
 struct VecSrc {
-    const float* p;                // fp32 vector, or nullptr for the embedding row
+    const float* p = nullptr;      // fp32 vector, or nullptr for the embedding row
     MatDesc emb;
-    int tok;
+    int tok = 0;
 };
 
 __device__ __forceinline__ float4 src_load4(const VecSrc& s, int i) {

@@ -50,7 +50,7 @@ enum { AION_MODE_W4A16 = 0, AION_MODE_W4A8 = 1 };
 typedef struct aion_opts {
     int32_t device;     /* CUDA device ordinal                                        */
     int32_t mode;       /* AION_MODE_W4A16 (default) or AION_MODE_W4A8                */
-    int32_t max_batch;  /* sequences decoded in lock-step (default 1)                  */
+    int32_t max_batch;  /* sequences (KV caches) held, for aion_prefill (default 1)      */
     int32_t max_pos;    /* KV positions allocated (0 = header seq_len; <= seq_len)     */
     int32_t tp_size;    /* tensor-parallel ranks (default 1)                           */
     int32_t tp_rank;    /* this rank, 0 <= tp_rank < tp_size                           */
@@ -87,7 +87,7 @@ AION_API aion_status aion_get_config(const aion_ctx* ctx, aion_config* out);
  * readable through aion_logits_dev().  Requires 0 <= pos < max_pos. */
 AION_API aion_status aion_forward(aion_ctx* ctx, int32_t token, int32_t pos, float* logits_host);
 
-/* Device pointer to the logits of the last step ([max_batch][vocab] fp32). */
+/* Device pointer to the logits of the last decode step ([vocab] fp32). */
 AION_API const float* aion_logits_dev(const aion_ctx* ctx);
 
 /* Replaces the greedy loop of main (src/kernel_simd.c:1223-1258): starts at
@@ -111,8 +111,30 @@ AION_API aion_status aion_decode_async(aion_ctx* ctx, int32_t token, int32_t pos
 /* Copies the input tokens of positions [0, n) recorded on the device. */
 AION_API aion_status aion_tokens(aion_ctx* ctx, int32_t* out, int32_t n);
 
-/* Clears the KV cache (a new sequence). */
+/* Clears the KV cache of the selected sequence (a new sequence). */
 AION_API aion_status aion_reset(aion_ctx* ctx);
+
+/* ---------------------------------------------------------------------------
+ * Several sequences and batched prefill (no counterpart in the reference,
+ * whose transformer() takes one token of one sequence).  A context holds
+ * opts.max_batch sequences, each with its own KV cache.
+ * ------------------------------------------------------------------------- */
+
+/* Selects the sequence whose KV cache aion_forward / aion_decode_async /
+ * aion_generate / aion_reset use (default 0).  The step state (position,
+ * token history) is shared: set the position explicitly after switching. */
+AION_API aion_status aion_set_sequence(aion_ctx* ctx, int32_t seq);
+
+/* Runs tokens[n_seq][n_tok] (host memory, row-major) through the model at
+ * positions 0..n_tok-1 of sequences 0..n_seq-1, all tokens at once: every
+ * matrix product on the tensor cores (int4 weights dequantized to bf16,
+ * operands split into two bf16 parts, fp32 accumulate), causal attention
+ * per sequence and head.  Writes each sequence's KV cache at those
+ * positions and the logits of each sequence's last position to
+ * logits_host[n_seq][vocab] (may be NULL).  Equivalent to n_tok
+ * transformer() calls per sequence.  n_seq <= max_batch, n_tok <= max_pos. */
+AION_API aion_status aion_prefill(aion_ctx* ctx, const int32_t* tokens, int32_t n_seq, int32_t n_tok,
+                                  float* logits_host);
 
 /* ---------------------------------------------------------------------------
  * Kernel level (device pointers; stream = cudaStream_t or NULL)
