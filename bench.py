@@ -21,6 +21,11 @@ N > 1: independent replicas, one per GPU (the 7B path does not shard;
 built from the reference's src/kernel_simd.c; scalar int4 kernel, host
 thread pool) on the same workload, bounded to a few minutes.
 --matvec times the isolated matvec shapes only (for profiling).
+The JSON line also carries "prefill": the batched-prefill workload on the
+same model (32 sequences x 512 uniform random tokens, seed 2, through every
+layer at once on the tensor cores, then 128 greedy decode steps per
+sequence), with its own roofline against the measured bf16 peak
+(--no-prefill skips it).
 --profile-layers L runs the same path on a 7B-shape checkpoint truncated to
 L layers (same seed and shapes; for ncu captures that must stay small, never
 for the reported metric).
@@ -203,6 +208,59 @@ def run_reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+PREFILL_SEQ, PREFILL_TOK, PREFILL_DECODE, PREFILL_SEED = 32, 512, 128, 2
+
+
+def bf16_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured (sustained)"
+        except Exception:
+            pass
+    return 1400.0, "fallback (sustained)"
+
+
+def prefill_leg(model, layers: int, stream, device: int) -> dict:
+    """32 x 512 prefill then 128 decode steps per sequence, timed with CUDA
+    events on the model's stream."""
+    import torch
+    dim, hid, vocab = CFG_7B[0], CFG_7B[1], CFG_7B[5]
+    toks = np.random.default_rng(PREFILL_SEED).integers(0, vocab, (PREFILL_SEQ, PREFILL_TOK)).astype(np.int32)
+    model.prefill(toks[:2, :64])          # warm-up: buffers, tensor maps, module load
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    logits = model.prefill(toks)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    rows = PREFILL_SEQ * PREFILL_TOK
+    lin_flops = 2.0 * rows * layers * (4 * dim * dim + 3 * dim * hid) + 2.0 * PREFILL_SEQ * vocab * dim
+    attn_flops = PREFILL_SEQ * layers * 2.0 * (PREFILL_TOK * (PREFILL_TOK + 1) / 2) * dim * 2
+    tflops = (lin_flops + attn_flops) / (ms * 1e-3) / 1e12
+    peak, kind = bf16_peak()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    for s in range(PREFILL_SEQ):
+        model.set_sequence(s)
+        model.decode_async(PREFILL_DECODE, int(np.argmax(logits[s])), PREFILL_TOK)
+    d1.record(stream)
+    torch.cuda.synchronize()
+    dms = d0.elapsed_time(d1)
+    model.set_sequence(0)
+    return {"workload": f"{PREFILL_SEQ} x {PREFILL_TOK} uniform random tokens (seed {PREFILL_SEED}) prefill, "
+                        f"then {PREFILL_DECODE} greedy decode steps per sequence (one sequence at a time)",
+            "prefill_ms": ms, "prefill_tok_s": rows / (ms * 1e-3),
+            "roofline": {"kernel": "prefill (k_gemm_bf16_tn dominant)", "bound": "tensor",
+                         "achieved": tflops, "peak": peak, "peak_kind": kind, "unit": "TFLOP/s",
+                         "frac": tflops / peak, "algorithmic_flops": lin_flops + attn_flops,
+                         "note": "algorithmic bf16-equivalent flops; the kernels issue 3x the linear MMA work "
+                                 "(two-part bf16 operands)"},
+            "decode_ms": dms, "decode_tok_s": PREFILL_SEQ * PREFILL_DECODE / (dms * 1e-3)}
+
+
 def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
     """GB/s of the W4A16 matvec kernel on the isolated 7B shapes, rotating over
     enough distinct weight copies to exceed 2x L2 so every launch reads HBM."""
@@ -246,6 +304,7 @@ def main() -> None:
     ap.add_argument("--shape", default=None, help="with --matvec: one shape, e.g. 32000x4096")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the isolated matvec shapes")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill leg")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling only: 7B shapes truncated to this many layers")
@@ -288,7 +347,9 @@ def main() -> None:
         return
 
     path = ensure_7b(rank, args.profile_layers)
-    model = A.Model(path, device=local)
+    do_prefill = not args.no_prefill and rank == 0
+    model = A.Model(path, device=local, max_batch=PREFILL_SEQ if do_prefill else 1,
+                    max_pos=PREFILL_TOK + PREFILL_DECODE if do_prefill else 0)
     L = model.config.n_layers
     stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{local}")
 
@@ -381,6 +442,8 @@ def main() -> None:
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     barrier()
 
+    prefill = prefill_leg(model, L, stream, local) if do_prefill else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and args.profile_layers <= 0:
         cb = cpu_reference_decode(path, 2, 1000, budget_s=20.0)
@@ -403,6 +466,7 @@ def main() -> None:
                     "d2h_bytes_per_step": vocab * 4},
             "cpu_baseline": cpu,
             "parity": parity,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     model.close()
