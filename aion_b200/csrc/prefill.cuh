@@ -26,14 +26,25 @@ __device__ __forceinline__ void split_store(__nv_bfloat16* row, int kp, int k, f
     row[kp + k] = lo;
     row[2 * kp + k] = hi;
 }
-// B operand row: [hi | hi | lo].
-__device__ __forceinline__ void split_store_b(__nv_bfloat16* row, int kp, int k, float v) {
-    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
-    row[k] = hi;
-    row[kp + k] = hi;
-    row[2 * kp + k] = lo;
+// Eight consecutive values k0..k0+7 (k0 % 8 == 0) of an A row ([hi|lo|hi])
+// or a B row ([hi|hi|lo]) as three 16-byte stores.
+template <bool B>
+__device__ __forceinline__ void split8_store(__nv_bfloat16* row, int kp, int k0, const float (&v)[8]) {
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        const float2 hf = __bfloat1622float2(h);
+        const __nv_bfloat162 l = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+        hi[i] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[i] = *reinterpret_cast<const uint32_t*>(&l);
+    }
+    const uint4 H = make_uint4(hi[0], hi[1], hi[2], hi[3]), Lo = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4*>(row + k0) = H;
+    *reinterpret_cast<uint4*>(row + kp + k0) = B ? H : Lo;
+    *reinterpret_cast<uint4*>(row + 2 * kp + k0) = B ? Lo : H;
 }
+
 
 // B operand of an int4 matrix: out[n][3*kp] for n < np (zero past the
 // matrix), from the tile layout of matvec.cuh.  One thread per (row, 8
@@ -45,9 +56,11 @@ __global__ void k_pf_dequant(MatDesc m, int np, int kp, __nv_bfloat16* out) {
         const int n = (int)(i / (kp / 8)), c8 = (int)(i % (kp / 8));
         const int k0 = c8 * 8;
         __nv_bfloat16* row = out + (size_t)n * 3 * kp;
+        float v[8];
         if (n >= m.d || k0 >= m.n) {
 #pragma unroll
-            for (int e = 0; e < 8; e++) split_store_b(row, kp, k0 + e, 0.0f);
+            for (int e = 0; e < 8; e++) v[e] = 0.0f;
+            split8_store<true>(row, kp, k0, v);
             continue;
         }
         const int g = k0 >> 5, j = (k0 & 31) >> 3;   // group, eighth of the group
@@ -61,9 +74,9 @@ __global__ void k_pf_dequant(MatDesc m, int np, int kp, __nv_bfloat16* out) {
 #pragma unroll
         for (int e = 0; e < 8; e++) {
             const uint32_t w = e < 4 ? w0 : w1;
-            const int q = (int)((w >> (8 * (e & 3) + shift)) & 0xF) - 8;
-            split_store_b(row, kp, k0 + e, (float)q * sc);
+            v[e] = (float)((int)((w >> (8 * (e & 3) + shift)) & 0xF) - 8) * sc;
         }
+        split8_store<true>(row, kp, k0, v);
     }
 }
 
@@ -87,7 +100,8 @@ __global__ void k_pf_norm_split(const float* x, const int* map, int mrows, int k
     const int m = blockIdx.x;
     __nv_bfloat16* row = out + (size_t)m * 3 * kp;
     if (m >= mrows) {
-        for (int i = threadIdx.x; i < kp; i += blockDim.x) split_store(row, kp, i, 0.0f);
+        const float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int i = 8 * threadIdx.x; i < kp; i += 8 * blockDim.x) split8_store<false>(row, kp, i, z);
         return;
     }
     const float* xr = x + (size_t)(map ? map[m] : m) * k;
@@ -99,8 +113,12 @@ __global__ void k_pf_norm_split(const float* x, const int* map, int mrows, int k
     float tot = 0.0f;
     for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
     const float ss = 1.0f / sqrtf(tot / (float)k + 1e-5f);
-    for (int i = threadIdx.x; i < kp; i += blockDim.x)
-        split_store(row, kp, i, i < k ? (xr[i] * ss) * w[i] : 0.0f);
+    for (int i = 8 * threadIdx.x; i < kp; i += 8 * blockDim.x) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[e] = i + e < k ? (xr[i + e] * ss) * w[i + e] : 0.0f;
+        split8_store<false>(row, kp, i, v);
+    }
 }
 
 // QKV output (ld columns per row) -> RoPE'd q rows, and K / V rows of each
@@ -238,14 +256,19 @@ __global__ void k_pf_residual(float* x, const float* c, int ldc, int mrows, int 
 __global__ void k_pf_swiglu_split(const float* c, int ldc, int mrows, int hidden, int kp, __nv_bfloat16* out) {
     const int m = blockIdx.x;
     __nv_bfloat16* row = out + (size_t)m * 3 * kp;
-    for (int j = threadIdx.x; j < kp; j += blockDim.x) {
-        float v = 0.0f;
-        if (m < mrows && j < hidden) {
-            const int col = 4 * (j >> 1) + (j & 1);
-            const float g = c[(size_t)m * ldc + col], u = c[(size_t)m * ldc + col + 2];
-            v = (g / (1.0f + expf(-g))) * u;
+    for (int j0 = 8 * threadIdx.x; j0 < kp; j0 += 8 * blockDim.x) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int j = j0 + e;
+            v[e] = 0.0f;
+            if (m < mrows && j < hidden) {
+                const int col = 4 * (j >> 1) + (j & 1);
+                const float g = c[(size_t)m * ldc + col], u = c[(size_t)m * ldc + col + 2];
+                v[e] = (g / (1.0f + expf(-g))) * u;
+            }
         }
-        split_store(row, kp, j, v);
+        split8_store<false>(row, kp, j0, v);
     }
 }
 
