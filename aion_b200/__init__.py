@@ -96,6 +96,8 @@ def lib() -> ctypes.CDLL:
         "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_set_sequence": (I32, [VP, I32]),
+        "aion_tp_handle": (I32, [VP, VP]),
+        "aion_tp_connect": (I32, [VP, VP]),
         "aion_quantize_activations": (I32, [VP, VP, VP, I64, VP]),
         "aion_quantize_buffer": (None, [VP, VP, VP, I64]),
         "aion_checkpoint_bytes": (I64, [P(I32), ctypes.c_int]),
@@ -166,7 +168,7 @@ class Model:
     reference (src/kernel_simd.c:941-1008), on one B200."""
 
     def __init__(self, path, device: int = 0, mode: str = "int4", max_pos: int = 0, use_graph: bool = True,
-                 max_batch: int = 1):
+                 max_batch: int = 1, tp_size: int = 1, tp_rank: int = 0):
         L = lib()
         o = Opts()
         L.aion_default_opts(ctypes.byref(o))
@@ -175,6 +177,8 @@ class Model:
         o.max_pos = max_pos
         o.use_graph = 1 if use_graph else 0
         o.max_batch = max_batch
+        o.tp_size = tp_size
+        o.tp_rank = tp_rank
         h = ctypes.c_void_p()
         _check(L.aion_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)))
         self._h = h
@@ -218,6 +222,17 @@ class Model:
         out = np.empty((t.shape[0], self.config.vocab_size), np.float32)
         _check(lib().aion_prefill(self._h, _ptr(t), t.shape[0], t.shape[1], _ptr(out)), self._h)
         return out
+
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-region handle, for every rank's tp_connect."""
+        buf = ctypes.create_string_buffer(64)
+        _check(lib().aion_tp_handle(self._h, buf), self._h)
+        return buf.raw
+
+    def tp_connect(self, handles) -> None:
+        """Maps the other ranks' exchange regions (handles in rank order)."""
+        blob = b"".join(handles)
+        _check(lib().aion_tp_connect(self._h, ctypes.create_string_buffer(blob, len(blob))), self._h)
 
     def set_sequence(self, seq: int) -> None:
         """Selects the sequence (KV cache) that forward / decode calls use."""

@@ -133,9 +133,13 @@ static cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Source rows hold src_G groups; the tiles take groups [src_g0, src_g0 + m.G)
+// of each (src_G = 0: the tiles' own width).
 static cudaError_t retile(const MatDesc& m, const float* scales, const uint8_t* packed, long long rows, int row_offset,
-                          int interleave, int slot, int inverse, cudaStream_t st) {
+                          int interleave, int slot, int inverse, cudaStream_t st, int src_G = 0, int src_g0 = 0) {
     RetileArgs a;
+    a.src_G = src_G > 0 ? src_G : m.G;
+    a.src_g0 = src_g0;
     a.src_scales = scales;
     a.src_packed = packed;
     a.m = m;
@@ -220,6 +224,16 @@ struct aion_ctx {
     int exp_n = 0;
     double exp_delta = 0.0;
     long long dim = 0, hidden = 0, L = 0, nh = 0, nkv = 0, vocab = 0, seq = 0, hs = 0, kv_dim = 0, kv_mul = 0;
+    // This rank's share under tensor parallelism (the full sizes when tp_n == 1).
+    int tp_n = 1, tp_rank = 0;
+    long long q_l = 0, kv_l = 0, hid_l = 0, nh_l = 0, vocab_l = 0, vocab_off = 0;
+    MatDesc cls;                   // classifier rows of this rank: a view of emb
+    unsigned char* xr = nullptr;   // exchange region (receive rows, keys, flags)
+    size_t xr_bytes = 0;
+    int xr_keys_off = 0, xr_flags_off = 0;
+    std::vector<unsigned char*> peers;           // exchange regions of every rank (IPC-mapped)
+    unsigned char** peers_dev = nullptr;         // the same pointers in device memory
+    bool tp_connected = false;
     int max_pos = 0;
     cudaStream_t stream = nullptr;
     uint8_t* arena = nullptr;
@@ -367,6 +381,10 @@ static void ctx_destroy(aion_ctx* c) {
     if (c->graph) cudaGraphDestroy(c->graph);
     if (c->arena) cudaFree(c->arena);
     if (c->exp_tab) cudaFree(c->exp_tab);
+    for (int j = 0; j < (int)c->peers.size(); j++)
+        if (j != c->tp_rank && c->peers[j]) cudaIpcCloseMemHandle(c->peers[j]);
+    if (c->peers_dev) cudaFree(c->peers_dev);
+    if (c->xr) cudaFree(c->xr);
     for (void* p : {(void*)c->pf.a, (void*)c->pf.b, (void*)c->pf.c, (void*)c->pf.x, (void*)c->pf.q,
                     (void*)c->pf.tok, (void*)c->pf.map})
         if (p) cudaFree(p);
@@ -411,13 +429,20 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.nops = c->nops;
     a.emb = c->emb;
     a.dim = (int)c->dim;
-    a.hidden = (int)c->hidden;
+    a.hidden = (int)c->hid_l;
     a.n_layers = (int)c->L;
-    a.n_heads = (int)c->nh;
+    a.n_heads = (int)c->nh_l;
     a.kv_mul = (int)c->kv_mul;
     a.head_size = (int)c->hs;
-    a.kv_dim = (int)c->kv_dim;
+    a.kv_dim = (int)c->kv_l;
     a.vocab = (int)c->vocab;
+    a.q_dim = (int)c->q_l;
+    a.tp_n = c->tp_n;
+    a.tp_rank = c->tp_rank;
+    a.vocab_off = (int)c->vocab_off;
+    a.tp_peers = c->peers_dev;
+    a.tp_keys_off = c->xr_keys_off;
+    a.tp_flags_off = c->xr_flags_off;
     a.max_pos = c->max_pos;
     a.rms_att = c->rms_att;
     a.rms_ffn = c->rms_ffn;
@@ -477,8 +502,12 @@ static aion_status build_graph(aion_ctx* c) {
 
 // Enqueues `steps` decode steps: one graph replay when steps == 1 and graphs
 // are on, else one launch that runs all steps.
+static aion_status tp_ready(aion_ctx* c);
+
 static aion_status enqueue_steps(aion_ctx* c, int steps) {
     if (steps <= 0) return AION_OK;
+    const aion_status ready = tp_ready(c);
+    if (ready != AION_OK) return ready;
     if (steps == 1 && c->opts.use_graph) {
         aion_status s = build_graph(c);
         if (s != AION_OK) return s;
@@ -630,19 +659,36 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         }
         c->max_chunks = (c->max_pos + kAttnUnit - 1) / kAttnUnit;
         const long long dim = c->dim, hid = c->hidden, L = c->L, kv = c->kv_dim;
+        const long long N = c->tp_n, R = c->tp_rank;
+        if (N > 1 && (c->nh % N || c->nkv % N || (dim / N) % 32 || (hid / N) % 32 || c->vocab % (N * kTR))) {
+            set_err(&c->err,
+                    "tensor parallelism over %lld ranks needs n_heads, n_kv_heads divisible by it, dim/%lld and "
+                    "hidden/%lld multiples of 32 and vocab a multiple of %lld", N, N, N, N * kTR);
+            s = AION_ERR_SHAPE;
+            break;
+        }
+        c->q_l = dim / N;
+        c->kv_l = kv / N;
+        c->hid_l = hid / N;
+        c->nh_l = c->nh / N;
+        c->vocab_l = c->vocab / N;
+        c->vocab_off = R * c->vocab_l;
+        const long long ql = c->q_l, kvl = c->kv_l, hl = c->hid_l;
 
-        // Matrix layouts (pointers filled below).
+        // Matrix layouts (pointers filled below).  Under tensor parallelism
+        // this rank holds wq/wk/wv/w1/w3 rows [R/N, (R+1)/N) of each and
+        // wo/w2 columns [R/N, (R+1)/N) (partial sums, summed across ranks).
         c->emb = make_desc(nullptr, c->vocab, (int)dim);
-        MatDesc dq = make_desc(nullptr, dim + 2 * kv, (int)dim), dwo = make_desc(nullptr, dim, (int)dim);
-        MatDesc d13 = make_desc(nullptr, 2 * hid, (int)dim), d2 = make_desc(nullptr, dim, (int)hid);
+        MatDesc dq = make_desc(nullptr, ql + 2 * kvl, (int)dim), dwo = make_desc(nullptr, dim, (int)ql);
+        MatDesc d13 = make_desc(nullptr, 2 * hl, (int)dim), d2 = make_desc(nullptr, dim, (int)hl);
 
         size_t bytes = align256(desc_bytes(c->emb));
         bytes += L * (align256(desc_bytes(dq)) + align256(desc_bytes(dwo)) + align256(desc_bytes(d13)) +
                       align256(desc_bytes(d2)));
         bytes += align256(L * dim * 4) * 2 + align256(dim * 4) + 2 * align256(c->seq * (c->hs / 2) * 4);
-        bytes += 2 * align256((size_t)c->nseq * L * c->max_pos * kv * 4);
-        bytes += 3 * align256(dim * 4) + align256(hid * 4) + align256(c->vocab * 4);
-        bytes += align256((size_t)c->nh * c->max_chunks * (c->hs + 4) * 4) + align256(c->nh * 4);
+        bytes += 2 * align256((size_t)c->nseq * L * c->max_pos * kvl * 4);
+        bytes += 3 * align256(dim * 4) + align256(hl * 4) + align256(c->vocab_l * 4);
+        bytes += align256((size_t)c->nh_l * c->max_chunks * (c->hs + 4) * 4) + align256(c->nh_l * 4);
         bytes += align256(sizeof(StepState)) + align256(8) + align256((size_t)c->max_pos * 4);
         bytes += align256((size_t)(4 * L + 1) * sizeof(OpDesc));
         c->max_tiles = std::max({c->emb.ntiles, dq.ntiles, dwo.ntiles, d13.ntiles, d2.ntiles});
@@ -652,6 +698,8 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         CK_RET(&c->err, cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream));
 
         c->emb.w = arena_take(c, desc_bytes(c->emb));
+        // Classifier rows of this rank: tiles [vocab_off / 16, ...) of the embedding.
+        c->cls = make_desc(c->emb.w + (size_t)(c->vocab_off / kTR) * c->emb.tile_bytes, c->vocab_l, (int)dim);
         c->qkv.assign(L, dq); c->wo.assign(L, dwo); c->w13.assign(L, d13); c->w2.assign(L, d2);
         for (long long l = 0; l < L; l++) {
             c->qkv[l].w = arena_take(c, desc_bytes(dq));
@@ -664,16 +712,16 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         c->rms_final = (float*)arena_take(c, dim * 4);
         c->freq_re = (float*)arena_take(c, c->seq * (c->hs / 2) * 4);
         c->freq_im = (float*)arena_take(c, c->seq * (c->hs / 2) * 4);
-        c->kv_seq = (size_t)L * c->max_pos * kv;
+        c->kv_seq = (size_t)L * c->max_pos * kvl;
         c->kcache = (float*)arena_take(c, (size_t)c->nseq * c->kv_seq * 4);
         c->vcache = (float*)arena_take(c, (size_t)c->nseq * c->kv_seq * 4);
         c->x = (float*)arena_take(c, dim * 4);
         c->q = (float*)arena_take(c, dim * 4);
         c->att = (float*)arena_take(c, dim * 4);
-        c->hb = (float*)arena_take(c, hid * 4);
-        c->logits = (float*)arena_take(c, c->vocab * 4);
-        c->attn_part = (float*)arena_take(c, (size_t)c->nh * c->max_chunks * (c->hs + 4) * 4);
-        c->attn_cnt = (int*)arena_take(c, c->nh * 4);
+        c->hb = (float*)arena_take(c, hl * 4);
+        c->logits = (float*)arena_take(c, c->vocab_l * 4);
+        c->attn_part = (float*)arena_take(c, (size_t)c->nh_l * c->max_chunks * (c->hs + 4) * 4);
+        c->attn_cnt = (int*)arena_take(c, c->nh_l * 4);
         c->step = (StepState*)arena_take(c, sizeof(StepState));
         c->argmax = (unsigned long long*)arena_take(c, 8);
         c->history = (int32_t*)arena_take(c, (size_t)c->max_pos * 4);
@@ -720,13 +768,16 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             off += count * 4;
             return r;
         };
-        auto per_layer = [&](long long rows, long long n, std::vector<MatDesc>* dst, int row_offset, int interleave,
-                             int slot) {
-            return [c, L, rows, n, dst, row_offset, interleave, slot](const float* sc, const uint8_t* pk) -> cudaError_t {
+        // Layer l's matrix in the file is [rows][n]; the tiles take rows
+        // [r0, r0 + take) and column groups [g0, g0 + tiles' width).
+        auto per_layer = [&](long long rows, long long n, long long r0, long long take, long long g0,
+                             std::vector<MatDesc>* dst, int row_offset, int interleave, int slot) {
+            return [c, L, rows, n, r0, take, g0, dst, row_offset, interleave, slot](const float* sc,
+                                                                                  const uint8_t* pk) -> cudaError_t {
                 for (long long l = 0; l < L; l++) {
-                    const long long e0 = l * rows * n;
-                    cudaError_t e = retile((*dst)[l], sc + e0 / 32, pk + e0 / 2, rows, row_offset, interleave, slot, 0,
-                                           c->stream);
+                    const long long e0 = l * rows * n + r0 * n;
+                    cudaError_t e = retile((*dst)[l], sc + e0 / 32, pk + e0 / 2, take, row_offset, interleave, slot, 0,
+                                           c->stream, (int)(n / 32), (int)g0);
                     if (e != cudaSuccess) return e;
                 }
                 return cudaSuccess;
@@ -737,14 +788,17 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
                  return e != cudaSuccess ? e : fill_pad(c->emb, c->stream);
              })) != AION_OK) break;
         if ((s = ftensor(L * dim, c->rms_att)) != AION_OK) break;
-        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, &c->qkv, 0, 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, &c->qkv, (int)dim, 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, &c->qkv, (int)(dim + kv), 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, &c->wo, 0, 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, R * ql, ql, 0, &c->qkv, 0, 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, R * kvl, kvl, 0, &c->qkv, (int)ql, 0, 0))) != AION_OK)
+            break;
+        if ((s = qtensor(L * dim * kv, per_layer(kv, dim, R * kvl, kvl, 0, &c->qkv, (int)(ql + kvl), 0, 0))) !=
+            AION_OK)
+            break;
+        if ((s = qtensor(L * dim * dim, per_layer(dim, dim, 0, dim, R * ql / 32, &c->wo, 0, 0, 0))) != AION_OK) break;
         if ((s = ftensor(L * dim, c->rms_ffn)) != AION_OK) break;
-        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, &c->w13, 0, 1, 0))) != AION_OK) break;
-        if ((s = qtensor(L * hid * dim, per_layer(dim, hid, &c->w2, 0, 0, 0))) != AION_OK) break;
-        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, &c->w13, 0, 1, 1))) != AION_OK) break;
+        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, R * hl, hl, 0, &c->w13, 0, 1, 0))) != AION_OK) break;
+        if ((s = qtensor(L * hid * dim, per_layer(dim, hid, 0, dim, R * hl / 32, &c->w2, 0, 0, 0))) != AION_OK) break;
+        if ((s = qtensor(L * dim * hid, per_layer(hid, dim, R * hl, hl, 0, &c->w13, 0, 1, 1))) != AION_OK) break;
         if ((s = ftensor(dim, c->rms_final)) != AION_OK) break;
         if ((s = ftensor(c->seq * (c->hs / 2), c->freq_re)) != AION_OK) break;
         if ((s = ftensor(c->seq * (c->hs / 2), c->freq_im)) != AION_OK) break;
@@ -764,7 +818,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             ops.push_back({c->w13[l], OP_W13, (int)l});
             ops.push_back({c->w2[l], OP_W2, (int)l});
         }
-        ops.push_back({c->emb, OP_CLS, 0});
+        ops.push_back({c->cls, OP_CLS, 0});
         for (const OpDesc& o : ops) max_chunk = std::max(max_chunk, max_chunk_bytes(o.m));
         c->nops = (int)ops.size();
         CK_RET(&c->err, cudaMemcpyAsync(c->ops, ops.data(), ops.size() * sizeof(OpDesc), cudaMemcpyHostToDevice,
@@ -814,8 +868,15 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
         delete c;
         return AION_ERR_ARG;
     }
-    if (c->opts.tp_size > 1) {
-        set_err(&c->err, "tp_size > 1 is not available in this build");
+    if (c->opts.tp_size < 1 || c->opts.tp_size > 64 || c->opts.tp_rank < 0 || c->opts.tp_rank >= c->opts.tp_size) {
+        set_err(&c->err, "tp_size %d / tp_rank %d out of range", c->opts.tp_size, c->opts.tp_rank);
+        delete c;
+        return AION_ERR_ARG;
+    }
+    c->tp_n = c->opts.tp_size;
+    c->tp_rank = c->opts.tp_rank;
+    if (c->tp_n > 1 && c->opts.max_batch > 1) {
+        set_err(&c->err, "max_batch > 1 (batched prefill) is not available with tensor parallelism");
         delete c;
         return AION_ERR_ARG;
     }
@@ -841,6 +902,23 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
         return AION_ERR_CUDA;
     }
     aion_status s = load_impl(c, path);
+    if (s == AION_OK && c->tp_n > 1) {
+        // Exchange region: receive rows [tp_n][dim] fp32, keys [tp_n] u64,
+        // flags [tp_n] u32; shared with the other ranks by aion_tp_connect.
+        const size_t recv = align256((size_t)c->tp_n * c->dim * 4), keys = align256((size_t)c->tp_n * 8);
+        c->xr_keys_off = (int)recv;
+        c->xr_flags_off = (int)(recv + keys);
+        c->xr_bytes = recv + keys + align256((size_t)c->tp_n * 4);
+        cudaError_t e2 = cudaMalloc(&c->xr, c->xr_bytes);
+        if (e2 == cudaSuccess) e2 = cudaMemset(c->xr, 0, c->xr_bytes);
+        if (e2 == cudaSuccess) e2 = cudaMalloc(&c->peers_dev, (size_t)c->tp_n * sizeof(unsigned char*));
+        if (e2 != cudaSuccess) {
+            set_err(&c->err, "exchange region: %s", cudaGetErrorString(e2));
+            s = cuda_status(e2);
+        }
+        c->peers.assign(c->tp_n, nullptr);
+        c->peers[c->tp_rank] = c->xr;
+    }
     if (s != AION_OK) {
         g_thread_err = c->err;
         ctx_destroy(c);
@@ -850,12 +928,54 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
     return AION_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Tensor parallelism: sharing the exchange regions between the ranks'
+// processes (no counterpart in the reference).
+// ---------------------------------------------------------------------------
+extern "C" AION_API aion_status aion_tp_handle(const aion_ctx* c, void* handle_out) {
+    if (!c || !handle_out || c->tp_n < 2) return AION_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    CK_RET(nullptr, cudaSetDevice(c->dev));
+    CK_RET(nullptr, cudaIpcGetMemHandle(&h, c->xr));
+    static_assert(sizeof(h) == AION_TP_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle_out, &h, sizeof(h));
+    return AION_OK;
+}
+
+extern "C" AION_API aion_status aion_tp_connect(aion_ctx* c, const void* handles) {
+    if (!c || !handles || c->tp_n < 2) return AION_ERR_ARG;
+    if (c->tp_connected) return AION_OK;
+    CK_RET(&c->err, cudaSetDevice(c->dev));
+    for (int j = 0; j < c->tp_n; j++) {
+        if (j == c->tp_rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const unsigned char*>(handles) + (size_t)j * AION_TP_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        CK_RET(&c->err, cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+        c->peers[j] = static_cast<unsigned char*>(p);
+    }
+    CK_RET(&c->err, cudaMemcpy(c->peers_dev, c->peers.data(), (size_t)c->tp_n * sizeof(unsigned char*),
+                               cudaMemcpyHostToDevice));
+    c->tp_connected = true;
+    return AION_OK;
+}
+
+static aion_status tp_ready(aion_ctx* c) {
+    if (c->tp_n > 1 && !c->tp_connected) {
+        set_err(&c->err, "tensor-parallel context not connected (aion_tp_connect)");
+        return AION_ERR_STATE;
+    }
+    return AION_OK;
+}
+
 static aion_status set_step(aion_ctx* c, int32_t token, int32_t pos) {
     memset(c->h_step, 0, sizeof(StepState));
     c->h_step->pos_next = pos;
     c->h_step->forced_token = token;
     // The pinned host buffer is reused: wait for the copy before returning.
-    CK_RET(&c->err, cudaMemcpyAsync(c->step, c->h_step, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    // The barrier and exchange counters stay (they only ever grow).
+    CK_RET(&c->err, cudaMemcpyAsync(c->step, c->h_step, offsetof(StepState, barrier), cudaMemcpyHostToDevice,
+                                    c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return AION_OK;
 }
@@ -872,7 +992,7 @@ extern "C" AION_API aion_status aion_forward(aion_ctx* c, int32_t token, int32_t
     if (s == AION_OK) s = enqueue_steps(c, 1);
     if (s != AION_OK) return s;
     if (logits_host)
-        CK_RET(&c->err, cudaMemcpyAsync(logits_host, c->logits, c->vocab * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK_RET(&c->err, cudaMemcpyAsync(logits_host, c->logits, c->vocab_l * 4, cudaMemcpyDeviceToHost, c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return check_device_error(c);
 }
@@ -993,6 +1113,10 @@ static aion_status pf_matmul(aion_ctx* c, const MatDesc& w, long long mpad, long
 extern "C" AION_API aion_status aion_prefill(aion_ctx* c, const int32_t* tokens, int32_t n_seq, int32_t n_tok,
                                              float* logits_host) {
     if (!c || !tokens || n_seq < 1 || n_tok < 1) return AION_ERR_ARG;
+    if (c->tp_n > 1) {
+        set_err(&c->err, "aion_prefill is not available with tensor parallelism");
+        return AION_ERR_STATE;
+    }
     if (n_seq > c->nseq || n_tok > c->max_pos) {
         set_err(&c->err, "aion_prefill: %d sequences x %d tokens exceed the context (%d sequences, %d positions)",
                 n_seq, n_tok, c->nseq, c->max_pos);

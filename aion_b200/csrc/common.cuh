@@ -28,7 +28,8 @@ struct StepState {
     int32_t token;
     int32_t error;
     uint32_t barrier;        // grid-barrier arrival counter of the persistent decode kernel
-    int32_t pad[2];
+    uint32_t tp_count;       // tensor parallelism: exchanges completed so far (same on every rank)
+    int32_t pad;
 };
 
 // Argmax key: (order-preserving float bits << 32) | (0xFFFFFFFF - index).
@@ -161,6 +162,14 @@ __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
 }
 __device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ int32_t ld_relaxed_i32(const int32_t* p) {
     int32_t v;

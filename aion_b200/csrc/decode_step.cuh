@@ -61,6 +61,16 @@ struct DecodeArgs {
     int P, slot_bytes, xbytes, xs_off;
     int ops_off;                   // shared-memory copy of ops[] (xbytes = ring offset)
     ExpTable exp_host;             // the host expf's deviations (W4A8), or empty
+    // Tensor parallelism over tp_n GPUs (tp_n == 1: off).  This rank holds
+    // q_dim query rows (n_heads heads, kv_dim K/V rows), hidden FFN rows and
+    // vocab rows [vocab_off, vocab_off + classifier rows); WO and W2 give
+    // partial sums over its slice of their inputs.  tp_peers[j] is rank j's
+    // exchange region (mapped into this process): recv fp32 [tp_n][dim],
+    // then keys u64 [tp_n] at tp_keys_off, flags u32 [tp_n] at tp_flags_off.
+    int q_dim;
+    int tp_n, tp_rank, vocab_off;
+    unsigned char* const* tp_peers;
+    int tp_keys_off, tp_flags_off;
 };
 
 // ---------------------------------------------------------------------------
@@ -462,7 +472,7 @@ struct DecodeEpi {
     // Split mode: rows [row0, row0 + rows) end on this CTA; WO / W2 fetch
     // their residual rows into shared memory while the op streams.
     __device__ __forceinline__ void prefetch(int row0, int rows, float* dst) {
-        if (op->kind != OP_WO && op->kind != OP_W2) return;
+        if ((op->kind != OP_WO && op->kind != OP_W2) || a->tp_n > 1) return;
         const int tid = threadIdx.x;
         if (4 * tid < rows) cp_async16(dst + 4 * tid, a->x + row0 + 4 * tid);
         pre = dst;
@@ -477,10 +487,10 @@ struct DecodeEpi {
             if (r0 >= d) break;
             const int hs = A.head_size;
             const size_t lkv = (size_t)op->layer * A.max_pos * A.kv_dim;
-            if (r0 < A.dim + A.kv_dim) {
+            if (r0 < A.q_dim + A.kv_dim) {
                 // RoPE on adjacent pairs (src/kernel_simd.c:1068-1085)
-                const bool is_q = r0 < A.dim;
-                const int base = is_q ? r0 : r0 - A.dim;
+                const bool is_q = r0 < A.q_dim;
+                const int base = is_q ? r0 : r0 - A.q_dim;
                 float out[kRB];
                 for (int r = 0; r < kRB; r += 2) {
                     const int hd = (base + r) % hs;
@@ -492,7 +502,7 @@ struct DecodeEpi {
                 float* dst = is_q ? A.q + base : A.kcache + lkv + (size_t)pos * A.kv_dim + base;
                 __stcg(reinterpret_cast<float4*>(dst), make_float4(out[0], out[1], out[2], out[3]));
             } else {
-                const int base = r0 - A.dim - A.kv_dim;
+                const int base = r0 - A.q_dim - A.kv_dim;
                 __stcg(reinterpret_cast<float4*>(A.vcache + lkv + (size_t)pos * A.kv_dim + base),
                        make_float4(v[0], v[1], v[2], v[3]));
             }
@@ -500,6 +510,16 @@ struct DecodeEpi {
         }
         case OP_WO:
         case OP_W2:
+            if (A.tp_n > 1) {
+                // Partial sums over this rank's slice of the input: into
+                // slot tp_rank of every rank's receive rows.
+                for (int j = 0; j < A.tp_n; j++) {
+                    float* recv = reinterpret_cast<float*>(A.tp_peers[j]) + (size_t)A.tp_rank * A.dim;
+                    for (int r = 0; r < kRB; r++)
+                        if (r0 + r < d) recv[r0 + r] = v[r];
+                }
+                break;
+            }
             for (int r = 0; r < kRB; r++)
                 if (r0 + r < d) {
                     const float xr = pre ? pre[r0 + r - pre_row0] : __ldcg(A.x + r0 + r);
@@ -523,7 +543,7 @@ struct DecodeEpi {
                     __stcg(A.logits + r0 + r, v[r]);
                     if (v[r] > best) {
                         best = v[r];
-                        best_i = (uint32_t)(r0 + r);
+                        best_i = (uint32_t)(A.vocab_off + r0 + r);
                     }
                 }
             break;
@@ -753,6 +773,49 @@ __device__ __forceinline__ void cta_argmax(unsigned long long* dst, float best, 
 }
 
 // ---------------------------------------------------------------------------
+// Tensor parallelism: the exchange after WO, W2 and the classifier.  Every
+// thread makes its remote stores of the op visible system-wide, the CTAs
+// meet at a grid barrier, CTA 0 raises this rank's flag to `count` in every
+// rank's region, and each CTA waits (bounded) until every rank's flag in its
+// own region reached `count`.
+// ---------------------------------------------------------------------------
+__device__ bool tp_exchange(const DecodeArgs& a, uint32_t& nbar, uint32_t count) {
+    __shared__ int s_xok;
+    __threadfence_system();
+    if (!grid_barrier(a.step, nbar)) return false;
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0)
+            for (int j = 0; j < a.tp_n; j++)
+                st_release_sys_u32(reinterpret_cast<uint32_t*>(a.tp_peers[j] + a.tp_flags_off) + a.tp_rank, count);
+        const uint32_t* fl = reinterpret_cast<const uint32_t*>(a.tp_peers[a.tp_rank] + a.tp_flags_off);
+        int ok = 1;
+        for (int j = 0; j < a.tp_n && ok; j++) {
+            uint32_t i = 0;
+            while ((int32_t)(ld_acquire_sys_u32(fl + j) - count) < 0)
+                if (++i > (1u << 24)) {
+                    ok = 0;
+                    break;
+                }
+        }
+        if (!ok) set_error(a.step, DEV_BARRIER_TIMEOUT);
+        s_xok = ok;
+    }
+    csync();
+    return s_xok != 0;
+}
+
+// x[row] += sum over ranks j (in rank order) of their partial rows; rows are
+// spread over all threads of the grid.
+__device__ void tp_reduce_residual(const DecodeArgs& a) {
+    const float* recv = reinterpret_cast<const float*>(a.tp_peers[a.tp_rank]);
+    for (int row = blockIdx.x * kThreads + threadIdx.x; row < a.dim; row += gridDim.x * kThreads) {
+        float sum = 0.0f;
+        for (int j = 0; j < a.tp_n; j++) sum += __ldcg(recv + (size_t)j * a.dim + row);
+        __stcg(a.x + row, __ldcg(a.x + row) + sum);
+    }
+}
+
+// ---------------------------------------------------------------------------
 // The persistent decode kernel.
 // ---------------------------------------------------------------------------
 // Warps 0..kWarps-1 compute; warp kWarps is the producer: its lane w walks compute warp
@@ -811,6 +874,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
         return;
     }
     Seq seq;   // unused: the producer warp issues every chunk
+    __shared__ uint32_t s_xcount;
+    if (threadIdx.x == 0) s_xcount = *reinterpret_cast<volatile uint32_t*>(&a.step->tp_count);
+    csync();
+    uint32_t xcount = s_xcount;   // tensor-parallel exchanges so far (identical on every rank)
 
     uint32_t nbar = 0;
     bool ok = true;
@@ -874,6 +941,34 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
                 break;
             }
             if (op.kind == OP_CLS) cta_argmax(a.argmax, epi.best, epi.best_i, red64);
+            if (a.tp_n > 1 && (op.kind == OP_WO || op.kind == OP_W2)) {
+                // Sum the ranks' partial rows into the residual stream.
+                if (!tp_exchange(a, nbar, ++xcount)) { ok = false; break; }
+                tp_reduce_residual(a);
+                if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                continue;
+            }
+            if (a.tp_n > 1 && op.kind == OP_CLS) {
+                // The greedy token is the largest of the ranks' argmax keys.
+                if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                if (blockIdx.x == 0 && threadIdx.x == 0) {
+                    const unsigned long long key = __ldcg(a.argmax);
+                    for (int j = 0; j < a.tp_n; j++)
+                        reinterpret_cast<unsigned long long*>(a.tp_peers[j] + a.tp_keys_off)[a.tp_rank] = key;
+                }
+                if (!tp_exchange(a, nbar, ++xcount)) { ok = false; break; }
+                if (blockIdx.x == 0 && threadIdx.x == 0) {
+                    const unsigned long long* keys =
+                        reinterpret_cast<const unsigned long long*>(a.tp_peers[a.tp_rank] + a.tp_keys_off);
+                    unsigned long long m = 0;
+                    for (int j = 0; j < a.tp_n; j++) {
+                        const unsigned long long k = __ldcg(keys + j);
+                        m = k > m ? k : m;
+                    }
+                    *a.argmax = m;
+                    __threadfence();
+                }
+            }
             if (oi == a.nops - 1 && step == a.steps - 1) break;   // nothing after the last classifier
             if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             if (op.kind == OP_QKV) {
@@ -896,6 +991,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
             }
         }
     }
+    if (blockIdx.x == 0 && threadIdx.x == 0) a.step->tp_count = xcount;
 }
 
 // ---------------------------------------------------------------------------

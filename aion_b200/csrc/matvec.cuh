@@ -377,12 +377,13 @@ __device__ __forceinline__ const uint8_t* chunk_src(const MatDesc& m, int tile, 
 //                rows holds w1[2j], w1[2j+1], w3[2j], w3[2j+1])
 // ---------------------------------------------------------------------------
 struct RetileArgs {
-    const float* src_scales;     // [rows][n/32]
-    const uint8_t* src_packed;   // [rows][n/2]
+    const float* src_scales;     // [rows][src_G] (source rows of src_G groups)
+    const uint8_t* src_packed;   // [rows][src_G * 16]
     MatDesc m;                   // destination layout (m.w is written)
     long long rows;
     int row_offset, interleave, slot;
     int inverse;                 // 1: tiles -> quantize.c layout
+    int src_G, src_g0;           // source groups per row, first source group of the tiles' columns
 };
 
 __device__ __forceinline__ int nib(const uint8_t* b, int e) { return (e & 1) ? (b[e >> 1] >> 4) : (b[e >> 1] & 0xF); }
@@ -399,8 +400,8 @@ __global__ void k_retile(RetileArgs a) {
         const int rr = (int)(R % kTR), lr = rr & 7, half = rr >> 3;
         uint8_t* gp = base + (R / kTR) * a.m.tile_bytes + (size_t)g * kGB;
         float* dsc = reinterpret_cast<float*>(gp + 256 + 8 * lr + 4 * half);
-        float* ssc = const_cast<float*>(a.src_scales) + r * G + g;
-        uint8_t* spk = const_cast<uint8_t*>(a.src_packed) + r * (a.m.n / 2) + 16 * g;
+        float* ssc = const_cast<float*>(a.src_scales) + r * a.src_G + a.src_g0 + g;
+        uint8_t* spk = const_cast<uint8_t*>(a.src_packed) + r * (16LL * a.src_G) + 16 * (a.src_g0 + g);
         if (!a.inverse) {
             uint8_t src[16];
             *reinterpret_cast<uint4*>(src) = *reinterpret_cast<const uint4*>(spk);

@@ -52,9 +52,9 @@ typedef struct aion_opts {
     int32_t mode;       /* AION_MODE_W4A16 (default) or AION_MODE_W4A8                */
     int32_t max_batch;  /* sequences (KV caches) held, for aion_prefill (default 1)      */
     int32_t max_pos;    /* KV positions allocated (0 = header seq_len; <= seq_len)     */
-    int32_t tp_size;    /* tensor-parallel ranks (default 1)                           */
+    int32_t tp_size;    /* tensor-parallel ranks, one process per GPU (default 1)      */
     int32_t tp_rank;    /* this rank, 0 <= tp_rank < tp_size                           */
-    const void* nccl_id;/* 128-byte ncclUniqueId shared by all ranks when tp_size > 1  */
+    const void* nccl_id;/* reserved (the ranks exchange IPC handles, see aion_tp_*)    */
     int32_t use_graph;  /* 1 (default): replay one CUDA graph per decode step          */
     int32_t reserved[7];
 } aion_opts;
@@ -107,6 +107,21 @@ AION_API void* aion_stream(const aion_ctx* ctx);
  * token < 0 takes the previous step's argmax; pos >= 0 sets the first
  * position, pos < 0 continues at the next one. */
 AION_API aion_status aion_decode_async(aion_ctx* ctx, int32_t token, int32_t pos, int32_t steps);
+
+/* ---------------------------------------------------------------------------
+ * Tensor parallelism (opts.tp_size > 1; one process per GPU of one node).
+ * Rank r holds rows [r/N, (r+1)/N) of wq, wk, wv, w1, w3 and of the
+ * classifier, and columns [r/N, (r+1)/N) of wo and w2; the decode kernel
+ * sums the ranks' wo / w2 partial rows and picks the argmax across ranks
+ * itself, over NVLink peer memory (the reference has no counterpart).
+ * Before the first decode call every rank passes every rank's handle, in
+ * rank order, to aion_tp_connect; the caller's launcher moves the handles
+ * between processes (AION_TP_HANDLE_BYTES each).  aion_forward then writes
+ * this rank's slice of the logits, vocab rows [r*vocab/N, (r+1)*vocab/N).
+ * ------------------------------------------------------------------------- */
+#define AION_TP_HANDLE_BYTES 64
+AION_API aion_status aion_tp_handle(const aion_ctx* ctx, void* handle_out);
+AION_API aion_status aion_tp_connect(aion_ctx* ctx, const void* handles);
 
 /* Copies the input tokens of positions [0, n) recorded on the device. */
 AION_API aion_status aion_tokens(aion_ctx* ctx, int32_t* out, int32_t n);
