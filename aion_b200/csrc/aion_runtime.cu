@@ -903,9 +903,9 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
     }
     aion_status s = load_impl(c, path);
     if (s == AION_OK && c->tp_n > 1) {
-        // Exchange region: receive rows [tp_n][dim] fp32, keys [tp_n] u64,
+        // Exchange region: tagged receive rows [2][tp_n][dim] u64, keys [tp_n] u64,
         // flags [tp_n] u32; shared with the other ranks by aion_tp_connect.
-        const size_t recv = align256((size_t)c->tp_n * c->dim * 4), keys = align256((size_t)c->tp_n * 8);
+        const size_t recv = align256((size_t)2 * c->tp_n * c->dim * 8), keys = align256((size_t)c->tp_n * 8);
         c->xr_keys_off = (int)recv;
         c->xr_flags_off = (int)(recv + keys);
         c->xr_bytes = recv + keys + align256((size_t)c->tp_n * 4);

@@ -171,6 +171,20 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Tagged 64-bit entries: fp32 bits in the low half, a counter in the high half.
+__device__ __forceinline__ uint64_t tag_pack(float v, uint32_t ep) {
+    return ((uint64_t)ep << 32) | (uint64_t)__float_as_uint(v);
+}
+__device__ __forceinline__ float tag_val(uint64_t t) { return __uint_as_float((uint32_t)t); }
+__device__ __forceinline__ uint32_t tag_ep(uint64_t t) { return (uint32_t)(t >> 32); }
 __device__ __forceinline__ int32_t ld_relaxed_i32(const int32_t* p) {
     int32_t v;
     asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");

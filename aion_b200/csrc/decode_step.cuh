@@ -65,8 +65,11 @@ struct DecodeArgs {
     // q_dim query rows (n_heads heads, kv_dim K/V rows), hidden FFN rows and
     // vocab rows [vocab_off, vocab_off + classifier rows); WO and W2 give
     // partial sums over its slice of their inputs.  tp_peers[j] is rank j's
-    // exchange region (mapped into this process): recv fp32 [tp_n][dim],
-    // then keys u64 [tp_n] at tp_keys_off, flags u32 [tp_n] at tp_flags_off.
+    // exchange region (mapped into this process): recv u64 [2][tp_n][dim]
+    // (partial rows tagged with the exchange count, slot count & 1), then
+    // keys u64 [tp_n] at tp_keys_off, flags u32 [tp_n] at tp_flags_off.  A
+    // rank rewrites a slot only after an exchange that needs this rank's
+    // next partial rows, so no row is overwritten before it is read.
     int q_dim;
     int tp_n, tp_rank, vocab_off;
     unsigned char* const* tp_peers;
@@ -466,6 +469,7 @@ struct DecodeEpi {
     const float* freq;             // shared: this position's RoPE cos[hs/2], sin[hs/2]
     float best;
     uint32_t best_i;
+    uint32_t xcount = 0;           // tensor parallelism: the tag of this op's partial rows
     const float* pre = nullptr;    // shared: residual rows [pre_row0, ...) fetched ahead
     int pre_row0 = 0;
 
@@ -511,12 +515,14 @@ struct DecodeEpi {
         case OP_WO:
         case OP_W2:
             if (A.tp_n > 1) {
-                // Partial sums over this rank's slice of the input: into
-                // slot tp_rank of every rank's receive rows.
+                // Partial sums over this rank's slice of the input, tagged
+                // with the exchange count: into slot tp_rank of every rank's
+                // receive rows (one 8-byte store each, read whole).
                 for (int j = 0; j < A.tp_n; j++) {
-                    float* recv = reinterpret_cast<float*>(A.tp_peers[j]) + (size_t)A.tp_rank * A.dim;
+                    uint64_t* recv = reinterpret_cast<uint64_t*>(A.tp_peers[j]) +
+                                     ((size_t)(xcount & 1u) * A.tp_n + A.tp_rank) * A.dim;
                     for (int r = 0; r < kRB; r++)
-                        if (r0 + r < d) recv[r0 + r] = v[r];
+                        if (r0 + r < d) st_relaxed_sys_u64(recv + r0 + r, tag_pack(v[r], xcount));
                 }
                 break;
             }
@@ -779,24 +785,27 @@ __device__ __forceinline__ void cta_argmax(unsigned long long* dst, float best, 
 // rank's region, and each CTA waits (bounded) until every rank's flag in its
 // own region reached `count`.
 // ---------------------------------------------------------------------------
+// The threads that stored to peers fence those stores (system scope) right
+// after them; the flags are polled with plain volatile loads and one
+// system-scope fence follows the last one.
 __device__ bool tp_exchange(const DecodeArgs& a, uint32_t& nbar, uint32_t count) {
     __shared__ int s_xok;
-    __threadfence_system();
     if (!grid_barrier(a.step, nbar)) return false;
     if (threadIdx.x == 0) {
         if (blockIdx.x == 0)
             for (int j = 0; j < a.tp_n; j++)
                 st_release_sys_u32(reinterpret_cast<uint32_t*>(a.tp_peers[j] + a.tp_flags_off) + a.tp_rank, count);
-        const uint32_t* fl = reinterpret_cast<const uint32_t*>(a.tp_peers[a.tp_rank] + a.tp_flags_off);
+        const volatile uint32_t* fl = reinterpret_cast<const volatile uint32_t*>(a.tp_peers[a.tp_rank] + a.tp_flags_off);
         int ok = 1;
         for (int j = 0; j < a.tp_n && ok; j++) {
             uint32_t i = 0;
-            while ((int32_t)(ld_acquire_sys_u32(fl + j) - count) < 0)
+            while ((int32_t)(fl[j] - count) < 0)
                 if (++i > (1u << 24)) {
                     ok = 0;
                     break;
                 }
         }
+        __threadfence_system();
         if (!ok) set_error(a.step, DEV_BARRIER_TIMEOUT);
         s_xok = ok;
     }
@@ -804,15 +813,30 @@ __device__ bool tp_exchange(const DecodeArgs& a, uint32_t& nbar, uint32_t count)
     return s_xok != 0;
 }
 
-// x[row] += sum over ranks j (in rank order) of their partial rows; rows are
-// spread over all threads of the grid.
-__device__ void tp_reduce_residual(const DecodeArgs& a) {
-    const float* recv = reinterpret_cast<const float*>(a.tp_peers[a.tp_rank]);
-    for (int row = blockIdx.x * kThreads + threadIdx.x; row < a.dim; row += gridDim.x * kThreads) {
+// x[row] += sum over ranks j (in rank order) of their partial rows, each
+// read once its tag shows exchange `count` (bounded wait); rows are spread
+// over all threads of the grid.  False if a wait gave up.
+__device__ bool tp_reduce_residual(const DecodeArgs& a, uint32_t count) {
+    const uint64_t* recv =
+        reinterpret_cast<const uint64_t*>(a.tp_peers[a.tp_rank]) + (size_t)(count & 1u) * a.tp_n * a.dim;
+    bool ok = true;
+    for (int row = blockIdx.x * kThreads + threadIdx.x; row < a.dim && ok; row += gridDim.x * kThreads) {
         float sum = 0.0f;
-        for (int j = 0; j < a.tp_n; j++) sum += __ldcg(recv + (size_t)j * a.dim + row);
+        for (int j = 0; j < a.tp_n && ok; j++) {
+            uint64_t t = ld_relaxed_sys_u64(recv + (size_t)j * a.dim + row);
+            for (uint32_t i = 0; tag_ep(t) != count; i++) {
+                if (i > (1u << 22)) {
+                    ok = false;
+                    break;
+                }
+                t = ld_relaxed_sys_u64(recv + (size_t)j * a.dim + row);
+            }
+            sum += tag_val(t);
+        }
         __stcg(a.x + row, __ldcg(a.x + row) + sum);
     }
+    if (!ok) set_error(a.step, DEV_BARRIER_TIMEOUT);
+    return ok;
 }
 
 // ---------------------------------------------------------------------------
@@ -934,6 +958,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
             build_input<MODE>(xf, xs, src, op.m.n, nw, red);
             csync();
             DecodeEpi epi{&a, &op, pos, s_freq, -1e9f, 0u};
+            if (a.tp_n > 1 && (op.kind == OP_WO || op.kind == OP_W2)) epi.xcount = ++xcount;
             if (!run_op<MODE, true>(op.m, ring, ring_base, seq, ops, a.nops, a.steps, xf, xs, os, a.split_part, a.split_cnt,
                               epi)) {
                 set_error(a.step, DEV_COPY_TIMEOUT);
@@ -943,8 +968,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
             if (op.kind == OP_CLS) cta_argmax(a.argmax, epi.best, epi.best_i, red64);
             if (a.tp_n > 1 && (op.kind == OP_WO || op.kind == OP_W2)) {
                 // Sum the ranks' partial rows into the residual stream.
-                if (!tp_exchange(a, nbar, ++xcount)) { ok = false; break; }
-                tp_reduce_residual(a);
+                if (csync_or(!tp_reduce_residual(a, epi.xcount))) { ok = false; break; }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
                 continue;
             }
@@ -955,6 +979,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
                     const unsigned long long key = __ldcg(a.argmax);
                     for (int j = 0; j < a.tp_n; j++)
                         reinterpret_cast<unsigned long long*>(a.tp_peers[j] + a.tp_keys_off)[a.tp_rank] = key;
+                    __threadfence_system();
                 }
                 if (!tp_exchange(a, nbar, ++xcount)) { ok = false; break; }
                 if (blockIdx.x == 0 && threadIdx.x == 0) {

@@ -26,6 +26,9 @@ same model (32 sequences x 512 uniform random tokens, seed 2, through every
 layer at once on the tensor cores, then 128 greedy decode steps per
 sequence), with its own roofline against the measured bf16 peak
 (--no-prefill skips it).
+--tp13b runs the 13B-shape model (dim 5120, hidden 13824, 40 layers, seed 3)
+tensor-parallel over the N ranks of the launch (one process per GPU): greedy
+decode of a 256-token workload from BOS, one sequence, "scaling": "strong".
 --profile-layers L runs the same path on a 7B-shape checkpoint truncated to
 L layers (same seed and shapes; for ncu captures that must stay small, never
 for the reported metric).
@@ -49,6 +52,9 @@ sys.path.insert(0, str(ROOT))
 
 CFG_7B = (4096, 11008, 32, 32, 32, 32000, 2048)
 SEED_7B = 1
+CFG_13B = (5120, 13824, 40, 40, 40, 32000, 2048)
+SEED_13B = 3
+TP_TOKENS = 256
 BOS = 1
 WORKLOAD_TOKENS = 512
 WEIGHT_BYTES_PER_TOKEN = 4_129_423_360          # 0.625 B x 6,607,077,376 weights
@@ -100,6 +106,21 @@ def ensure_7b(rank: int, layers: int = 0) -> Path:
     if rank == 0 and not done.exists():
         tmp = path.with_suffix(".tmp")
         A.synth_checkpoint(tmp, cfg, SEED_7B, int4=True)
+        tmp.rename(path)
+        done.write_text("ok")
+    while not done.exists():
+        time.sleep(1.0)
+    return path
+
+
+def ensure_13b(rank: int) -> Path:
+    """Writes the seeded 13B int4 checkpoint once per host (rank 0)."""
+    import aion_b200 as A
+    path = ckpt_dir() / "llama2_13b_seed3.int4"
+    done = path.with_suffix(".done")
+    if rank == 0 and not done.exists():
+        tmp = path.with_suffix(".tmp")
+        A.synth_checkpoint(tmp, CFG_13B, SEED_13B, int4=True)
         tmp.rename(path)
         done.write_text("ok")
     while not done.exists():
@@ -294,6 +315,58 @@ def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
     return out
 
 
+def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
+    """13B-shape decode, tensor-parallel over the launch's ranks."""
+    import torch
+    import aion_b200 as A
+    path = ensure_13b(rank)
+    barrier()
+    model = A.Model(path, device=local, tp_size=world, tp_rank=rank, max_pos=TP_TOKENS)
+    if world > 1:
+        handles = [None] * world
+        pg.all_gather_object(handles, model.tp_handle())
+        model.tp_connect(handles)
+    stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{local}")
+    steps = min(args.steps, TP_TOKENS - args.warmup)
+    model.decode_async(args.warmup, BOS, 0)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    model.decode_async(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    toks = model.tokens(args.warmup + steps)
+    dim, hid, L, vocab = CFG_13B[0], CFG_13B[1], CFG_13B[2], CFG_13B[5]
+    wbytes = int(0.625 * (L * (4 * dim * dim + 3 * dim * hid) + vocab * dim)) // world
+    gbs = wbytes * steps / (ms * 1e-3) / 1e9
+    peak, kind = hbm_peak()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "Llama-2-13B int4 decode tok/s (batch 1, tensor-parallel)", "value": steps / (ms * 1e-3),
+            "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "s4 weights x s8 activation digits (int32 tensor-core dot), fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": f"llama2-13b-shape W4A16 greedy decode, batch 1, {TP_TOKENS}-token workload",
+                       "dim": dim, "hidden": hid, "layers": L, "vocab": vocab, "seed": SEED_13B,
+                       "parallelism": f"tp{world}"},
+            "roofline": {"kernel": "k_decode<W4A16> (persistent decode, in-kernel NVLink exchange)", "bound": "hbm",
+                         "achieved": gbs, "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                         "frac": gbs / peak, "bytes_per_token_per_gpu": wbytes},
+            "gpu_launches": 1, "clocks": clk,
+            "token_stream_head": toks[:16]}), flush=True)
+    model.close()
+    if pg:
+        pg.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -306,6 +379,7 @@ def main() -> None:
     ap.add_argument("--no-matvec", action="store_true", help="skip the isolated matvec shapes")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill leg")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
+    ap.add_argument("--tp13b", action="store_true", help="13B shape, tensor-parallel over the launch's ranks")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling only: 7B shapes truncated to this many layers")
     args = ap.parse_args()
@@ -338,6 +412,10 @@ def main() -> None:
         t = torch.tensor([v], device=f"cuda:{local}", dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item())
+
+    if args.tp13b:
+        run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks)
+        return
 
     if args.matvec:
         shapes = [tuple(int(v) for v in args.shape.split("x"))] if args.shape else None
