@@ -97,6 +97,7 @@ def lib() -> ctypes.CDLL:
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_set_sequence": (I32, [VP, I32]),
         "aion_tp_handle": (I32, [VP, VP]),
+        "aion_quantize_buffer_dev": (I32, [VP, VP, VP, I64, VP]),
         "aion_tp_connect": (I32, [VP, VP]),
         "aion_quantize_activations": (I32, [VP, VP, VP, I64, VP]),
         "aion_quantize_buffer": (None, [VP, VP, VP, I64]),

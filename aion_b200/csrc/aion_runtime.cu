@@ -1503,6 +1503,24 @@ extern "C" AION_API aion_status aion_gemm_bf16_tn(const void* a_dev, const void*
     return s;
 }
 
+extern "C" AION_API aion_status aion_quantize_buffer_dev(const float* in_dev, uint8_t* packed_dev, float* scales_dev,
+                                                         int64_t n, void* stream) {
+    if (!in_dev || !packed_dev || !scales_dev || n < 0 || n % 32) {
+        set_err(nullptr, "aion_quantize_buffer_dev: null pointer, or n not a multiple of 32");
+        return AION_ERR_ARG;
+    }
+    if (((uintptr_t)in_dev & 15) || ((uintptr_t)packed_dev & 15) || ((uintptr_t)scales_dev & 3)) {
+        set_err(nullptr, "aion_quantize_buffer_dev: in and packed must be 16-byte aligned, scales 4-byte aligned");
+        return AION_ERR_ARG;
+    }
+    if (n == 0) return AION_OK;
+    const long long groups = n / 32;
+    const int grid = (int)std::min<long long>((groups + 255) / 256, 148LL * 16);
+    k_quantize_groups<<<grid, 256, 0, (cudaStream_t)stream>>>(in_dev, packed_dev, scales_dev, groups);
+    CK_RET(nullptr, cudaGetLastError());
+    return AION_OK;
+}
+
 extern "C" AION_API aion_status aion_quantize_activations(const float* x, int8_t* qx, float* xs, int64_t n, void* stream) {
     if (!x || !qx || !xs || n <= 0 || n % 32) {
         set_err(nullptr, "aion_quantize_activations: invalid arguments (n must be a positive multiple of 32)");

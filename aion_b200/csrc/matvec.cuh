@@ -431,6 +431,51 @@ __global__ void k_retile(RetileArgs a) {
     }
 }
 
+// quantize_buffer (quantize.c:59-109) on the device, bit for bit: per group
+// of 32 values scale = max|w| / 7 (0 becomes 1.0), q = clamp(roundf(w *
+// (1 / scale)), -7, 7) stored as q + 8, even element in the low nibble.
+// One thread per group (its 128 input bytes are whole cache lines).
+__global__ void k_quantize_groups(const float* in, uint8_t* packed, float* scales, long long groups) {
+    for (long long g = blockIdx.x * (long long)blockDim.x + threadIdx.x; g < groups;
+         g += (long long)gridDim.x * blockDim.x) {
+        float w[32];
+        const float4* src = reinterpret_cast<const float4*>(in + g * 32);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float4 v = __ldcs(src + i);
+            w[4 * i] = v.x;
+            w[4 * i + 1] = v.y;
+            w[4 * i + 2] = v.z;
+            w[4 * i + 3] = v.w;
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const float a = fabsf(w[i]);
+            if (a > amax) amax = a;
+        }
+        float scale = __fdiv_rn(amax, 7.0f);
+        if (scale == 0.0f) scale = 1.0f;
+        scales[g] = scale;
+        const float inv = __fdiv_rn(1.0f, scale);
+        uint32_t words[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            uint32_t wd = 0;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int i = 8 * k + 2 * b;
+                int q0 = (int)roundf(__fmul_rn(w[i], inv)), q1 = (int)roundf(__fmul_rn(w[i + 1], inv));
+                q0 = q0 < -7 ? -7 : (q0 > 7 ? 7 : q0);
+                q1 = q1 < -7 ? -7 : (q1 > 7 ? 7 : q1);
+                wd |= (uint32_t)(((q0 + 8) & 0xF) | (((q1 + 8) & 0xF) << 4)) << (8 * b);
+            }
+            words[k] = wd;
+        }
+        *reinterpret_cast<uint4*>(packed + g * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+    }
+}
+
 // Padding rows of the last tile: scale 0, nibbles 8 (q = 0).
 __global__ void k_fill_pad(MatDesc m) {
     const long long rows_pad = (long long)m.ntiles * kTR;

@@ -205,6 +205,11 @@ AION_API aion_status aion_quantize_activations(const float* x_dev, int8_t* qx_de
  * Checkpoint tools (host)
  * ------------------------------------------------------------------------- */
 
+/* quantize_buffer (quantize.c:59-109) on the device, bit-exact with it:
+ * in_dev[n] fp32 -> packed_dev[n/2], scales_dev[n/32] (device memory;
+ * n a multiple of 32, in and packed 16-byte aligned). */
+AION_API aion_status aion_quantize_buffer_dev(const float* in_dev, uint8_t* packed_dev, float* scales_dev, int64_t n,
+                                              void* stream);
 /* quantize_buffer (quantize.c:59-109) with 64-bit element counts. */
 AION_API void aion_quantize_buffer(const float* in, uint8_t* packed, float* scales, int64_t n);
 /* Byte size of a checkpoint for a 7-int header, fp32 (int4 = 0) or int4. */
