@@ -97,6 +97,7 @@ def lib() -> ctypes.CDLL:
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_set_sequence": (I32, [VP, I32]),
         "aion_tp_handle": (I32, [VP, VP]),
+        "aion_tp_plan": (I32, [P(Config), I32, I32, P(I64)]),
         "aion_quantize_buffer_dev": (I32, [VP, VP, VP, I64, VP]),
         "aion_tp_connect": (I32, [VP, VP]),
         "aion_quantize_activations": (I32, [VP, VP, VP, I64, VP]),
@@ -164,6 +165,15 @@ def quantize_buffer(w: np.ndarray):
 # ---------------------------------------------------------------------------
 # Model level
 # ---------------------------------------------------------------------------
+def tp_plan(cfg7, tp_size: int, tp_rank: int) -> dict:
+    """Rows and columns that rank tp_rank of tp_size holds (aion_tp_plan)."""
+    c = Config(*cfg7)
+    out = (ctypes.c_int64 * 9)()
+    _check(lib().aion_tp_plan(ctypes.byref(c), tp_size, tp_rank, out))
+    keys = ["q0", "q", "kv0", "kv", "hid0", "hid", "vocab0", "vocab", "heads"]
+    return dict(zip(keys, list(out)))
+
+
 class Model:
     """A device-resident int4 model: load_checkpoint_int4 + RunState of the
     reference (src/kernel_simd.c:941-1008), on one B200."""

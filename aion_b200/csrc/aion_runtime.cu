@@ -659,20 +659,21 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         }
         c->max_chunks = (c->max_pos + kAttnUnit - 1) / kAttnUnit;
         const long long dim = c->dim, hid = c->hidden, L = c->L, kv = c->kv_dim;
-        const long long N = c->tp_n, R = c->tp_rank;
-        if (N > 1 && (c->nh % N || c->nkv % N || (dim / N) % 32 || (hid / N) % 32 || c->vocab % (N * kTR))) {
+        const long long R = c->tp_rank;
+        int64_t plan[AION_TP_PLAN_FIELDS];
+        if (aion_tp_plan(&c->cfg, c->tp_n, c->tp_rank, plan) != AION_OK) {
             set_err(&c->err,
-                    "tensor parallelism over %lld ranks needs n_heads, n_kv_heads divisible by it, dim/%lld and "
-                    "hidden/%lld multiples of 32 and vocab a multiple of %lld", N, N, N, N * kTR);
+                    "tensor parallelism over %d ranks needs n_heads, n_kv_heads divisible by it, dim/%d and "
+                    "hidden/%d multiples of 32 and vocab a multiple of %d", c->tp_n, c->tp_n, c->tp_n, c->tp_n * kTR);
             s = AION_ERR_SHAPE;
             break;
         }
-        c->q_l = dim / N;
-        c->kv_l = kv / N;
-        c->hid_l = hid / N;
-        c->nh_l = c->nh / N;
-        c->vocab_l = c->vocab / N;
-        c->vocab_off = R * c->vocab_l;
+        c->q_l = plan[1];
+        c->kv_l = plan[3];
+        c->hid_l = plan[5];
+        c->vocab_off = plan[6];
+        c->vocab_l = plan[7];
+        c->nh_l = plan[8];
         const long long ql = c->q_l, kvl = c->kv_l, hl = c->hid_l;
 
         // Matrix layouts (pointers filled below).  Under tensor parallelism
@@ -929,9 +930,22 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
 }
 
 // ---------------------------------------------------------------------------
-// Tensor parallelism: sharing the exchange regions between the ranks'
-// processes (no counterpart in the reference).
+// Tensor parallelism: the shard plan, and sharing the exchange regions
+// between the ranks' processes (no counterpart in the reference).
 // ---------------------------------------------------------------------------
+extern "C" AION_API aion_status aion_tp_plan(const aion_config* cfg, int32_t tp_size, int32_t tp_rank, int64_t* out) {
+    if (!cfg || !out || tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size || cfg->n_heads <= 0 || cfg->n_kv_heads <= 0)
+        return AION_ERR_ARG;
+    const long long N = tp_size, R = tp_rank, dim = cfg->dim, hid = cfg->hidden_dim, nh = cfg->n_heads,
+                    nkv = cfg->n_kv_heads, vocab = cfg->vocab_size < 0 ? -(long long)cfg->vocab_size : cfg->vocab_size;
+    const long long kv = dim * nkv / nh;
+    if (N > 1 && (nh % N || nkv % N || (dim / N) % 32 || dim % N || (hid / N) % 32 || hid % N || vocab % (N * kTR)))
+        return AION_ERR_SHAPE;
+    const long long ql = dim / N, kvl = kv / N, hl = hid / N, vl = vocab / N;
+    const int64_t v[AION_TP_PLAN_FIELDS] = {R * ql, ql, R * kvl, kvl, R * hl, hl, R * vl, vl, nh / N};
+    memcpy(out, v, sizeof(v));
+    return AION_OK;
+}
 extern "C" AION_API aion_status aion_tp_handle(const aion_ctx* c, void* handle_out) {
     if (!c || !handle_out || c->tp_n < 2) return AION_ERR_ARG;
     cudaIpcMemHandle_t h;

@@ -120,6 +120,13 @@ AION_API aion_status aion_decode_async(aion_ctx* ctx, int32_t token, int32_t pos
  * this rank's slice of the logits, vocab rows [r*vocab/N, (r+1)*vocab/N).
  * ------------------------------------------------------------------------- */
 #define AION_TP_HANDLE_BYTES 64
+/* The rows and columns rank tp_rank holds: out[0..8] = first query row /
+ * query rows (of wq; also the columns of wo), first K/V row / K/V rows (of
+ * wk, wv), first hidden row / hidden rows (of w1, w3; also the columns of
+ * w2), first vocab row / vocab rows (of the classifier), heads.
+ * AION_ERR_SHAPE when the shape does not shard over tp_size ranks. */
+#define AION_TP_PLAN_FIELDS 9
+AION_API aion_status aion_tp_plan(const aion_config* cfg, int32_t tp_size, int32_t tp_rank, int64_t* out);
 AION_API aion_status aion_tp_handle(const aion_ctx* ctx, void* handle_out);
 AION_API aion_status aion_tp_connect(aion_ctx* ctx, const void* handles);
 

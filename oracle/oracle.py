@@ -56,6 +56,7 @@ class Oracle:
             "orc_reset": (None, [_P]),
             "orc_tensor": (ctypes.c_int, [_P, ctypes.c_int, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
             "orc_forward": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+            "orc_fp32_tensor": (_P, [_P, ctypes.c_int]),
             "orc_argmax": (ctypes.c_int, [_P, _I64, _P]),
             "orc_generate": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
         }
@@ -99,6 +100,12 @@ class Oracle:
         o = np.empty_like(x)
         self.L.orc_rmsnorm(_np(o), _np(x), _np(w), x.size)
         return o
+
+    def dequant(self, scales, packed, n: int) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.L.orc_dequant(_np(out), _np(np.ascontiguousarray(scales, np.float32)),
+                           _np(np.ascontiguousarray(packed, np.uint8)), n)
+        return out
 
     def open(self, path) -> "OracleModel":
         return OracleModel(self, path)
@@ -153,6 +160,14 @@ class OracleModel:
         p = np.ctypeslib.as_array(ctypes.cast(pp.value + layer_elems // 2, ctypes.POINTER(ctypes.c_uint8)),
                                   (count // 2,))
         return s.copy(), p.copy()
+
+    def fp32_tensor(self, which: int, count: int) -> np.ndarray:
+        """Copy of the first `count` floats of fp32 tensor `which` (0 rms_att,
+        1 rms_ffn, 2 rms_final, 3 freq_re, 4 freq_im)."""
+        ptr = self.o.L.orc_fp32_tensor(self.h, which)
+        if not ptr:
+            raise ValueError("bad tensor index")
+        return np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_float)), (count,)).copy()
 
 
 class Reference:
