@@ -95,6 +95,7 @@ def lib() -> ctypes.CDLL:
         "aion_matvec_w4a16_static": (I32, [VP, VP, VP, VP]),
         "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
+        "aion_decode_batch": (I32, [VP, I32, I32, VP, VP, VP, VP]),
         "aion_set_sequence": (I32, [VP, I32]),
         "aion_tp_handle": (I32, [VP, VP]),
         "aion_tp_plan": (I32, [P(Config), I32, I32, P(I64)]),
@@ -233,6 +234,21 @@ class Model:
         out = np.empty((t.shape[0], self.config.vocab_size), np.float32)
         _check(lib().aion_prefill(self._h, _ptr(t), t.shape[0], t.shape[1], _ptr(out)), self._h)
         return out
+
+    def decode_batch(self, first_tokens, pos0, steps: int, want_logits: bool = False):
+        """Lock-step greedy decode of sequences 0..n-1 from first_tokens[b] at
+        positions pos0[b]; returns (tokens[steps + 1][n], logits[n][vocab] of
+        the last step or None).  Row i of tokens holds step i's inputs, the
+        last row the picks after the last step."""
+        f = np.ascontiguousarray(first_tokens, dtype=np.int32).ravel()
+        p = np.ascontiguousarray(pos0, dtype=np.int32).ravel()
+        if f.size != p.size:
+            raise ValueError("first_tokens and pos0 differ in length")
+        toks = np.empty((steps + 1, f.size), np.int32)
+        lg = np.empty((f.size, self.config.vocab_size), np.float32) if want_logits else None
+        _check(lib().aion_decode_batch(self._h, f.size, steps, _ptr(f), _ptr(p), _ptr(toks),
+                                       _ptr(lg) if lg is not None else None), self._h)
+        return toks, lg
 
     def tp_handle(self) -> bytes:
         """This rank's exchange-region handle, for every rank's tp_connect."""

@@ -26,6 +26,7 @@
 #include <cudaTypedefs.h>
 
 #include "../../include/aion.h"
+#include "decode_batch.cuh"
 #include "decode_step.cuh"
 #include "gemm_tc.cuh"
 #include "prefill.cuh"
@@ -220,6 +221,20 @@ struct aion_ctx {
         int* map = nullptr;
         size_t a_cap = 0, b_cap = 0, c_cap = 0, x_cap = 0, q_cap = 0, tok_cap = 0, map_cap = 0;
     } pf;
+    struct BatchBufs {             // lock-step batched decode, allocated on first use
+        float *x = nullptr, *q = nullptr, *att = nullptr, *hb = nullptr, *logits = nullptr;
+        float *part = nullptr, *ssq = nullptr, *attn_part = nullptr;
+        int* attn_cnt = nullptr;
+        unsigned long long* argmax = nullptr;
+        int32_t *first = nullptr, *pos0 = nullptr, *tokens = nullptr;
+        size_t part_cap = 0, tok_cap = 0;
+        int nb = 0;                // sequences the fixed buffers hold
+        struct Plan {
+            BOpDesc* ops = nullptr;
+            int P = 0, fac_off = 0, ring_off = 0, ops_off = 0, total = 0;
+            size_t part_floats = 0;
+        } plan[kBMaxSeq / 8 + 1];
+    } bt;
     uint32_t* exp_tab = nullptr;   // W4A8: inputs where the host expf is not correctly rounded
     int exp_n = 0;
     double exp_delta = 0.0;
@@ -388,6 +403,12 @@ static void ctx_destroy(aion_ctx* c) {
     for (void* p : {(void*)c->pf.a, (void*)c->pf.b, (void*)c->pf.c, (void*)c->pf.x, (void*)c->pf.q,
                     (void*)c->pf.tok, (void*)c->pf.map})
         if (p) cudaFree(p);
+    for (void* p : {(void*)c->bt.x, (void*)c->bt.q, (void*)c->bt.att, (void*)c->bt.hb, (void*)c->bt.logits,
+                    (void*)c->bt.part, (void*)c->bt.ssq, (void*)c->bt.attn_part, (void*)c->bt.attn_cnt,
+                    (void*)c->bt.argmax, (void*)c->bt.first, (void*)c->bt.pos0, (void*)c->bt.tokens})
+        if (p) cudaFree(p);
+    for (auto& pl : c->bt.plan)
+        if (pl.ops) cudaFree(pl.ops);
     if (c->h_step) cudaFreeHost(c->h_step);
     if (c->stream) cudaStreamDestroy(c->stream);
     cudaSetDevice(prev);
@@ -1426,6 +1447,202 @@ extern "C" AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, 
     CK_RET(nullptr, cudaMemsetAsync(sc.split_cnt, 0, kStaticFlagBytes + sizeof(int), (cudaStream_t)stream));
     CK_RET(nullptr, launch_standalone<MODE_W4A16>(w->m, sc, x_dev, y_dev, w->device, (cudaStream_t)stream));
     return AION_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Lock-step batched decode (no counterpart in the reference, which decodes
+// one sequence): sequences 0..n_seq-1, each on its own KV cache.
+// ---------------------------------------------------------------------------
+// K slices of a matvec for NBLK blocks of 8 sequences: enough that one
+// slice's digits fit kBDigitBudget, and enough (tile, slice) units for about
+// two per warp; at most one slice per group and per CTA.
+static int batch_slices(const MatDesc& m, int nblk, int grid) {
+    const int gs_max = std::max(1, kBDigitBudget / (nblk * (kBBlockBytes + kBFacBytes)));
+    int S = (m.G + gs_max - 1) / gs_max;
+    S = std::max(S, (2 * kWarps * grid + m.ntiles - 1) / m.ntiles);
+    return std::min(S, std::min(m.G, grid));
+}
+
+template <int NBLK>
+static aion_status batch_plan(aion_ctx* c) {
+    auto& pl = c->bt.plan[NBLK];
+    if (pl.ops) return AION_OK;
+    const DevInfo& di = dev_info(c->dev);
+    const int grid = di.sms;
+    std::vector<BOpDesc> ops;
+    auto add = [&](const MatDesc& m, int kind, int layer) {
+        BOpDesc o;
+        o.m = m;
+        o.kind = kind;
+        o.layer = layer;
+        o.S = batch_slices(m, NBLK, grid);
+        o.pad = 0;
+        ops.push_back(o);
+    };
+    for (long long l = 0; l < c->L; l++) {
+        add(c->qkv[l], OP_QKV, (int)l);
+        add(c->wo[l], OP_WO, (int)l);
+        add(c->w13[l], OP_W13, (int)l);
+        add(c->w2[l], OP_W2, (int)l);
+    }
+    add(c->cls, OP_CLS, 0);
+    int gs = 1;
+    size_t part = 0;
+    for (const BOpDesc& o : ops) {
+        for (int cta = 0; cta < grid; cta++) {
+            const BSlice sl = bslice(o, cta, grid);
+            gs = std::max(gs, sl.gb - sl.ga);
+        }
+        part = std::max(part, (size_t)o.S * o.m.ntiles * 8 * NBLK * kTR);
+    }
+    if ((long long)gs * NBLK * (kBBlockBytes + kBFacBytes) > kBDigitBudget + NBLK * (kBBlockBytes + kBFacBytes) * 8) {
+        set_err(&c->err, "batched decode: a K slice of %d groups does not fit shared memory", gs);
+        return AION_ERR_SHAPE;
+    }
+    cudaFuncAttributes fa;
+    CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode_batch<NBLK>));
+    const int digits = (int)align256((size_t)gs * NBLK * kBBlockBytes);
+    const int facb = (int)align256((size_t)gs * NBLK * kBFacBytes);
+    const int opsb = (int)align256(ops.size() * sizeof(BOpDesc));
+    const int avail = di.smem_optin - (int)fa.sharedSizeBytes - digits - facb - opsb - 1024;
+    const int P = std::min(8, avail / (kWarps * kBChunkBytes));
+    if (P < 2) {
+        set_err(&c->err, "batched decode: shared memory too small for the rings (P = %d)", P);
+        return AION_ERR_SHAPE;
+    }
+    pl.fac_off = digits;
+    pl.ring_off = digits + facb;
+    pl.ops_off = pl.ring_off + P * kWarps * kBChunkBytes;
+    pl.total = pl.ops_off + opsb;
+    pl.P = P;
+    pl.part_floats = part;
+    CK_RET(&c->err, cudaFuncSetAttribute(k_decode_batch<NBLK>, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.total));
+    int nb = 0;
+    CK_RET(&c->err, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k_decode_batch<NBLK>, kDecodeThreads, pl.total));
+    if (nb < 1) {
+        set_err(&c->err, "batched decode kernel cannot be resident (smem %d)", pl.total);
+        return AION_ERR_CUDA;
+    }
+    CK_RET(&c->err, cudaMalloc(&pl.ops, ops.size() * sizeof(BOpDesc)));
+    CK_RET(&c->err, cudaMemcpy(pl.ops, ops.data(), ops.size() * sizeof(BOpDesc), cudaMemcpyHostToDevice));
+    return AION_OK;
+}
+
+template <int NBLK>
+static aion_status batch_launch(aion_ctx* c, int nb, int steps) {
+    aion_status s = batch_plan<NBLK>(c);
+    if (s != AION_OK) return s;
+    auto& bt = c->bt;
+    auto& pl = bt.plan[NBLK];
+    CK_RET(&c->err, pf_grow((void**)&bt.part, &bt.part_cap, pl.part_floats * 4));
+    BatchArgs a;
+    a.ops = pl.ops;
+    a.nops = c->nops;
+    a.emb = c->emb;
+    a.dim = (int)c->dim;
+    a.hidden = (int)c->hid_l;
+    a.n_layers = (int)c->L;
+    a.n_heads = (int)c->nh_l;
+    a.kv_mul = (int)c->kv_mul;
+    a.head_size = (int)c->hs;
+    a.kv_dim = (int)c->kv_l;
+    a.q_dim = (int)c->q_l;
+    a.vocab = (int)c->vocab;
+    a.max_pos = c->max_pos;
+    a.rms_att = c->rms_att;
+    a.rms_ffn = c->rms_ffn;
+    a.rms_final = c->rms_final;
+    a.freq_re = c->freq_re;
+    a.freq_im = c->freq_im;
+    a.nb = nb;
+    a.x = bt.x;
+    a.q = bt.q;
+    a.att = bt.att;
+    a.hb = bt.hb;
+    a.logits = bt.logits;
+    a.kcache = c->kcache;
+    a.vcache = c->vcache;
+    a.kv_seq = c->kv_seq;
+    a.part = bt.part;
+    a.ssq = bt.ssq;
+    a.attn_part = bt.attn_part;
+    a.attn_cnt = bt.attn_cnt;
+    a.max_chunks = c->max_chunks;
+    a.step = c->step;
+    a.argmax = bt.argmax;
+    a.first = bt.first;
+    a.pos0 = bt.pos0;
+    a.tokens = bt.tokens;
+    a.steps = steps;
+    a.P = pl.P;
+    a.fac_off = pl.fac_off;
+    a.ring_off = pl.ring_off;
+    a.ops_off = pl.ops_off;
+    CK_RET(&c->err, cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream));
+    CK_RET(&c->err, launch_ex(k_decode_batch<NBLK>, dim3(dev_info(c->dev).sms), dim3(kDecodeThreads), (size_t)pl.total,
+                              c->stream, false, true, a));
+    return AION_OK;
+}
+
+extern "C" AION_API aion_status aion_decode_batch(aion_ctx* c, int32_t n_seq, int32_t steps, const int32_t* first_tokens,
+                                                  const int32_t* pos0, int32_t* tokens, float* logits) {
+    if (!c || !first_tokens || !pos0 || !tokens) return AION_ERR_ARG;
+    if (c->mode != MODE_W4A16 || c->tp_n > 1) {
+        set_err(&c->err, "aion_decode_batch runs the W4A16 mode on one GPU");
+        return AION_ERR_STATE;
+    }
+    const int cap = std::min(c->nseq, kBMaxSeq);
+    if (n_seq < 1 || n_seq > cap || steps < 1) {
+        set_err(&c->err, "aion_decode_batch: %d sequences (1..%d held) x %d steps", n_seq, cap, steps);
+        return AION_ERR_ARG;
+    }
+    for (int b = 0; b < n_seq; b++)
+        if (first_tokens[b] < 0 || first_tokens[b] >= c->vocab || pos0[b] < 0 ||
+            (long long)pos0[b] + steps > c->max_pos) {
+            set_err(&c->err, "aion_decode_batch: sequence %d: token %d at position %d for %d steps is out of range", b,
+                    first_tokens[b], pos0[b], steps);
+            return AION_ERR_ARG;
+        }
+    if ((c->dim + dev_info(c->dev).sms - 1) / dev_info(c->dev).sms > kBMaxResRows) {
+        set_err(&c->err, "aion_decode_batch: dim %lld too large", c->dim);
+        return AION_ERR_SHAPE;
+    }
+    CK_RET(&c->err, cudaSetDevice(c->dev));
+    auto& bt = c->bt;
+    if (!bt.x) {
+        const size_t nb = (size_t)cap, grid = (size_t)dev_info(c->dev).sms;
+        CK_RET(&c->err, cudaMalloc(&bt.x, nb * c->dim * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.q, nb * c->q_l * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.att, nb * c->q_l * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.hb, nb * c->hid_l * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.logits, nb * c->vocab * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.ssq, grid * nb * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.attn_part, nb * c->nh_l * c->max_chunks * (c->hs + 4) * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.attn_cnt, nb * c->nh_l * 4));
+        CK_RET(&c->err, cudaMemset(bt.attn_cnt, 0, nb * c->nh_l * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.argmax, 2 * kBMaxSeq * 8));
+        CK_RET(&c->err, cudaMalloc(&bt.first, kBMaxSeq * 4));
+        CK_RET(&c->err, cudaMalloc(&bt.pos0, kBMaxSeq * 4));
+        bt.nb = cap;
+    }
+    CK_RET(&c->err, pf_grow((void**)&bt.tokens, &bt.tok_cap, ((size_t)steps + 1) * n_seq * 4));
+    CK_RET(&c->err, cudaMemcpyAsync(bt.first, first_tokens, n_seq * 4, cudaMemcpyHostToDevice, c->stream));
+    CK_RET(&c->err, cudaMemcpyAsync(bt.pos0, pos0, n_seq * 4, cudaMemcpyHostToDevice, c->stream));
+    aion_status s;
+    switch ((n_seq + 7) / 8) {
+    case 1: s = batch_launch<1>(c, n_seq, steps); break;
+    case 2: s = batch_launch<2>(c, n_seq, steps); break;
+    case 3: s = batch_launch<3>(c, n_seq, steps); break;
+    default: s = batch_launch<4>(c, n_seq, steps); break;
+    }
+    if (s != AION_OK) return s;
+    CK_RET(&c->err, cudaMemcpyAsync(tokens, bt.tokens, ((size_t)steps + 1) * n_seq * 4, cudaMemcpyDeviceToHost,
+                                    c->stream));
+    if (logits)
+        CK_RET(&c->err, cudaMemcpyAsync(logits, bt.logits, (size_t)n_seq * c->vocab * 4, cudaMemcpyDeviceToHost,
+                                        c->stream));
+    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    return check_device_error(c);
 }
 
 // ---------------------------------------------------------------------------

@@ -50,7 +50,8 @@ enum { AION_MODE_W4A16 = 0, AION_MODE_W4A8 = 1 };
 typedef struct aion_opts {
     int32_t device;     /* CUDA device ordinal                                        */
     int32_t mode;       /* AION_MODE_W4A16 (default) or AION_MODE_W4A8                */
-    int32_t max_batch;  /* sequences (KV caches) held, for aion_prefill (default 1)      */
+    int32_t max_batch;  /* sequences (KV caches) held, for aion_prefill and
+                           aion_decode_batch (default 1)                            */
     int32_t max_pos;    /* KV positions allocated (0 = header seq_len; <= seq_len)     */
     int32_t tp_size;    /* tensor-parallel ranks, one process per GPU (default 1)      */
     int32_t tp_rank;    /* this rank, 0 <= tp_rank < tp_size                           */
@@ -157,6 +158,21 @@ AION_API aion_status aion_set_sequence(aion_ctx* ctx, int32_t seq);
  * transformer() calls per sequence.  n_seq <= max_batch, n_tok <= max_pos. */
 AION_API aion_status aion_prefill(aion_ctx* ctx, const int32_t* tokens, int32_t n_seq, int32_t n_tok,
                                   float* logits_host);
+
+/* Lock-step greedy decode of sequences 0..n_seq-1 (n_seq <= min(max_batch,
+ * 32)), W4A16 on one GPU, one persistent launch.  Step i feeds sequence b
+ * one token at position pos0[b] + i: first_tokens[b] at step 0, afterwards
+ * the first maximum of its previous logits (src/kernel_simd.c:1236-1243).
+ * Each step is transformer() (src/kernel_simd.c:1014) of every sequence:
+ * it writes the sequence's KV cache at that position.  tokens[(steps + 1)
+ * * n_seq] (host) receives row i = the inputs of step i and row steps = the
+ * picks after the last step; logits[n_seq][vocab] (host, may be NULL) the
+ * last step's logits.  Each weight is read once per step for all sequences.
+ * Activations enter the integer dot as 24-bit fixed point per group of 32
+ * (relative error below 2^-22 of the group's largest value), fp32
+ * accumulate.  Needs pos0[b] + steps <= max_pos. */
+AION_API aion_status aion_decode_batch(aion_ctx* ctx, int32_t n_seq, int32_t steps, const int32_t* first_tokens,
+                                       const int32_t* pos0, int32_t* tokens, float* logits);
 
 /* ---------------------------------------------------------------------------
  * Kernel level (device pointers; stream = cudaStream_t or NULL)

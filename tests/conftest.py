@@ -2,9 +2,11 @@
 rest run on a CPU-only host.  The oracle (oracle/) is the checker."""
 from __future__ import annotations
 
+import hashlib
 import json
 import os
 import sys
+import tempfile
 from pathlib import Path
 
 import pytest
@@ -71,7 +73,6 @@ def tiny_path(built, workdir, golden_tiny):
     import aion_b200 as A
     p = workdir / "tiny_int4.bin"
     A.synth_checkpoint(p, cases.TINY, cases.SEEDS["tiny"], int4=True)
-    import hashlib
     assert hashlib.sha256(p.read_bytes()).hexdigest() == golden_tiny["int4_sha"]
     return p
 
@@ -91,3 +92,28 @@ def cuda(built):
     import torch
     torch.cuda.init()
     return torch
+
+
+def _sha(p: Path) -> str:
+    h = hashlib.sha256()
+    with open(p, "rb") as f:
+        for b in iter(lambda: f.read(1 << 24), b""):
+            h.update(b)
+    return h.hexdigest()
+
+
+@pytest.fixture(scope="session")
+def ckpt7b(cuda, golden_7b):
+    import aion_b200 as A
+    d = Path(os.environ.get("AION_CKPT_DIR", Path(tempfile.gettempdir()) / "aion_ckpt"))
+    d.mkdir(parents=True, exist_ok=True)
+    path = d / "llama2_7b_seed1.int4"
+    done = path.with_suffix(".done")
+    if not done.exists():
+        tmp = path.with_suffix(".tmp")
+        A.synth_checkpoint(tmp, cases.LLAMA7B, cases.SEEDS["7b"], int4=True)
+        tmp.rename(path)
+        done.write_text("ok")
+    assert path.stat().st_size == golden_7b["int4_bytes"]
+    assert _sha(path) == golden_7b["int4_sha"]
+    return path

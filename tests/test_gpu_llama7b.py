@@ -9,42 +9,10 @@ tokens, 32 W4A8 tokens); step-0 logits within 1e-3 relative of the oracle
 """
 from __future__ import annotations
 
-import hashlib
-import os
-import tempfile
-from pathlib import Path
-
 import numpy as np
 import pytest
 
-import cases
-
 pytestmark = pytest.mark.gpu
-
-
-def _sha(p: Path) -> str:
-    h = hashlib.sha256()
-    with open(p, "rb") as f:
-        for b in iter(lambda: f.read(1 << 24), b""):
-            h.update(b)
-    return h.hexdigest()
-
-
-@pytest.fixture(scope="module")
-def ckpt7b(cuda, golden_7b):
-    import aion_b200 as A
-    d = Path(os.environ.get("AION_CKPT_DIR", Path(tempfile.gettempdir()) / "aion_ckpt"))
-    d.mkdir(parents=True, exist_ok=True)
-    path = d / "llama2_7b_seed1.int4"
-    done = path.with_suffix(".done")
-    if not done.exists():
-        tmp = path.with_suffix(".tmp")
-        A.synth_checkpoint(tmp, cases.LLAMA7B, cases.SEEDS["7b"], int4=True)
-        tmp.rename(path)
-        done.write_text("ok")
-    assert path.stat().st_size == golden_7b["int4_bytes"]
-    assert _sha(path) == golden_7b["int4_sha"]
-    return path
 
 
 def test_7b_w4a16_stream(ckpt7b, golden_7b, oracle):
