@@ -222,16 +222,16 @@ struct aion_ctx {
         size_t a_cap = 0, b_cap = 0, c_cap = 0, x_cap = 0, q_cap = 0, tok_cap = 0, map_cap = 0;
     } pf;
     struct BatchBufs {             // lock-step batched decode, allocated on first use
-        float *x = nullptr, *q = nullptr, *att = nullptr, *hb = nullptr, *logits = nullptr;
-        float *part = nullptr, *ssq = nullptr, *attn_part = nullptr;
-        int* attn_cnt = nullptr;
+        float *x = nullptr, *q = nullptr, *att = nullptr, *logits = nullptr;
+        float *part = nullptr, *ssq = nullptr;
+        unsigned char* dg = nullptr;
         unsigned long long* argmax = nullptr;
         int32_t *first = nullptr, *pos0 = nullptr, *tokens = nullptr;
         size_t part_cap = 0, tok_cap = 0;
         int nb = 0;                // sequences the fixed buffers hold
         struct Plan {
             BOpDesc* ops = nullptr;
-            int P = 0, fac_off = 0, ring_off = 0, ops_off = 0, total = 0;
+            int P = 0, ring_off = 0, ops_off = 0, total = 0;
             size_t part_floats = 0;
         } plan[kBMaxSeq / 8 + 1];
     } bt;
@@ -403,9 +403,8 @@ static void ctx_destroy(aion_ctx* c) {
     for (void* p : {(void*)c->pf.a, (void*)c->pf.b, (void*)c->pf.c, (void*)c->pf.x, (void*)c->pf.q,
                     (void*)c->pf.tok, (void*)c->pf.map})
         if (p) cudaFree(p);
-    for (void* p : {(void*)c->bt.x, (void*)c->bt.q, (void*)c->bt.att, (void*)c->bt.hb, (void*)c->bt.logits,
-                    (void*)c->bt.part, (void*)c->bt.ssq, (void*)c->bt.attn_part, (void*)c->bt.attn_cnt,
-                    (void*)c->bt.argmax, (void*)c->bt.first, (void*)c->bt.pos0, (void*)c->bt.tokens})
+    for (void* p : {(void*)c->bt.x, (void*)c->bt.q, (void*)c->bt.att, (void*)c->bt.dg, (void*)c->bt.logits,
+                    (void*)c->bt.part, (void*)c->bt.ssq, (void*)c->bt.argmax, (void*)c->bt.first, (void*)c->bt.pos0, (void*)c->bt.tokens})
         if (p) cudaFree(p);
     for (auto& pl : c->bt.plan)
         if (pl.ops) cudaFree(pl.ops);
@@ -1457,7 +1456,7 @@ extern "C" AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, 
 // slice's digits fit kBDigitBudget, and enough (tile, slice) units for about
 // two per warp; at most one slice per group and per CTA.
 static int batch_slices(const MatDesc& m, int nblk, int grid) {
-    const int gs_max = std::max(1, kBDigitBudget / (nblk * (kBBlockBytes + kBFacBytes)));
+    const int gs_max = std::max(1, kBDigitBudget / (nblk * kBGroupBytes));
     int S = (m.G + gs_max - 1) / gs_max;
     S = std::max(S, (2 * kWarps * grid + m.ntiles - 1) / m.ntiles);
     return std::min(S, std::min(m.G, grid));
@@ -1495,23 +1494,21 @@ static aion_status batch_plan(aion_ctx* c) {
         }
         part = std::max(part, (size_t)o.S * o.m.ntiles * 8 * NBLK * kTR);
     }
-    if ((long long)gs * NBLK * (kBBlockBytes + kBFacBytes) > kBDigitBudget + NBLK * (kBBlockBytes + kBFacBytes) * 8) {
+    if ((long long)gs * NBLK * kBGroupBytes > kBDigitBudget + NBLK * kBGroupBytes * 8) {
         set_err(&c->err, "batched decode: a K slice of %d groups does not fit shared memory", gs);
         return AION_ERR_SHAPE;
     }
     cudaFuncAttributes fa;
     CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode_batch<NBLK>));
-    const int digits = (int)align256((size_t)gs * NBLK * kBBlockBytes);
-    const int facb = (int)align256((size_t)gs * NBLK * kBFacBytes);
+    const int digits = (int)align256(std::max((size_t)gs * NBLK * kBGroupBytes, (size_t)kBAttnScratch));
     const int opsb = (int)align256(ops.size() * sizeof(BOpDesc));
-    const int avail = di.smem_optin - (int)fa.sharedSizeBytes - digits - facb - opsb - 1024;
+    const int avail = di.smem_optin - (int)fa.sharedSizeBytes - digits - opsb - 1024;
     const int P = std::min(8, avail / (kWarps * kBChunkBytes));
     if (P < 2) {
         set_err(&c->err, "batched decode: shared memory too small for the rings (P = %d)", P);
         return AION_ERR_SHAPE;
     }
-    pl.fac_off = digits;
-    pl.ring_off = digits + facb;
+    pl.ring_off = digits;
     pl.ops_off = pl.ring_off + P * kWarps * kBChunkBytes;
     pl.total = pl.ops_off + opsb;
     pl.P = P;
@@ -1558,16 +1555,13 @@ static aion_status batch_launch(aion_ctx* c, int nb, int steps) {
     a.x = bt.x;
     a.q = bt.q;
     a.att = bt.att;
-    a.hb = bt.hb;
+    a.dg = bt.dg;
     a.logits = bt.logits;
     a.kcache = c->kcache;
     a.vcache = c->vcache;
     a.kv_seq = c->kv_seq;
     a.part = bt.part;
     a.ssq = bt.ssq;
-    a.attn_part = bt.attn_part;
-    a.attn_cnt = bt.attn_cnt;
-    a.max_chunks = c->max_chunks;
     a.step = c->step;
     a.argmax = bt.argmax;
     a.first = bt.first;
@@ -1575,7 +1569,6 @@ static aion_status batch_launch(aion_ctx* c, int nb, int steps) {
     a.tokens = bt.tokens;
     a.steps = steps;
     a.P = pl.P;
-    a.fac_off = pl.fac_off;
     a.ring_off = pl.ring_off;
     a.ops_off = pl.ops_off;
     CK_RET(&c->err, cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream));
@@ -1603,8 +1596,8 @@ extern "C" AION_API aion_status aion_decode_batch(aion_ctx* c, int32_t n_seq, in
                     first_tokens[b], pos0[b], steps);
             return AION_ERR_ARG;
         }
-    if ((c->dim + dev_info(c->dev).sms - 1) / dev_info(c->dev).sms > kBMaxResRows) {
-        set_err(&c->err, "aion_decode_batch: dim %lld too large", c->dim);
+    if ((c->dim / 32 + dev_info(c->dev).sms - 1) / dev_info(c->dev).sms > kBMaxResGroups || c->vocab % 4) {
+        set_err(&c->err, "aion_decode_batch: dim %lld or vocab %lld unsupported", c->dim, c->vocab);
         return AION_ERR_SHAPE;
     }
     CK_RET(&c->err, cudaSetDevice(c->dev));
@@ -1614,12 +1607,10 @@ extern "C" AION_API aion_status aion_decode_batch(aion_ctx* c, int32_t n_seq, in
         CK_RET(&c->err, cudaMalloc(&bt.x, nb * c->dim * 4));
         CK_RET(&c->err, cudaMalloc(&bt.q, nb * c->q_l * 4));
         CK_RET(&c->err, cudaMalloc(&bt.att, nb * c->q_l * 4));
-        CK_RET(&c->err, cudaMalloc(&bt.hb, nb * c->hid_l * 4));
+        const size_t gmax = (size_t)std::max(c->dim, c->hid_l) / 32;
+        CK_RET(&c->err, cudaMalloc(&bt.dg, gmax * (kBMaxSeq / 8) * kBGroupBytes));
         CK_RET(&c->err, cudaMalloc(&bt.logits, nb * c->vocab * 4));
         CK_RET(&c->err, cudaMalloc(&bt.ssq, grid * nb * 4));
-        CK_RET(&c->err, cudaMalloc(&bt.attn_part, nb * c->nh_l * c->max_chunks * (c->hs + 4) * 4));
-        CK_RET(&c->err, cudaMalloc(&bt.attn_cnt, nb * c->nh_l * 4));
-        CK_RET(&c->err, cudaMemset(bt.attn_cnt, 0, nb * c->nh_l * 4));
         CK_RET(&c->err, cudaMalloc(&bt.argmax, 2 * kBMaxSeq * 8));
         CK_RET(&c->err, cudaMalloc(&bt.first, kBMaxSeq * 4));
         CK_RET(&c->err, cudaMalloc(&bt.pos0, kBMaxSeq * 4));

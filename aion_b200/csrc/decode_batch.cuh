@@ -35,10 +35,11 @@ namespace aion {
 constexpr int kBMaxSeq = 32;
 constexpr int kBChunkG = 8;                       // groups per bulk copy
 constexpr int kBChunkBytes = kBChunkG * kGB;      // 2560
-constexpr int kBBlockBytes = 768;                 // digits of 8 sequences for one group (3 B operands)
-constexpr int kBFacBytes = 32;                    // factors of 8 sequences for one group
 constexpr int kBDigitBudget = 112 * 1024;         // shared memory for one slice's digits + factors
-constexpr int kBMaxResRows = 40;                  // residual rows per CTA (dim <= 40 * grid)
+constexpr int kBMaxResGroups = 40;                // residual groups of 32 per CTA (dim <= 1280 * grid)
+constexpr int kBAttnStage = 16 * kMaxHead * 4;   // one warp's K and V rows of 8 positions
+// Attention stages and partials, in the digit area (idle while attention runs).
+constexpr int kBAttnScratch = kWarps * kBAttnStage + kWarps * (kMaxHead + 4) * 4;
 
 struct BOpDesc {
     MatDesc m;
@@ -73,14 +74,12 @@ struct BatchArgs {
     int dim, hidden, n_layers, n_heads, kv_mul, head_size, kv_dim, q_dim, vocab, max_pos;
     const float *rms_att, *rms_ffn, *rms_final, *freq_re, *freq_im;
     int nb;                  // sequences; batch entry b uses KV cache b
-    float *x, *q, *att, *hb, *logits;   // [nb][dim], [nb][q_dim] x2, [nb][hidden], [nb][vocab]
+    float *x, *q, *att, *logits;        // [nb][dim], [nb][q_dim] x2, [nb][vocab]
+    unsigned char* dg;       // digits of the next matvec's input: [groups][NBLK][kBGroupBytes]
     float *kcache, *vcache;  // sequence b at + b * kv_seq: [L][max_pos][kv_dim]
     size_t kv_seq;
     float* part;             // [S][ntiles][nb8][16]: partial rows of the last matvec
     float* ssq;              // [grid][nb]: per CTA, sum of squares of its residual rows
-    float* attn_part;        // [nb][n_heads][max_chunks][head_size + 4]
-    int* attn_cnt;           // [nb][n_heads], zero between uses
-    int max_chunks;
     StepState* step;         // barrier counter and error code
     unsigned long long* argmax;   // [2][kBMaxSeq] keys, by step parity
     const int32_t* first;    // [nb] tokens of step 0
@@ -88,7 +87,7 @@ struct BatchArgs {
     int32_t* tokens;         // [steps + 1][nb]: each step's input tokens, then the last step's pick
     int steps;
     int P;                   // ring slots per warp (kBChunkBytes each)
-    int fac_off, ring_off, ops_off;   // dynamic shared memory: digits at 0
+    int ring_off, ops_off;   // dynamic shared memory: digits (or attention scratch) at 0
 };
 
 // ---------------------------------------------------------------------------
@@ -162,61 +161,80 @@ __device__ void bproduce(const BatchArgs& a, const BOpDesc* ops, unsigned char* 
 }
 
 // ---------------------------------------------------------------------------
-// Digits of this CTA's slice: groups [ga, gb) of every sequence's input
-// src + b * ld, times the RMSNorm weight w when given (the per-sequence
-// RMSNorm factor is applied to the sums).  Layout: group gl, block blk at
-// (gl * NBLK + blk) * 768: B operands of MMA 0, 1, 2 (256 bytes each: column
-// c at 32c, quad lane t at 8t, elements 4t..4t+3 then 16+4t..16+4t+3);
-// factors at fac[((gl * NBLK + blk) * 4 + t) * 2 + hi] for sequence
-// 8 blk + t + 4 hi.  Padding sequences (b >= nb) get zero digits and factors.
+// Digit layout of an input vector, per group slot g and block blk of 8
+// sequences, kBGroupBytes at (g * NBLK + blk) * kBGroupBytes: the B
+// operands of MMA 0, 1, 2 (256 bytes each: column c at 32c, quad lane t at
+// 8t, elements 4t..4t+3 then 16+4t..16+4t+3), then 8 fp32 factors, pair t
+// = (sequence t, sequence t + 4).  The same layout serves the whole vector
+// in global memory (slot = group) and one slice in shared memory (slot =
+// group - first group of the slice).  Padding sequences (b >= nb) carry
+// zero digits and factors.
 // ---------------------------------------------------------------------------
+constexpr int kBGroupBytes = 800;
+
+// Largest magnitude of a group of 32 held by 8 consecutive lanes (4 each).
+__device__ __forceinline__ float group_max8(float4 v) {
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    return fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+}
+
+// Digits of elements 4q..4q+3 (v) of group slot g of sequence b, whose
+// group maximum is m.
 template <int NBLK>
-__device__ void bbuild_digits(unsigned char* xd, float* fac, const float* src, int ld, const float* w, int ga, int gb,
-                              int nb) {
-    constexpr int NB8 = 8 * NBLK;
-    const int total = (gb - ga) * NB8 * 8;
-    for (int base = 0; base < total; base += kThreads) {   // uniform trip count: the shuffles see full warps
-        const int i = base + threadIdx.x;
-        const bool valid = i < total;
-        const int q = i & 7, rest = i >> 3;
-        const int b = rest % NB8, gl = rest / NB8;
-        const int col = (ga + gl) * 32 + 4 * q;
-        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (valid && b < nb) {
-            v = __ldcg(reinterpret_cast<const float4*>(src + (size_t)b * ld + col));
-            if (w) {
-                const float4 g = __ldg(reinterpret_cast<const float4*>(w + col));
-                v.x = __fmul_rn(v.x, g.x);
-                v.y = __fmul_rn(v.y, g.y);
-                v.z = __fmul_rn(v.z, g.z);
-                v.w = __fmul_rn(v.w, g.w);
-            }
-        }
-        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-        if (!valid) continue;
-        const int ebits = (int)((__float_as_uint(m) >> 23) & 0xFF);
-        const bool live = ebits >= 26;                    // groups below 2^-101 count as zero
-        const int E = 148 - ebits;                        // max * 2^E in [2^21, 2^22)
-        const float sa = __int_as_float((127 + E / 2) << 23), sb = __int_as_float((127 + E - E / 2) << 23);
-        const float e[4] = {v.x, v.y, v.z, v.w};
-        uint32_t Z[4];
+__device__ __forceinline__ void bdigit_store(unsigned char* base, int g, int b, int q, float4 v, float m) {
+    const int ebits = (int)((__float_as_uint(m) >> 23) & 0xFF);
+    const bool live = ebits >= 26;                    // groups below 2^-101 count as zero
+    const int E = 148 - ebits;                        // max * 2^E in [2^21, 2^22)
+    const float sa = __int_as_float((127 + E / 2) << 23), sb = __int_as_float((127 + E - E / 2) << 23);
+    const float e[4] = {v.x, v.y, v.z, v.w};
+    uint32_t Z[4];
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const int X = live ? __float2int_rn(__fmul_rn(__fmul_rn(e[k], sa), sb)) : 0;
-            Z[k] = ((uint32_t)X + 0x8080u) ^ 0x8080u;      // bytes d0, d1, d2 as signed bytes
+    for (int k = 0; k < 4; k++) {
+        const int X = live ? __float2int_rn(__fmul_rn(__fmul_rn(e[k], sa), sb)) : 0;
+        Z[k] = ((uint32_t)X + 0x8080u) ^ 0x8080u;      // bytes d0, d1, d2 as signed bytes
+    }
+    const uint32_t t01 = __byte_perm(Z[0], Z[1], 0x5140), t23 = __byte_perm(Z[2], Z[3], 0x5140);
+    const uint32_t u01 = __byte_perm(Z[0], Z[1], 0x7362), u23 = __byte_perm(Z[2], Z[3], 0x7362);
+    const int blk = b >> 3, j = b & 7, t = q & 3, h = q >> 2;
+    unsigned char* gp = base + (size_t)(g * NBLK + blk) * kBGroupBytes;
+    unsigned char* lo = gp + (j >> 2) * 256 + (2 * (j & 3)) * 32 + 8 * t + 4 * h;
+    *reinterpret_cast<uint32_t*>(lo) = __byte_perm(t01, t23, 0x5410);        // d0
+    *reinterpret_cast<uint32_t*>(lo + 32) = __byte_perm(t01, t23, 0x7632);   // d1
+    *reinterpret_cast<uint32_t*>(gp + 512 + (2 * (j & 3) + (j >> 2)) * 32 + 8 * t + 4 * h) =
+        __byte_perm(u01, u23, 0x5410);                                       // d2
+    if (q == 0)
+        *reinterpret_cast<float*>(gp + 768 + ((j & 3) * 2 + (j >> 2)) * 4) =
+            live ? __int_as_float((123 - E) << 23) : 0.0f;                  // 2^-E / 16
+}
+
+// Digits of groups [ga, gb) of every sequence's input src + b * ld into
+// shared memory (slots from 0).  Item i = (local group, sequence, quarter);
+// each pass loads four items per thread before digitising them, so the L2
+// round trips overlap.
+template <int NBLK>
+__device__ void bbuild_digits(unsigned char* xd, const float* src, int ld, int ga, int gb, int nb) {
+    constexpr int NB8 = 8 * NBLK, U = 4;
+    const int total = (gb - ga) * NB8 * 8;
+    for (int base = 0; base < total; base += U * kThreads) {   // uniform trip count: the shuffles see full warps
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = base + u * kThreads + threadIdx.x;
+            const int q = i & 7, rest = i >> 3;
+            const int b = rest % NB8, gl = rest / NB8;
+            v[u] = (i < total && b < nb)
+                       ? __ldcg(reinterpret_cast<const float4*>(src + (size_t)b * ld + (ga + gl) * 32 + 4 * q))
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
-        const uint32_t t01 = __byte_perm(Z[0], Z[1], 0x5140), t23 = __byte_perm(Z[2], Z[3], 0x5140);
-        const uint32_t u01 = __byte_perm(Z[0], Z[1], 0x7362), u23 = __byte_perm(Z[2], Z[3], 0x7362);
-        const int blk = b >> 3, j = b & 7, t = q & 3, h = q >> 2;
-        unsigned char* blkp = xd + (size_t)(gl * NBLK + blk) * kBBlockBytes + 8 * t + 4 * h;
-        unsigned char* lo = blkp + (j >> 2) * 256 + (2 * (j & 3)) * 32;
-        *reinterpret_cast<uint32_t*>(lo) = __byte_perm(t01, t23, 0x5410);        // d0
-        *reinterpret_cast<uint32_t*>(lo + 32) = __byte_perm(t01, t23, 0x7632);   // d1
-        *reinterpret_cast<uint32_t*>(blkp + 512 + (2 * (j & 3) + (j >> 2)) * 32) = __byte_perm(u01, u23, 0x5410);
-        if (q == 0) fac[((gl * NBLK + blk) * 4 + (j & 3)) * 2 + (j >> 2)] = live ? __int_as_float((123 - E) << 23) : 0.0f;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = base + u * kThreads + threadIdx.x;
+            const float m = group_max8(v[u]);
+            const int q = i & 7, rest = i >> 3;
+            if (i < total) bdigit_store<NBLK>(xd, rest / NB8, rest % NB8, q, v[u], m);
+        }
     }
 }
 
@@ -224,8 +242,7 @@ __device__ void bbuild_digits(unsigned char* xd, float* fac, const float* src, i
 // 16 x nb8 partial rows.  False if a wait gave up (not uniform: the caller
 // reduces it over the CTA).
 template <int NBLK>
-__device__ bool brun_op(const BOpDesc& op, Ring& ring, unsigned char* ring_base, const unsigned char* xd,
-                        const float* fac, float* part) {
+__device__ bool brun_op(const BOpDesc& op, Ring& ring, unsigned char* ring_base, const unsigned char* xd, float* part) {
     constexpr int NB8 = 8 * NBLK;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, r = lane >> 2, t = lane & 3;
     BCursor cu;
@@ -243,14 +260,14 @@ __device__ bool brun_op(const BOpDesc& op, Ring& ring, unsigned char* ring_base,
             const uint2 wv = *reinterpret_cast<const uint2*>(ch + k * kGB + 8 * lane);
             const float2 sw = *reinterpret_cast<const float2*>(ch + k * kGB + 256 + 8 * r);
             const uint32_t a0 = lo16(wv.x), a1 = lo16(wv.y), a2 = hi16(wv.x), a3 = hi16(wv.y);
-            const unsigned char* xb = xd + (size_t)(gl0 + k) * NBLK * kBBlockBytes + 8 * lane;
-            const float* fb = fac + ((gl0 + k) * NBLK * 4 + t) * 2;
+            const unsigned char* gp = xd + (size_t)(gl0 + k) * NBLK * kBGroupBytes;
 #pragma unroll
             for (int blk = 0; blk < NBLK; blk++) {
-                const uint2 b0 = *reinterpret_cast<const uint2*>(xb + blk * kBBlockBytes);
-                const uint2 b1 = *reinterpret_cast<const uint2*>(xb + blk * kBBlockBytes + 256);
-                const uint2 b2 = *reinterpret_cast<const uint2*>(xb + blk * kBBlockBytes + 512);
-                const float2 f = *reinterpret_cast<const float2*>(fb + blk * 8);
+                const unsigned char* xb = gp + blk * kBGroupBytes + 8 * lane;
+                const uint2 b0 = *reinterpret_cast<const uint2*>(xb);
+                const uint2 b1 = *reinterpret_cast<const uint2*>(xb + 256);
+                const uint2 b2 = *reinterpret_cast<const uint2*>(xb + 512);
+                const float2 f = *reinterpret_cast<const float2*>(gp + blk * kBGroupBytes + 768 + 8 * t);
                 int dl[4], dh[4], d2[4];
                 mma_s8(dl, a0, a1, a2, a3, b0.x, b0.y);
                 mma_s8(dh, a0, a1, a2, a3, b1.x, b1.y);
@@ -285,12 +302,29 @@ __device__ bool brun_op(const BOpDesc& op, Ring& ring, unsigned char* ring_base,
     return true;
 }
 
-// Sum over the S slices (in slice order) of row `row` of sequence b.
-__device__ __forceinline__ float bsum(const float* part, int S, int T, int nb8, int b, int row) {
+// Sum over the S slices (in slice order) of rows row4..row4+3 (row4 % 4 ==
+// 0) of sequence b; four slices' loads are in flight at a time.
+__device__ __forceinline__ float4 bsum4(const float* part, int S, int T, int nb8, int b, int row4) {
     const size_t stride = (size_t)T * nb8 * kTR;
-    const float* p = part + ((size_t)(row >> 4) * nb8 + b) * kTR + (row & 15);
-    float v = 0.0f;
-    for (int s = 0; s < S; s++) v += __ldcg(p + s * stride);
+    const float4* p = reinterpret_cast<const float4*>(part + ((size_t)(row4 >> 4) * nb8 + b) * kTR + (row4 & 15));
+    const size_t st4 = stride / 4;
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    int s = 0;
+    auto add = [&](float4 t) {
+        v.x += t.x;
+        v.y += t.y;
+        v.z += t.z;
+        v.w += t.w;
+    };
+    for (; s + 4 <= S; s += 4) {
+        const float4 t0 = __ldcg(p + s * st4), t1 = __ldcg(p + (s + 1) * st4);
+        const float4 t2 = __ldcg(p + (s + 2) * st4), t3 = __ldcg(p + (s + 3) * st4);
+        add(t0);
+        add(t1);
+        add(t2);
+        add(t3);
+    }
+    for (; s < S; s++) add(__ldcg(p + s * st4));
     return v;
 }
 
@@ -319,159 +353,169 @@ __device__ void bnorm_factors(const BatchArgs& a, float* s_ss) {
     csync();
 }
 
-// Residual rows [r0, r1) of this CTA for every sequence: x = f(b, row)
-// (the embedding, or x + the sums of the last matvec), then this CTA's sums
-// of squares per sequence.
-template <class F>
-__device__ void bresidual(const BatchArgs& a, float* s_sq, F f) {
-    const int G = gridDim.x, c = blockIdx.x;
-    const int r0 = (int)((long long)c * a.dim / G), r1 = (int)((long long)(c + 1) * a.dim / G), nr = r1 - r0;
-    for (int i = threadIdx.x; i < a.nb * nr; i += kThreads) {
-        const int b = i / nr, row = r0 + i % nr;
-        const float v = f(b, row);
-        __stcg(a.x + (size_t)b * a.dim + row, v);
-        s_sq[i] = v * v;
+// Residual update of this CTA's groups [g0, g1) of the model dimension for
+// every sequence: x = f(b, row4) (float4 of rows row4..row4+3), this CTA's
+// sums of squares per sequence, and the digits of x * nw (the RMSNorm
+// weight of the op that reads x next) into the global digit buffer.
+template <int NBLK, class F>
+__device__ void bresidual(const BatchArgs& a, const float* nw, float* s_sq, F f) {
+    constexpr int NB8 = 8 * NBLK;
+    const int G = gridDim.x, c = blockIdx.x, Gd = a.dim / 32;
+    const int g0 = (int)((long long)c * Gd / G), g1 = (int)((long long)(c + 1) * Gd / G), ng = g1 - g0;
+    const int total = ng * NB8 * 8;
+    for (int base = 0; base < total; base += kThreads) {
+        const int i = base + threadIdx.x;
+        const int q = i & 7, rest = i >> 3, b = rest % NB8, gl = rest / NB8;
+        const bool live = i < total && b < a.nb;
+        const int row4 = (g0 + gl) * 32 + 4 * q;
+        float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f), v = x;
+        if (live) {
+            x = f(b, row4);
+            __stcg(reinterpret_cast<float4*>(a.x + (size_t)b * a.dim + row4), x);
+            const float4 w = __ldg(reinterpret_cast<const float4*>(nw + row4));
+            v = make_float4(__fmul_rn(x.x, w.x), __fmul_rn(x.y, w.y), __fmul_rn(x.z, w.z), __fmul_rn(x.w, w.w));
+        }
+        float sq = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+        sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+        const float m = group_max8(v);
+        if (i < total) {
+            if (live && q == 0) s_sq[b * ng + gl] = sq;
+            bdigit_store<NBLK>(a.dg, g0 + gl, b, q, v, m);
+        }
     }
     csync();
     if (threadIdx.x < a.nb) {
         float s = 0.0f;
-        for (int k = 0; k < nr; k++) s += s_sq[threadIdx.x * nr + k];
+        for (int k = 0; k < ng; k++) s += s_sq[threadIdx.x * ng + k];
         __stcg(a.ssq + (size_t)c * a.nb + threadIdx.x, s);
     }
 }
 
-// Attention of one layer for every sequence: units (b, head, 16-position
-// chunk) spread over all warps of the grid, as in attention_layer; s_uoff[b]
-// is the first unit of sequence b (s_uoff[nb] = total).
-__device__ void battention(const BatchArgs& a, int layer, const int* s_pos, const int* s_uoff) {
+// Attention of one layer for every sequence (src/kernel_simd.c:1099-1117):
+// one CTA per (sequence b, head h) at a time.  Warp w takes the 8-position
+// blocks w, w + 11, ... of positions 0..pos.  Its lane 0 bulk-copies the
+// block's K and V rows (hs floats each) into the warp's stage in shared
+// memory; the copies bypass the L1 path that a kernel with this much shared
+// memory leaves narrow.  Then lane 4p + s scores position p on quarter s of
+// the head (elements 4(s + 4j)..+3, j < hs/16), lane l accumulates V
+// elements 4l..4l+3, and the warp folds the block into its running max, sum
+// and weighted V sum (online softmax).  The warps' partials meet in shared
+// memory and are merged in warp order.
+// `area`: kWarps stages of kBAttnStage bytes, then kWarps * (hs + 4) floats.
+__device__ bool battention(const BatchArgs& a, int layer, const int* s_pos, unsigned char* area, uint64_t* abar,
+                           uint32_t& aphase) {
     const int hs = a.head_size, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int hq = hs / 4, sub = lane & 3, pg = lane >> 2;
+    const int sub = lane & 3, pg = lane >> 2, nq = hs / 16;
     const float rs = sqrtf((float)hs);
-    const int pstride = hs + 4;
-    const int nw = gridDim.x * kWarps;
     const bool vl = 4 * lane < hs;
     const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    const int units = s_uoff[a.nb];
-    for (int u = warp * gridDim.x + blockIdx.x; u < units; u += nw) {
-        int b = 0;
-        while (s_uoff[b + 1] <= u) b++;
-        const int pos = s_pos[b], nch = pos / kAttnUnit + 1;
-        const int v = u - s_uoff[b], h = v / nch, k = v - h * nch;
-        const int kvh = h / a.kv_mul;
-        const size_t lkv = (size_t)b * a.kv_seq + (size_t)layer * a.max_pos * a.kv_dim;
+    const int pstride = hs + 4;
+    const uint32_t rowb = (uint32_t)hs * 4;
+    float* stage = reinterpret_cast<float*>(area + (size_t)warp * kBAttnStage);   // K rows [8][hs], V rows [8][hs]
+    float* scratch = reinterpret_cast<float*>(area + (size_t)kWarps * kBAttnStage);
+    const uint32_t bar = smem_addr(abar + warp);
+    bool ok = true;
+    const int units = a.nb * a.n_heads;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int b = u / a.n_heads, h = u - b * a.n_heads;
+        const int pos = s_pos[b], kvh = h / a.kv_mul;
+        const size_t lkv = (size_t)b * a.kv_seq + (size_t)layer * a.max_pos * a.kv_dim + (size_t)kvh * hs;
         const float* kc = a.kcache + lkv;
         const float* vc = a.vcache + lkv;
-        const int t0 = k * kAttnUnit, n = min(kAttnUnit, pos + 1 - t0);
-        const float* qp = a.q + (size_t)b * a.q_dim + h * hs + sub * hq;
-        const float* kr0 = kc + (size_t)(t0 + pg) * a.kv_dim + kvh * hs + sub * hq;
-        const float* kr1 = kr0 + (size_t)8 * a.kv_dim;
-        float4 qv[kQ4], k0[kQ4], k1[kQ4];
+        const float* qp = a.q + (size_t)b * a.q_dim + h * hs;
+        float4 qv[kQ4];
 #pragma unroll
-        for (int j = 0; j < kQ4; j++) {
-            const bool in = 4 * j < hq;
-            qv[j] = in ? __ldcg(reinterpret_cast<const float4*>(qp + 4 * j)) : z4;
-            k0[j] = (in && pg < n) ? __ldcg(reinterpret_cast<const float4*>(kr0 + 4 * j)) : z4;
-            k1[j] = (in && pg + 8 < n) ? __ldcg(reinterpret_cast<const float4*>(kr1 + 4 * j)) : z4;
-        }
-        float d0 = 0.0f, d1 = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kQ4; j++) {
-            d0 = fmaf(qv[j].x, k0[j].x, d0);
-            d0 = fmaf(qv[j].y, k0[j].y, d0);
-            d0 = fmaf(qv[j].z, k0[j].z, d0);
-            d0 = fmaf(qv[j].w, k0[j].w, d0);
-            d1 = fmaf(qv[j].x, k1[j].x, d1);
-            d1 = fmaf(qv[j].y, k1[j].y, d1);
-            d1 = fmaf(qv[j].z, k1[j].z, d1);
-            d1 = fmaf(qv[j].w, k1[j].w, d1);
-        }
-        d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
-        d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
-        d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
-        d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
-        float sc[kAttnUnit];
-#pragma unroll
-        for (int pp = 0; pp < 8; pp++) {
-            sc[pp] = __shfl_sync(0xffffffffu, d0, pp * 4);
-            sc[8 + pp] = __shfl_sync(0xffffffffu, d1, pp * 4);
-        }
-        const float* vr = vc + (size_t)t0 * a.kv_dim + kvh * hs + 4 * lane;
-        float4 vv[kAttnUnit];
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++)
-            vv[p] = (p < n && vl) ? __ldcg(reinterpret_cast<const float4*>(vr + (size_t)p * a.kv_dim)) : z4;
-        float m = -INFINITY;
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++) {
-            sc[p] = p < n ? __fdiv_rn(sc[p], rs) : -INFINITY;
-            m = fmaxf(m, sc[p]);
-        }
-        float l = 0.0f;
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++) {
-            sc[p] = p < n ? expf(sc[p] - m) : 0.0f;
-            l += sc[p];
-        }
+        for (int j = 0; j < kQ4; j++)
+            qv[j] = j < nq ? __ldcg(reinterpret_cast<const float4*>(qp + 4 * (sub + 4 * j))) : z4;
+        float m = -INFINITY, l = 0.0f;
         float4 o = z4;
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++) {
-            o.x = fmaf(sc[p], vv[p].x, o.x);
-            o.y = fmaf(sc[p], vv[p].y, o.y);
-            o.z = fmaf(sc[p], vv[p].z, o.z);
-            o.w = fmaf(sc[p], vv[p].w, o.w);
-        }
-        float* ap = a.att + (size_t)b * a.q_dim + h * hs + 4 * lane;
-        if (nch == 1) {
-            const float inv = 1.0f / l;
-            if (vl) __stcg(reinterpret_cast<float4*>(ap), make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv));
-            continue;
-        }
-        const int bh = b * a.n_heads + h;
-        float* part = a.attn_part + ((size_t)bh * a.max_chunks + k) * pstride;
-        if (vl) __stcg(reinterpret_cast<float4*>(part + 4 + 4 * lane), o);
-        if (lane == 0) {
-            __stcg(part, m);
-            __stcg(part + 1, l);
-        }
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) last = atomicAdd(a.attn_cnt + bh, 1) == nch - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        __threadfence();
-        const float* ph = a.attn_part + (size_t)bh * a.max_chunks * pstride;
-        float M = -INFINITY;
-        for (int c0 = 0; c0 < nch; c0 += 32)
-            if (c0 + lane < nch) M = fmaxf(M, __ldcg(ph + (size_t)(c0 + lane) * pstride));
-        M = warp_max(M);
-        float L = 0.0f;
-        float4 acc = z4;
-        for (int c0 = 0; c0 < nch; c0 += 32) {
-            const int cn = min(32, nch - c0);
-            float wl = 0.0f, ll = 0.0f;
-            if (lane < cn) {
-                wl = expf(__ldcg(ph + (size_t)(c0 + lane) * pstride) - M);
-                ll = __ldcg(ph + (size_t)(c0 + lane) * pstride + 1);
-            }
-            for (int c = 0; c < cn; c++) {
-                const float wgt = __shfl_sync(0xffffffffu, wl, c);
-                const float lc = __shfl_sync(0xffffffffu, ll, c);
-                L = fmaf(lc, wgt, L);
-                if (vl) {
-                    const float4 oc =
-                        __ldcg(reinterpret_cast<const float4*>(ph + (size_t)(c0 + c) * pstride + 4 + 4 * lane));
-                    acc.x = fmaf(oc.x, wgt, acc.x);
-                    acc.y = fmaf(oc.y, wgt, acc.y);
-                    acc.z = fmaf(oc.z, wgt, acc.z);
-                    acc.w = fmaf(oc.w, wgt, acc.w);
+        for (int t0 = warp * 8; t0 <= pos && ok; t0 += kWarps * 8) {
+            const int n = min(8, pos + 1 - t0);
+            __syncwarp();   // every lane is done with the stage's previous rows
+            if (lane == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive_expect_tx(bar, 2u * (uint32_t)n * rowb);
+                for (int p = 0; p < n; p++) {
+                    bulk_g2s(smem_addr(stage + p * hs), kc + (size_t)(t0 + p) * a.kv_dim, rowb, bar);
+                    bulk_g2s(smem_addr(stage + (8 + p) * hs), vc + (size_t)(t0 + p) * a.kv_dim, rowb, bar);
                 }
             }
+            if (!mbar_wait(bar, aphase)) {
+                // Give up on this warp's attention; let the copies in flight
+                // land (bounded) before the stage is reused or the CTA ends.
+                mbar_wait(bar, aphase, 1u << 20);
+                ok = false;
+                break;
+            }
+            aphase ^= 1u;
+            float4 kv[kQ4], vv[8];
+#pragma unroll
+            for (int j = 0; j < kQ4; j++)
+                kv[j] = (j < nq && pg < n) ? *reinterpret_cast<const float4*>(stage + pg * hs + 4 * (sub + 4 * j)) : z4;
+#pragma unroll
+            for (int p = 0; p < 8; p++)
+                vv[p] = (p < n && vl) ? *reinterpret_cast<const float4*>(stage + (8 + p) * hs + 4 * lane) : z4;
+            float d = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kQ4; j++) {
+                d = fmaf(qv[j].x, kv[j].x, d);
+                d = fmaf(qv[j].y, kv[j].y, d);
+                d = fmaf(qv[j].z, kv[j].z, d);
+                d = fmaf(qv[j].w, kv[j].w, d);
+            }
+            d += __shfl_xor_sync(0xffffffffu, d, 1);
+            d += __shfl_xor_sync(0xffffffffu, d, 2);
+            const float sc_own = pg < n ? __fdiv_rn(d, rs) : -INFINITY;
+            float sc[8];
+            float mb = -INFINITY;
+#pragma unroll
+            for (int p = 0; p < 8; p++) {
+                sc[p] = __shfl_sync(0xffffffffu, sc_own, 4 * p);
+                mb = fmaxf(mb, sc[p]);
+            }
+            const float mn = fmaxf(m, mb);
+            const float corr = expf(m - mn);
+            l *= corr;
+            o.x *= corr;
+            o.y *= corr;
+            o.z *= corr;
+            o.w *= corr;
+#pragma unroll
+            for (int p = 0; p < 8; p++) {
+                const float e = expf(sc[p] - mn);
+                l += e;
+                o.x = fmaf(e, vv[p].x, o.x);
+                o.y = fmaf(e, vv[p].y, o.y);
+                o.z = fmaf(e, vv[p].z, o.z);
+                o.w = fmaf(e, vv[p].w, o.w);
+            }
+            m = mn;
         }
-        const float inv = 1.0f / L;
-        if (vl) __stcg(reinterpret_cast<float4*>(ap), make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
-        if (lane == 0) a.attn_cnt[bh] = 0;
+        float* wp = scratch + warp * pstride;
+        if (lane == 0) {
+            wp[0] = m;
+            wp[1] = l;
+        }
+        if (vl) *reinterpret_cast<float4*>(wp + 4 + 4 * lane) = o;
+        csync();
+        for (int j = threadIdx.x; j < hs; j += kThreads) {
+            float M = -INFINITY;
+            for (int k = 0; k < kWarps; k++) M = fmaxf(M, scratch[k * pstride]);
+            float L = 0.0f, O = 0.0f;
+            for (int k = 0; k < kWarps; k++) {
+                const float mk = scratch[k * pstride];
+                if (mk == -INFINITY) continue;   // a warp with no positions
+                const float wk = expf(mk - M);
+                L = fmaf(scratch[k * pstride + 1], wk, L);
+                O = fmaf(scratch[k * pstride + 4 + j], wk, O);
+            }
+            __stcg(a.att + (size_t)b * a.q_dim + h * hs + j, O / L);
+        }
+        csync();
     }
+    return ok;
 }
 
 // ---------------------------------------------------------------------------
@@ -482,12 +526,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
     constexpr int NB8 = 8 * NBLK;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[kWarps * 2 * 8];
-    __shared__ float s_sq[kBMaxSeq * kBMaxResRows];
+    __shared__ __align__(8) uint64_t s_dbar;          // the slice's digits, copied from the global buffer
+    __shared__ __align__(8) uint64_t s_abar[kWarps];  // each warp's attention stage
+    __shared__ float s_sq[kBMaxSeq * kBMaxResGroups];
     __shared__ float s_ss[kBMaxSeq];
-    __shared__ int s_tok[kBMaxSeq], s_pos[kBMaxSeq], s_uoff[kBMaxSeq + 1];
+    __shared__ int s_tok[kBMaxSeq], s_pos[kBMaxSeq];
     __shared__ int s_bad;
     unsigned char* xd = smem;
-    float* fac = reinterpret_cast<float*>(smem + a.fac_off);
     unsigned char* ring_base = smem + a.ring_off;
     BOpDesc* ops = reinterpret_cast<BOpDesc*>(smem + a.ops_off);
     static_assert(sizeof(BOpDesc) % 4 == 0, "BOpDesc copy");
@@ -496,6 +541,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     Ring ring;
     if (warp < kWarps) ring_init(ring, ring_base, bars, a.P, kBChunkBytes, warp, lane == 0);
+    if (threadIdx.x == 0) {
+        mbar_init(smem_addr(&s_dbar), 1);
+        for (int w = 0; w < kWarps; w++) mbar_init(smem_addr(&s_abar[w]), 1);
+    }
     fence_mbar_init();
     __syncthreads();
     if (warp == kWarps) {
@@ -503,15 +552,31 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
         return;
     }
 
-    uint32_t nbar = 0;
+    uint32_t nbar = 0, dphase = 0, aphase = 0;
     bool ok = true;
     const int tid = threadIdx.x;
-    // A matvec phase: digits of this CTA's slice, then its units.
-    auto matvec = [&](const BOpDesc& op, const float* src, int ld, const float* nw) -> bool {
+    // A matvec phase: the digits of this CTA's slice (built from att for WO,
+    // else copied from the global buffer the previous phase wrote), then its
+    // units.
+    auto matvec = [&](const BOpDesc& op) -> bool {
         const BSlice sl = bslice(op, blockIdx.x, gridDim.x);
-        bbuild_digits<NBLK>(xd, fac, src, ld, nw, sl.ga, sl.gb, a.nb);
-        csync();
-        const bool fine = brun_op<NBLK>(op, ring, ring_base, xd, fac, a.part);
+        bool fine = true;
+        if (op.kind == OP_WO) {
+            bbuild_digits<NBLK>(xd, a.att, a.q_dim, sl.ga, sl.gb, a.nb);
+            csync();
+        } else {
+            if (tid == 0) {
+                // The buffer was written by other CTAs' generic stores before
+                // the grid barrier; the copy runs in the async proxy.
+                asm volatile("fence.proxy.async;" ::: "memory");
+                const uint32_t bytes = (uint32_t)((sl.gb - sl.ga) * NBLK * kBGroupBytes);
+                mbar_arrive_expect_tx(smem_addr(&s_dbar), bytes);
+                bulk_g2s(smem_addr(xd), a.dg + (size_t)sl.ga * NBLK * kBGroupBytes, bytes, smem_addr(&s_dbar));
+            }
+            fine = mbar_wait(smem_addr(&s_dbar), dphase);
+            dphase ^= 1u;
+        }
+        if (fine) fine = brun_op<NBLK>(op, ring, ring_base, xd, a.part);
         if (csync_or(!fine)) {
             if (tid == 0) set_error(a.step, DEV_COPY_TIMEOUT);
             return false;
@@ -534,12 +599,6 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
             for (int b = 0; b < a.nb; b++)
                 bad |= (s_tok[b] < 0 || s_tok[b] >= a.vocab || s_pos[b] < 0 || s_pos[b] >= a.max_pos);
             s_bad = bad;
-            int u = 0;
-            for (int b = 0; b < a.nb; b++) {
-                s_uoff[b] = u;
-                u += a.n_heads * (s_pos[b] / kAttnUnit + 1);
-            }
-            s_uoff[a.nb] = u;
         }
         csync();
         if (s_bad) {
@@ -550,80 +609,111 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
             a.tokens[(size_t)step * a.nb + tid] = s_tok[tid];
             a.argmax[par * kBMaxSeq + tid] = argmax_key(-1e9f, 0);   // this step's keys start here
         }
-        bresidual(a, s_sq, [&](int b, int row) { return emb_elem(a.emb, s_tok[b], row); });
+        bresidual<NBLK>(a, a.rms_att, s_sq, [&](int b, int row4) {
+            return make_float4(emb_elem(a.emb, s_tok[b], row4), emb_elem(a.emb, s_tok[b], row4 + 1),
+                               emb_elem(a.emb, s_tok[b], row4 + 2), emb_elem(a.emb, s_tok[b], row4 + 3));
+        });
         if (!grid_barrier(a.step, nbar)) { ok = false; break; }
 
         for (int oi = 0; oi < a.nops && ok; oi++) {
             const BOpDesc op = ops[oi];
             const int T = op.m.ntiles, S = op.S;
             const int l = op.layer;
+            if (!(ok = matvec(op))) break;
             if (op.kind == OP_QKV) {
-                if (!(ok = matvec(op, a.x, a.dim, a.rms_att + (size_t)l * a.dim))) break;
                 // q, k, v rows: RoPE on adjacent pairs (src/kernel_simd.c:1068-1085), KV append.
                 bnorm_factors(a, s_ss);
-                const int npair = (a.q_dim + 2 * a.kv_dim) / 2, h2 = a.head_size / 2;
-                for (int i = blockIdx.x * kThreads + tid; i < a.nb * npair; i += gridDim.x * kThreads) {
-                    const int b = i / npair, p = i - b * npair, row = 2 * p;
+                const int nq = (a.q_dim + 2 * a.kv_dim) / 4, h2 = a.head_size / 2;
+                for (int i = blockIdx.x * kThreads + tid; i < a.nb * nq; i += gridDim.x * kThreads) {
+                    const int b = i / nq, row = 4 * (i - b * nq);
                     const float ss = s_ss[b];
-                    const float v0 = __fmul_rn(bsum(a.part, S, T, NB8, b, row), ss);
-                    const float v1 = __fmul_rn(bsum(a.part, S, T, NB8, b, row + 1), ss);
+                    float4 v = bsum4(a.part, S, T, NB8, b, row);
+                    v = make_float4(__fmul_rn(v.x, ss), __fmul_rn(v.y, ss), __fmul_rn(v.z, ss), __fmul_rn(v.w, ss));
                     const int pos = s_pos[b];
                     const size_t lkv = (size_t)b * a.kv_seq + (size_t)l * a.max_pos * a.kv_dim + (size_t)pos * a.kv_dim;
                     if (row < a.q_dim + a.kv_dim) {
                         const bool is_q = row < a.q_dim;
                         const int base = is_q ? row : row - a.q_dim;
-                        const int hd = base % a.head_size;
-                        const float fr = __ldg(a.freq_re + (size_t)pos * h2 + hd / 2);
-                        const float fi = __ldg(a.freq_im + (size_t)pos * h2 + hd / 2);
-                        const float o0 = __fsub_rn(__fmul_rn(v0, fr), __fmul_rn(v1, fi));
-                        const float o1 = __fadd_rn(__fmul_rn(v0, fi), __fmul_rn(v1, fr));
+                        const int hd = base % a.head_size;   // the quad's pairs: hd, hd + 2 in the same head
+                        const float fr0 = __ldg(a.freq_re + (size_t)pos * h2 + hd / 2);
+                        const float fi0 = __ldg(a.freq_im + (size_t)pos * h2 + hd / 2);
+                        const float fr1 = __ldg(a.freq_re + (size_t)pos * h2 + hd / 2 + 1);
+                        const float fi1 = __ldg(a.freq_im + (size_t)pos * h2 + hd / 2 + 1);
+                        const float4 o = make_float4(__fsub_rn(__fmul_rn(v.x, fr0), __fmul_rn(v.y, fi0)),
+                                                     __fadd_rn(__fmul_rn(v.x, fi0), __fmul_rn(v.y, fr0)),
+                                                     __fsub_rn(__fmul_rn(v.z, fr1), __fmul_rn(v.w, fi1)),
+                                                     __fadd_rn(__fmul_rn(v.z, fi1), __fmul_rn(v.w, fr1)));
                         float* dst = is_q ? a.q + (size_t)b * a.q_dim + base : a.kcache + lkv + base;
-                        __stcg(reinterpret_cast<float2*>(dst), make_float2(o0, o1));
+                        __stcg(reinterpret_cast<float4*>(dst), o);
                     } else {
-                        const int base = row - a.q_dim - a.kv_dim;
-                        __stcg(reinterpret_cast<float2*>(a.vcache + lkv + base), make_float2(v0, v1));
+                        __stcg(reinterpret_cast<float4*>(a.vcache + lkv + (row - a.q_dim - a.kv_dim)), v);
                     }
                 }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
-                battention(a, l, s_pos, s_uoff);
+                if (csync_or(!battention(a, l, s_pos, xd, s_abar, aphase))) {
+                    if (tid == 0) set_error(a.step, DEV_COPY_TIMEOUT);
+                    ok = false;
+                    break;
+                }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             } else if (op.kind == OP_WO || op.kind == OP_W2) {
-                const bool wo = op.kind == OP_WO;
-                if (!(ok = matvec(op, wo ? a.att : a.hb, wo ? a.q_dim : a.hidden, nullptr))) break;
-                bresidual(a, s_sq, [&](int b, int row) {
-                    return __ldcg(a.x + (size_t)b * a.dim + row) + bsum(a.part, S, T, NB8, b, row);
+                // x += the op's sums; digits of x for the next op (W13 after
+                // WO; the next layer's QKV, or the classifier, after W2).
+                const float* nw = op.kind == OP_WO ? a.rms_ffn + (size_t)l * a.dim
+                                  : (l + 1 < a.n_layers ? a.rms_att + (size_t)(l + 1) * a.dim : a.rms_final);
+                bresidual<NBLK>(a, nw, s_sq, [&](int b, int row4) {
+                    const float4 x = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)b * a.dim + row4));
+                    const float4 d = bsum4(a.part, S, T, NB8, b, row4);
+                    return make_float4(x.x + d.x, x.y + d.y, x.z + d.z, x.w + d.w);
                 });
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             } else if (op.kind == OP_W13) {
-                if (!(ok = matvec(op, a.x, a.dim, a.rms_ffn + (size_t)l * a.dim))) break;
-                // rows w1[2j], w1[2j+1], w3[2j], w3[2j+1]; SwiGLU (src/kernel_simd.c:836-841)
+                // rows w1[2j], w1[2j+1], w3[2j], w3[2j+1]; SwiGLU (src/kernel_simd.c:836-841),
+                // straight into the digits of W2's input.
                 bnorm_factors(a, s_ss);
-                for (int i = blockIdx.x * kThreads + tid; i < a.nb * a.hidden; i += gridDim.x * kThreads) {
-                    const int b = i / a.hidden, j = i - b * a.hidden;
-                    const int row = 4 * (j >> 1) + (j & 1);
-                    const float ss = s_ss[b];
-                    const float g = __fmul_rn(bsum(a.part, S, T, NB8, b, row), ss);
-                    const float u = __fmul_rn(bsum(a.part, S, T, NB8, b, row + 2), ss);
-                    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf_cr(-g)));
-                    __stcg(a.hb + (size_t)b * a.hidden + j, __fmul_rn(s, u));
+                const int Gh = a.hidden / 32, total = Gh * NB8 * 8;
+                for (int base = 0; base < total; base += gridDim.x * kThreads) {
+                    const int i = base + blockIdx.x * kThreads + tid;
+                    const int q = i & 7, rest = i >> 3, b = rest % NB8, g = rest / NB8;
+                    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (i < total && b < a.nb) {
+                        const float ss = s_ss[b];
+                        const int j0 = g * 32 + 4 * q;          // hidden units j0..j0+3: rows 2 j0 .. 2 j0 + 7
+                        const float4 p0 = bsum4(a.part, S, T, NB8, b, 2 * j0);
+                        const float4 p1 = bsum4(a.part, S, T, NB8, b, 2 * j0 + 4);
+                        const float gv[4] = {p0.x, p0.y, p1.x, p1.y}, uv[4] = {p0.z, p0.w, p1.z, p1.w};
+                        float hv[4];
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            const float gk = __fmul_rn(gv[k], ss), uk = __fmul_rn(uv[k], ss);
+                            hv[k] = __fmul_rn(__fdiv_rn(gk, __fadd_rn(1.0f, expf_cr(-gk))), uk);
+                        }
+                        v = make_float4(hv[0], hv[1], hv[2], hv[3]);
+                    }
+                    const float m = group_max8(v);
+                    if (i < total) bdigit_store<NBLK>(a.dg, g, b, q, v, m);
                 }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             } else {   // OP_CLS
-                if (!(ok = matvec(op, a.x, a.dim, a.rms_final))) break;
                 bnorm_factors(a, s_ss);
-                const int G = gridDim.x, c = blockIdx.x;
-                const int r0 = (int)((long long)c * a.vocab / G), r1 = (int)((long long)(c + 1) * a.vocab / G);
+                const int G = gridDim.x, c = blockIdx.x, V4 = a.vocab / 4;
+                const int q0 = (int)((long long)c * V4 / G), q1 = (int)((long long)(c + 1) * V4 / G);
                 for (int b = warp; b < a.nb; b += kWarps) {
                     const float ss = s_ss[b];
                     float best = -1e9f;
                     uint32_t bi = 0;
-                    for (int row = r0 + lane; row < r1; row += 32) {
-                        const float v = __fmul_rn(bsum(a.part, S, T, NB8, b, row), ss);
-                        __stcg(a.logits + (size_t)b * a.vocab + row, v);
-                        if (v > best) {
-                            best = v;
-                            bi = (uint32_t)row;
-                        }
+                    for (int qd = q0 + lane; qd < q1; qd += 32) {
+                        const float4 s4 = bsum4(a.part, S, T, NB8, b, 4 * qd);
+                        const float v[4] = {__fmul_rn(s4.x, ss), __fmul_rn(s4.y, ss), __fmul_rn(s4.z, ss),
+                                            __fmul_rn(s4.w, ss)};
+                        __stcg(reinterpret_cast<float4*>(a.logits + (size_t)b * a.vocab + 4 * qd),
+                               make_float4(v[0], v[1], v[2], v[3]));
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            if (v[k] > best) {
+                                best = v[k];
+                                bi = (uint32_t)(4 * qd + k);
+                            }
                     }
                     unsigned long long key = best > -1e9f ? argmax_key(best, bi) : 0ull;
 #pragma unroll

@@ -55,6 +55,7 @@ SEED_7B = 1
 CFG_13B = (5120, 13824, 40, 40, 40, 32000, 2048)
 SEED_13B = 3
 TP_TOKENS = 256
+BATCH_13B = 16
 BOS = 1
 WORKLOAD_TOKENS = 512
 WEIGHT_BYTES_PER_TOKEN = 4_129_423_360          # 0.625 B x 6,607,077,376 weights
@@ -262,24 +263,39 @@ def prefill_leg(model, layers: int, stream, device: int) -> dict:
     attn_flops = PREFILL_SEQ * layers * 2.0 * (PREFILL_TOK * (PREFILL_TOK + 1) / 2) * dim * 2
     tflops = (lin_flops + attn_flops) / (ms * 1e-3) / 1e12
     peak, kind = bf16_peak()
+    # The 128 decode steps of all 32 sequences in lock step (one launch).
+    first = np.argmax(logits, axis=1).astype(np.int32)
+    pos0 = np.full(PREFILL_SEQ, PREFILL_TOK, np.int32)
     d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d0.record(stream)
-    for s in range(PREFILL_SEQ):
-        model.set_sequence(s)
-        model.decode_async(PREFILL_DECODE, int(np.argmax(logits[s])), PREFILL_TOK)
+    toks_out, _ = model.decode_batch(first, pos0, PREFILL_DECODE)
     d1.record(stream)
     torch.cuda.synchronize()
     dms = d0.elapsed_time(d1)
-    model.set_sequence(0)
+    wb = weight_bytes_per_token(layers)
+    kvb = sum(kv_step_bytes(layers, dim, [PREFILL_TOK + i] * PREFILL_SEQ) for i in range(PREFILL_DECODE))
+    dgbs = (wb * PREFILL_DECODE + kvb) / (dms * 1e-3) / 1e9
+    hpeak, hkind = hbm_peak()
     return {"workload": f"{PREFILL_SEQ} x {PREFILL_TOK} uniform random tokens (seed {PREFILL_SEED}) prefill, "
-                        f"then {PREFILL_DECODE} greedy decode steps per sequence (one sequence at a time)",
+                        f"then {PREFILL_DECODE} greedy decode steps of all {PREFILL_SEQ} sequences in lock step",
             "prefill_ms": ms, "prefill_tok_s": rows / (ms * 1e-3),
             "roofline": {"kernel": "prefill (k_gemm_bf16_tn dominant)", "bound": "tensor",
                          "achieved": tflops, "peak": peak, "peak_kind": kind, "unit": "TFLOP/s",
                          "frac": tflops / peak, "algorithmic_flops": lin_flops + attn_flops,
                          "note": "algorithmic bf16-equivalent flops; the kernels issue 3x the linear MMA work "
                                  "(two-part bf16 operands)"},
-            "decode_ms": dms, "decode_tok_s": PREFILL_SEQ * PREFILL_DECODE / (dms * 1e-3)}
+            "decode_ms": dms, "decode_tok_s": PREFILL_SEQ * PREFILL_DECODE / (dms * 1e-3),
+            "decode_roofline": {"kernel": "k_decode_batch<4> (lock-step batch of 32)", "bound": "hbm",
+                                "achieved": dgbs, "peak": hpeak, "peak_kind": hkind, "unit": "GB/s",
+                                "frac": dgbs / hpeak, "weight_bytes_per_step": wb,
+                                "kv_bytes_per_step_avg": kvb / PREFILL_DECODE},
+            "decode_stream_head": toks_out[:8, 0].tolist()}
+
+
+def kv_step_bytes(layers: int, kv_dim: int, positions) -> int:
+    """KV-cache bytes one decode step reads and writes: per sequence at
+    position p and layer, K and V rows 0..p read (fp32) and row p written."""
+    return sum(layers * 2 * kv_dim * 4 * (p + 2) for p in positions)
 
 
 def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
@@ -321,7 +337,8 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
     import aion_b200 as A
     path = ensure_13b(rank)
     barrier()
-    model = A.Model(path, device=local, tp_size=world, tp_rank=rank, max_pos=TP_TOKENS)
+    model = A.Model(path, device=local, tp_size=world, tp_rank=rank, max_pos=TP_TOKENS,
+                    max_batch=BATCH_13B if world == 1 else 1)
     if world > 1:
         handles = [None] * world
         pg.all_gather_object(handles, model.tp_handle())
@@ -347,6 +364,25 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
     wbytes = int(0.625 * (L * (4 * dim * dim + 3 * dim * hid) + vocab * dim)) // world
     gbs = wbytes * steps / (ms * 1e-3) / 1e9
     peak, kind = hbm_peak()
+    batch = None
+    if world == 1:
+        # Batch-16 decode of the same 256-token workload, all sequences from BOS.
+        model.decode_batch([BOS] * BATCH_13B, [0] * BATCH_13B, 4)   # warm-up
+        torch.cuda.synchronize()
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(stream)
+        btoks, _ = model.decode_batch([BOS] * BATCH_13B, [0] * BATCH_13B, TP_TOKENS - 1)
+        b1.record(stream)
+        torch.cuda.synchronize()
+        bms = b0.elapsed_time(b1)
+        nst = TP_TOKENS - 1
+        kvb = sum(kv_step_bytes(L, dim, [i] * BATCH_13B) for i in range(nst))
+        bgbs = (wbytes * nst + kvb) / (bms * 1e-3) / 1e9
+        batch = {"workload": f"batch {BATCH_13B} greedy decode of {TP_TOKENS} tokens from BOS (lock step)",
+                 "value": BATCH_13B * nst / (bms * 1e-3), "unit": "tok/s", "ms_per_step": bms / nst,
+                 "roofline": {"kernel": "k_decode_batch<2>", "bound": "hbm", "achieved": bgbs, "peak": peak,
+                              "peak_kind": kind, "unit": "GB/s", "frac": bgbs / peak},
+                 "same_stream_as_batch1": bool((btoks[:16, 0] == np.array(toks[:16])).all())}
     if rank == 0:
         print(json.dumps({
             "metric": "Llama-2-13B int4 decode tok/s (batch 1, tensor-parallel)", "value": steps / (ms * 1e-3),
@@ -361,7 +397,7 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
                          "achieved": gbs, "peak": peak, "peak_kind": kind, "unit": "GB/s",
                          "frac": gbs / peak, "bytes_per_token_per_gpu": wbytes},
             "gpu_launches": 1, "clocks": clk,
-            "token_stream_head": toks[:16]}), flush=True)
+            "token_stream_head": toks[:16], "batch16": batch}), flush=True)
     model.close()
     if pg:
         pg.destroy_process_group()
