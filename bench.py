@@ -331,6 +331,59 @@ def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
     return out
 
 
+def run_batch(args, local: int) -> None:
+    """7B-shape lock-step batched decode: args.batch sequences from BOS,
+    args.steps greedy steps each (positions 0..steps-1), one launch."""
+    import torch
+    import aion_b200 as A
+    nb = args.batch
+    path = ensure_7b(0, args.profile_layers)
+    model = A.Model(path, device=local, max_batch=nb, max_pos=args.steps + args.warmup + 1)
+    L = model.config.n_layers
+    stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{local}")
+    model.decode_batch([BOS] * nb, [0] * nb, args.warmup)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    toks, _ = model.decode_batch([BOS] * nb, [0] * nb, args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    dim = CFG_7B[0]
+    wb = weight_bytes_per_token(L)
+    kvb = sum(kv_step_bytes(L, dim, [i] * nb) for i in range(args.steps))
+    gbs = (wb * args.steps + kvb) / (ms * 1e-3) / 1e9
+    peak, kind = hbm_peak()
+    parity = None
+    gold = ROOT / "tests" / "golden" / "7b.json"
+    if gold.exists() and args.profile_layers <= 0:
+        want = json.loads(gold.read_text())["w4a16_tokens"]
+        k = min(len(want), args.steps + 1)
+        parity = {"tokens_compared": k, "identical_in_every_slot": all(
+            list(toks[:k, b]) == want[:k] for b in range(nb))}
+    print(json.dumps({
+        "metric": f"Llama-2-7B int4 decode tok/s (batch {nb}, lock step)", "value": nb * args.steps / (ms * 1e-3),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "s4 weights x s8 activation digits (24-bit fixed point per group, int32 tensor-core dot), "
+                 "fp32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": f"llama2-7b-shape W4A16 greedy decode of {nb} sequences from BOS, positions "
+                               f"0..{args.steps - 1}", "layers": L, "seed": 1, "parallelism": "replicas x1"},
+        "roofline": {"kernel": f"k_decode_batch<{(nb + 7) // 8}>", "bound": "hbm", "achieved": gbs, "peak": peak,
+                     "peak_kind": kind, "unit": "GB/s", "frac": gbs / peak,
+                     "weight_bytes_per_step": wb, "kv_bytes_per_step_avg": kvb / args.steps},
+        "e2e": {"value": nb * args.steps / wall, "unit": "tok/s", "h2d_bytes_per_step": 8 * nb / args.steps,
+                "d2h_bytes_per_step": 4 * nb * (args.steps + 1) / args.steps},
+        "gpu_launches": 1, "clocks": clk, "parity": parity}), flush=True)
+    model.close()
+
+
 def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
     """13B-shape decode, tensor-parallel over the launch's ranks."""
     import torch
@@ -416,6 +469,7 @@ def main() -> None:
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill leg")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
     ap.add_argument("--tp13b", action="store_true", help="13B shape, tensor-parallel over the launch's ranks")
+    ap.add_argument("--batch", type=int, default=0, help="7B lock-step batched decode of this many sequences")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling only: 7B shapes truncated to this many layers")
     args = ap.parse_args()
@@ -451,6 +505,11 @@ def main() -> None:
 
     if args.tp13b:
         run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks)
+        return
+
+    if args.batch > 0:
+        if rank == 0:
+            run_batch(args, local)
         return
 
     if args.matvec:
