@@ -39,6 +39,12 @@ class AionError(RuntimeError):
         super().__init__(f"AION_ERR_{self.code}: {message}")
 
 
+class Sampler(ctypes.Structure):
+    """aion_sampler: temperature <= 0 is greedy."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("top_k", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("seed", ctypes.c_uint64)]
+
+
 class Config(ctypes.Structure):
     """The 28-byte checkpoint header (src/kernel_simd.c:40-48)."""
     _fields_ = [(n, ctypes.c_int32) for n in
@@ -96,6 +102,8 @@ def lib() -> ctypes.CDLL:
         "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_decode_batch": (I32, [VP, I32, I32, VP, VP, VP, VP]),
+        "aion_set_sampler": (I32, [VP, VP]),
+        "aion_read_logits": (I32, [VP, VP]),
         "aion_set_sequence": (I32, [VP, I32]),
         "aion_tp_handle": (I32, [VP, VP]),
         "aion_tp_plan": (I32, [P(Config), I32, I32, P(I64)]),
@@ -198,6 +206,7 @@ class Model:
         _check(L.aion_get_config(self._h, ctypes.byref(cfg)), self._h)
         self.config = cfg
         self.mode = mode
+        self.tp_size = tp_size
 
     def close(self) -> None:
         if getattr(self, "_h", None):
@@ -249,6 +258,18 @@ class Model:
         _check(lib().aion_decode_batch(self._h, f.size, steps, _ptr(f), _ptr(p), _ptr(toks),
                                        _ptr(lg) if lg is not None else None), self._h)
         return toks, lg
+
+    def set_sampler(self, temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0, seed: int = 0) -> None:
+        """Next-token rule of the decode calls: greedy when temperature <= 0,
+        else a seeded draw with temperature, top-k and top-p (aion_set_sampler)."""
+        sp = Sampler(temperature, top_p, top_k, 0, seed)
+        _check(lib().aion_set_sampler(self._h, ctypes.byref(sp)), self._h)
+
+    def read_logits(self) -> np.ndarray:
+        """Logits of the last step run by decode_async / generate."""
+        out = np.empty(self.config.vocab_size // self.tp_size, np.float32)
+        _check(lib().aion_read_logits(self._h, _ptr(out)), self._h)
+        return out
 
     def tp_handle(self) -> bytes:
         """This rank's exchange-region handle, for every rank's tp_connect."""

@@ -274,6 +274,8 @@ struct aion_ctx {
     StepState* h_step = nullptr;   // pinned
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t gexec = nullptr;
+    SamplerParams samp = {};       // sampling (aion_set_sampler); off: greedy
+    int sampling = 0;
 };
 
 static uint8_t* arena_take(aion_ctx* c, size_t bytes) {
@@ -493,6 +495,8 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.exp_host.x = c->exp_tab;
     a.exp_host.n = c->exp_n;
     a.exp_host.delta = c->exp_delta;
+    a.samp = c->samp;
+    a.sampling = c->sampling;
     // The grid-barrier counter starts from zero in every launch.
     cudaError_t e = cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream);
     if (e != cudaSuccess) return e;
@@ -638,9 +642,11 @@ static aion_status setup_decode_kernel(aion_ctx* c, int max_n, int max_chunk) {
     cudaFuncAttributes fa;
     CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode<MODE>));
     // W4A8 stages the RMSNorm input (dim floats) and the reference-order
-    // attention scores (max_pos floats) in the digit area.
-    c->plan = plan_smem(max_n, max_chunk, di.smem_optin, (int)fa.sharedSizeBytes,
-                        MODE == MODE_W4A8 ? std::max(c->max_pos, (int)c->dim) * 4 : 0, (int)(c->nops * sizeof(OpDesc)));
+    // attention scores (max_pos floats) in the digit area; the sampler uses
+    // it as scratch between steps.
+    const int stage = MODE == MODE_W4A8 ? std::max(c->max_pos, (int)c->dim) * 4 : 0;
+    c->plan = plan_smem(max_n, max_chunk, di.smem_optin, (int)fa.sharedSizeBytes, std::max(stage, kSampleScratch),
+                        (int)(c->nops * sizeof(OpDesc)));
     if (c->plan.P < 2) {
         set_err(&c->err, "shared memory too small for the decode rings (P = %d)", c->plan.P);
         return AION_ERR_SHAPE;
@@ -1449,6 +1455,51 @@ extern "C" AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, 
 }
 
 // ---------------------------------------------------------------------------
+// Sampling beyond greedy (no counterpart in the reference, whose loop takes
+// the argmax): the decode kernels draw each next token on the device.
+// ---------------------------------------------------------------------------
+// Copies the logits of the last decoded step (aion_decode_async /
+// aion_generate) to the host.
+extern "C" AION_API aion_status aion_read_logits(aion_ctx* c, float* host) {
+    if (!c || !host) return AION_ERR_ARG;
+    CK_RET(&c->err, cudaSetDevice(c->dev));
+    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    CK_RET(&c->err, cudaMemcpy(host, c->logits, (size_t)c->vocab_l * 4, cudaMemcpyDeviceToHost));
+    return AION_OK;
+}
+
+extern "C" AION_API aion_status aion_set_sampler(aion_ctx* c, const aion_sampler* s) {
+    if (!c) return AION_ERR_ARG;
+    if (s && s->temperature > 0.0f) {
+        if (!std::isfinite(s->temperature) || !(s->top_p > 0.0f && s->top_p <= 1.0f) || s->top_k < 0) {
+            set_err(&c->err, "aion_set_sampler: temperature %g, top_p %g, top_k %d out of range", s->temperature,
+                    s->top_p, s->top_k);
+            return AION_ERR_ARG;
+        }
+        if (c->tp_n > 1) {
+            set_err(&c->err, "aion_set_sampler: sampling needs the whole vocabulary on one GPU (tp_size 1)");
+            return AION_ERR_STATE;
+        }
+    }
+    CK_RET(&c->err, cudaSetDevice(c->dev));
+    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    c->sampling = (s && s->temperature > 0.0f) ? 1 : 0;
+    c->samp = SamplerParams{};
+    if (c->sampling) {
+        c->samp.temperature = s->temperature;
+        c->samp.top_p = s->top_p;
+        c->samp.top_k = s->top_k;
+        c->samp.seed = s->seed;
+    }
+    // The single-step graph captured the old parameters.
+    if (c->gexec) cudaGraphExecDestroy(c->gexec);
+    if (c->graph) cudaGraphDestroy(c->graph);
+    c->gexec = nullptr;
+    c->graph = nullptr;
+    return AION_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Lock-step batched decode (no counterpart in the reference, which decodes
 // one sequence): sequences 0..n_seq-1, each on its own KV cache.
 // ---------------------------------------------------------------------------
@@ -1571,6 +1622,8 @@ static aion_status batch_launch(aion_ctx* c, int nb, int steps) {
     a.P = pl.P;
     a.ring_off = pl.ring_off;
     a.ops_off = pl.ops_off;
+    a.samp = c->samp;
+    a.sampling = c->sampling;
     CK_RET(&c->err, cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream));
     CK_RET(&c->err, launch_ex(k_decode_batch<NBLK>, dim3(dev_info(c->dev).sms), dim3(kDecodeThreads), (size_t)pl.total,
                               c->stream, false, true, a));

@@ -51,6 +51,18 @@ __host__ __device__ inline unsigned long long argmax_key(float v, uint32_t idx) 
 __host__ __device__ inline uint32_t key_index(unsigned long long k) {
     return 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull);
 }
+// The logit a key was made from.
+__host__ __device__ inline float key_value(unsigned long long k) {
+    const uint32_t ob = (uint32_t)(k >> 32);
+    const uint32_t u = (ob & 0x80000000u) ? (ob & 0x7FFFFFFFu) : ~ob;
+    float f;
+#ifdef __CUDA_ARCH__
+    f = __uint_as_float(u);
+#else
+    memcpy(&f, &u, 4);
+#endif
+    return f;
+}
 
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.

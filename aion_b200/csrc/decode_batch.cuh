@@ -87,6 +87,8 @@ struct BatchArgs {
     int32_t* tokens;         // [steps + 1][nb]: each step's input tokens, then the last step's pick
     int steps;
     int P;                   // ring slots per warp (kBChunkBytes each)
+    SamplerParams samp;      // used when sampling != 0 (else the greedy argmax)
+    int sampling;
     int ring_off, ops_off;   // dynamic shared memory: digits (or attention scratch) at 0
 };
 
@@ -724,6 +726,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
                     if (lane == 0 && key) atomicMax(a.argmax + par * kBMaxSeq + b, key);
                 }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                if (a.sampling) {
+                    // CTA b draws sequence b's next token (stream b, its position)
+                    // and leaves it in the key slot the next step reads.
+                    for (int b = blockIdx.x; b < a.nb; b += gridDim.x) {
+                        const float mx = key_value(__ldcg(a.argmax + par * kBMaxSeq + b));
+                        const int t = sample_token(a.logits + (size_t)b * a.vocab, a.vocab, mx, a.samp,
+                                                   (unsigned long long)b, (unsigned long long)s_pos[b],
+                                                   reinterpret_cast<unsigned long long*>(xd));
+                        if (tid == 0) a.argmax[par * kBMaxSeq + b] = argmax_key(0.0f, (uint32_t)t);
+                    }
+                    if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                }
                 if (step == a.steps - 1 && blockIdx.x == 0 && tid < a.nb)
                     a.tokens[(size_t)a.steps * a.nb + tid] = (int)key_index(__ldcg(a.argmax + par * kBMaxSeq + tid));
             }

@@ -21,6 +21,7 @@
 #pragma once
 
 #include "matvec.cuh"
+#include "sample.cuh"
 
 namespace aion {
 
@@ -61,6 +62,8 @@ struct DecodeArgs {
     int P, slot_bytes, xbytes, xs_off;
     int ops_off;                   // shared-memory copy of ops[] (xbytes = ring offset)
     ExpTable exp_host;             // the host expf's deviations (W4A8), or empty
+    SamplerParams samp;            // used when sampling != 0 (else the greedy argmax)
+    int sampling;
     // Tensor parallelism over tp_n GPUs (tp_n == 1: off).  This rank holds
     // q_dim query rows (n_heads heads, kv_dim K/V rows), hidden FFN rows and
     // vocab rows [vocab_off, vocab_off + classifier rows); WO and W2 give
@@ -992,6 +995,20 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
                     }
                     *a.argmax = m;
                     __threadfence();
+                }
+            }
+            if (op.kind == OP_CLS && a.sampling) {
+                // Every logit and the argmax key are in place: CTA 0 draws the
+                // next token and hands it to the next step as a forced token.
+                if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                if (blockIdx.x == 0) {
+                    const float mx = key_value(__ldcg(a.argmax));
+                    const int t = sample_token(a.logits, a.vocab, mx, a.samp, 0ull, (unsigned long long)pos,
+                                               reinterpret_cast<unsigned long long*>(xf));
+                    if (threadIdx.x == 0) {
+                        a.step->forced_token = t;
+                        __threadfence();
+                    }
                 }
             }
             if (oi == a.nops - 1 && step == a.steps - 1) break;   // nothing after the last classifier

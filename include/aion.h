@@ -175,6 +175,32 @@ AION_API aion_status aion_decode_batch(aion_ctx* ctx, int32_t n_seq, int32_t ste
                                        const int32_t* pos0, int32_t* tokens, float* logits);
 
 /* ---------------------------------------------------------------------------
+ * Sampling beyond greedy (no counterpart in the reference, which takes the
+ * argmax, src/kernel_simd.c:1236-1243).
+ * ------------------------------------------------------------------------- */
+typedef struct aion_sampler {
+    float temperature;  /* <= 0: greedy (the reference's argmax)                   */
+    float top_p;        /* keep the most likely tokens up to this mass; 1 = off     */
+    int32_t top_k;      /* keep the top_k most likely tokens (ties kept); 0 = off   */
+    int32_t reserved;
+    uint64_t seed;      /* each draw is a function of (seed, sequence, position)    */
+} aion_sampler;
+
+/* Sets how aion_decode_async / aion_generate / aion_decode_batch pick the
+ * next token (NULL: greedy).  With temperature T > 0 every step draws, on
+ * the device, from the distribution e^((logit - max) / T) restricted to
+ * the top_k largest logits and then to the smallest set of largest logits
+ * whose mass reaches top_p: weights are floor(e^x * 2^32) integers,
+ * thresholds exact, and the draw a SplitMix64 value of (seed, sequence,
+ * position) scanned in index order, so a run is reproducible.  aion_forward
+ * is unaffected (it returns logits).  Needs tp_size 1. */
+AION_API aion_status aion_set_sampler(aion_ctx* ctx, const aion_sampler* sampler);
+
+/* Copies the logits of the last step that aion_decode_async / aion_generate
+ * ran (this rank's vocab rows) to host[vocab]; waits for the stream. */
+AION_API aion_status aion_read_logits(aion_ctx* ctx, float* host);
+
+/* ---------------------------------------------------------------------------
  * Kernel level (device pointers; stream = cudaStream_t or NULL)
  * ------------------------------------------------------------------------- */
 
