@@ -317,6 +317,7 @@ def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
         for m in mats:
             m.matvec_w4a16(x, y)
         torch.cuda.synchronize()
+        # Eager: one ctypes call per launch (includes the host's launch cost).
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
@@ -324,8 +325,27 @@ def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
                 m.matvec_w4a16(x, y)
         e1.record()
         torch.cuda.synchronize()
+        eager_ms = e0.elapsed_time(e1) / (reps * copies)
+        # Kernel time: the same launches captured once in a CUDA graph and
+        # replayed, so the host's launch rate does not limit the GPU.
+        side = torch.cuda.Stream(device=f"cuda:{device}")
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for m in mats:
+                m.matvec_w4a16(x, y, stream=side)
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / (reps * copies)
-        out[f"{d}x{n}"] = {"us": ms * 1e3, "GBps": matvec_bytes(d, n) / (ms * 1e-3) / 1e9}
+        out[f"{d}x{n}"] = {"us": ms * 1e3, "GBps": matvec_bytes(d, n) / (ms * 1e-3) / 1e9,
+                           "frac": matvec_bytes(d, n) / (ms * 1e-3) / 1e9 / hbm_peak()[0],
+                           "eager_us": eager_ms * 1e3,
+                           "eager_GBps": matvec_bytes(d, n) / (eager_ms * 1e-3) / 1e9}
+        del g
         for m in mats:
             m.free()
     return out
