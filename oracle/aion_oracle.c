@@ -118,6 +118,40 @@ ORC_EXPORT void orc_dequant(float* out, const float* scales, const uint8_t* pack
 /* per multiply and per add (built with -ffp-contract=off).                   */
 /* ------------------------------------------------------------------------- */
 
+/* C10: the fp32 matvec of the reference's fp32 path, matmul_block_4x4
+ * (src/kernel_simd.c:547-620) as run on one thread (rows 0.. in blocks of
+ * 4): rows of a full block keep four lane sums, lane j adding w[k] * x[k]
+ * for k = j mod 4 with a fused multiply-add (FMLA) over the 16-column
+ * blocks, then (lane0 + lane1) + (lane2 + lane3) (FADDP), then the columns
+ * past the last full 16 one by one; rows after the last full block of 4
+ * sum w[k] * x[k] in order with separate multiply and add. */
+typedef struct { float* y; const float* x; const float* w; int64_t n, d; } orc_f32_args;
+
+static void orc_f32_rows(void* p, int64_t r0, int64_t r1) {
+    orc_f32_args* a = (orc_f32_args*)p;
+    const int64_t n = a->n, n16 = n / 16 * 16, d4 = a->d / 4 * 4;
+    for (int64_t i = r0; i < r1; i++) {
+        const float* w = a->w + i * n;
+        float val;
+        if (i < d4) {
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int64_t k = 0; k < n16; k += 4)
+                for (int j = 0; j < 4; j++) acc[j] = fmaf(w[k + j], a->x[k + j], acc[j]);
+            val = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+            for (int64_t k = n16; k < n; k++) val += w[k] * a->x[k];
+        } else {
+            val = 0.0f;
+            for (int64_t k = 0; k < n; k++) val += w[k] * a->x[k];
+        }
+        a->y[i] = val;
+    }
+}
+
+ORC_EXPORT void orc_matvec_f32(float* y, const float* x, const float* w, int64_t n, int64_t d) {
+    orc_f32_args a = {y, x, w, n, d};
+    orc_parallel_rows(orc_f32_rows, &a, d);
+}
+
 typedef struct { float* y; const float* x; const float* scales; const uint8_t* packed; int64_t n; } orc_mv_args;
 
 static void orc_matvec_rows(void* p, int64_t r0, int64_t r1) {
@@ -262,7 +296,8 @@ ORC_EXPORT void orc_swiglu(float* hb, const float* hb2, int64_t size) {
 /* ------------------------------------------------------------------------- */
 
 typedef struct { int32_t dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len; } orc_config;
-typedef struct { const float* scales; const uint8_t* packed; } orc_qw;
+/* A weight tensor: int4 (scales + packed) or, for fp32 files, plain floats. */
+typedef struct { const float* scales; const uint8_t* packed; const float* f; } orc_qw;
 
 typedef struct orc_model {
     orc_config c;
@@ -273,11 +308,28 @@ typedef struct orc_model {
     /* run state */
     float *x, *xb, *xb2, *hb, *hb2, *q, *k, *v, *att, *logits, *kcache, *vcache;
     int8_t* qx; float* xs;
+    int f32;                       /* fp32 llama2.c file (the reference's fp32 path) */
 } orc_model;
 
 static orc_qw qw_at(orc_qw w, int64_t elems) {
-    orc_qw r = { w.scales + elems / 32, w.packed + elems / 2 };
+    orc_qw r = { NULL, NULL, NULL };
+    if (w.f) r.f = w.f + elems;
+    else { r.scales = w.scales + elems / 32; r.packed = w.packed + elems / 2; }
     return r;
+}
+
+/* Expected byte size of an fp32 llama2.c file (src/kernel_simd.c:906-936),
+ * plus the separate classifier that a negative vocab_size announces (which
+ * the reference never reads). */
+ORC_EXPORT int64_t orc_f32_file_size(const int32_t* cfg7) {
+    int64_t dim = cfg7[0], hid = cfg7[1], L = cfg7[2], nh = cfg7[3], nkv = cfg7[4];
+    int64_t vocab = cfg7[5] < 0 ? -(int64_t)cfg7[5] : cfg7[5], seq = cfg7[6];
+    if (dim <= 0 || hid <= 0 || L <= 0 || nh <= 0 || nkv <= 0 || vocab <= 0 || seq <= 0) return -1;
+    int64_t hs = dim / nh, kv = dim * nkv / nh;
+    int64_t f = vocab * dim + L * dim + L * dim * dim + 2 * L * dim * kv + L * dim * dim + L * dim + 3 * L * dim * hid +
+                dim + 2 * seq * (hs / 2);
+    if (cfg7[5] < 0) f += vocab * dim;
+    return 28 + 4 * f;
 }
 
 /* Expected byte size of an int4 file for a header (size_t arithmetic). */
@@ -313,17 +365,19 @@ ORC_EXPORT orc_model* orc_open(const char* path, char* err, int errlen) {
     orc_model* m = calloc(1, sizeof(*m));
     m->map = map; m->map_size = (size_t)st.st_size;
     memcpy(&m->c, map, 28);
+    int64_t want = orc_int4_file_size(&m->c.dim), want_f = orc_f32_file_size(&m->c.dim);
     if (m->c.vocab_size < 0) m->c.vocab_size = -m->c.vocab_size;
-    int64_t want = orc_int4_file_size(&m->c.dim);
-    if (want < 0 || want != (int64_t)st.st_size) {
-        snprintf(err, errlen, "size mismatch: header implies %lld bytes, file has %lld", (long long)want, (long long)st.st_size);
+    if (want_f == (int64_t)st.st_size && want != want_f) m->f32 = 1;
+    else if (want < 0 || want != (int64_t)st.st_size) {
+        snprintf(err, errlen, "size mismatch: header implies %lld (int4) or %lld (fp32) bytes, file has %lld",
+                 (long long)want, (long long)want_f, (long long)st.st_size);
         orc_close(m); return NULL;
     }
     int64_t dim = m->c.dim, hid = m->c.hidden_dim, L = m->c.n_layers, vocab = m->c.vocab_size, seq = m->c.seq_len;
     m->head_size = dim / m->c.n_heads;
     m->kv_dim = dim * m->c.n_kv_heads / m->c.n_heads;
     const char* p = (const char*)map + 28;
-#define MAPQ(w, cnt) do { int64_t n_ = (cnt); (w).scales = (const float*)p; p += (n_ / 32) * 4; (w).packed = (const uint8_t*)p; p += n_ / 2; } while (0)
+#define MAPQ(w, cnt) do { int64_t n_ = (cnt); if (m->f32) { (w).f = (const float*)p; p += n_ * 4; } else { (w).scales = (const float*)p; p += (n_ / 32) * 4; (w).packed = (const uint8_t*)p; p += n_ / 2; } } while (0)
 #define MAPF(w, cnt) do { (w) = (const float*)p; p += (int64_t)(cnt) * 4; } while (0)
     MAPQ(m->emb, vocab * dim);
     MAPF(m->rms_att, L * dim);
@@ -379,7 +433,9 @@ ORC_EXPORT const float* orc_fp32_tensor(const orc_model* m, int which) {
 /* One matvec of the forward in the selected mode: W4A16 uses the scalar
  * int4 kernel; W4A8 quantizes the input per 32 and runs the integer kernel. */
 static void orc_mm(orc_model* m, int mode, float* y, const float* x, orc_qw w, int64_t n, int64_t d) {
-    if (mode == 1) {
+    if (w.f) {
+        orc_matvec_f32(y, x, w.f, n, d);
+    } else if (mode == 1) {
         orc_quantize_activations(m->qx, m->xs, x, n);
         orc_matvec_w4a8(y, m->qx, m->xs, w.scales, w.packed, n, d);
     } else {
@@ -396,7 +452,8 @@ ORC_EXPORT int orc_forward(orc_model* m, int token, int pos, int mode) {
     float* x = m->x;
 
     orc_qw row = qw_at(m->emb, (int64_t)token * dim);
-    orc_dequant(x, row.scales, row.packed, dim);
+    if (row.f) memcpy(x, row.f, (size_t)dim * 4);   /* fp32 path: src/kernel_simd.c:1041-1043 */
+    else orc_dequant(x, row.scales, row.packed, dim);
 
     for (int64_t l = 0; l < p->n_layers; l++) {
         orc_rmsnorm(m->xb, x, m->rms_att + l * dim, dim);

@@ -185,6 +185,8 @@ class Reference:
             "ref_reset": (None, []),
             "ref_forward": (None, [ctypes.c_int, ctypes.c_int]),
             "ref_forward_w4a8": (None, [ctypes.c_int, ctypes.c_int]),
+            "ref_open_f32": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int]),
+            "ref_forward_f32": (None, [ctypes.c_int, ctypes.c_int]),
             "ref_generate": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P]),
             "ref_matmul_int4_scalar": (None, [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int]),
             "ref_matmul_int4_neon": (None, [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int]),
@@ -238,6 +240,16 @@ class Reference:
     def open(self, path, threads: int = 4, scalar: bool = True):
         """The reference engine is process-global: open once per process."""
         self.L.ref_open(str(path).encode(), threads, 1 if scalar else 0)
+        cfg = np.zeros(7, np.int32)
+        self.L.ref_config(_np(cfg))
+        self.vocab = int(cfg[5])
+        return self
+
+    def open_f32(self, path, threads: int = 1):
+        """The reference's fp32 path (the CLI without "int4").  With one
+        thread every row takes the 4-lane fused-multiply-add block of
+        matmul_block_4x4 (src/kernel_simd.c:547), which the oracle restates."""
+        self.L.ref_open_f32(str(path).encode(), threads)
         cfg = np.zeros(7, np.int32)
         self.L.ref_config(_np(cfg))
         self.vocab = int(cfg[5])

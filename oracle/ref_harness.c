@@ -10,7 +10,9 @@
  *   - a W4A8 forward: the reference's transformer() sequence with
  *     quantize_activations_neon + dispatch_matmul_w4a8 in place of every
  *     dispatch_matmul_int4 (the CLI's "w4a8" flag never does this,
- *     src/kernel_simd.c:1193 vs :1054-1165).
+ *     src/kernel_simd.c:1193 vs :1054-1165);
+ *   - the fp32 path (the CLI without "int4"): load_checkpoint +
+ *     transformer() with TransformerWeights, unchanged.
  * The reference sources are read from the reference tree at build time and
  * never copied into this repository.
  */
@@ -22,6 +24,8 @@
 
 static Config g_cfg;
 static QuantizedTransformerWeights g_qw;
+static TransformerWeights g_w;
+static int g_f32 = 0;
 static RunState g_rs;
 static int g_fd = -1;
 static float* g_data = NULL;
@@ -30,6 +34,7 @@ static int g_pool = 0;
 static QActivations g_qa;
 
 REF_EXPORT int ref_open(const char* path, int n_threads, int scalar) {
+    g_f32 = 0;
     load_checkpoint_int4(path, &g_cfg, &g_qw, &g_fd, &g_data, &g_size);
     malloc_run_state(&g_rs, &g_cfg);
     int big = g_cfg.dim > g_cfg.hidden_dim ? g_cfg.dim : g_cfg.hidden_dim;
@@ -39,6 +44,17 @@ REF_EXPORT int ref_open(const char* path, int n_threads, int scalar) {
     if (!g_pool) { init_thread_pool(n_threads); g_pool = 1; }
     return 0;
 }
+
+/* The fp32 path: src/kernel_simd.c:906-936 (load_checkpoint) and the fp32
+ * branch of transformer(). */
+REF_EXPORT int ref_open_f32(const char* path, int n_threads) {
+    load_checkpoint(path, &g_cfg, &g_w, &g_fd, &g_data, &g_size);
+    malloc_run_state(&g_rs, &g_cfg);
+    g_f32 = 1;
+    if (!g_pool) { init_thread_pool(n_threads); g_pool = 1; }
+    return 0;
+}
+REF_EXPORT void ref_forward_f32(int token, int pos) { transformer(token, pos, &g_cfg, &g_rs, &g_w, NULL); }
 
 REF_EXPORT void ref_config(int* out7) { memcpy(out7, &g_cfg, sizeof(Config)); }
 REF_EXPORT float* ref_logits(void) { return g_rs.logits; }
@@ -148,7 +164,9 @@ REF_EXPORT int ref_generate(int bos, int steps, int w4a8, int* tokens, float* ga
     int token = bos;
     ref_reset();
     for (int pos = 0; pos < steps; pos++) {
-        if (w4a8) ref_forward_w4a8(token, pos); else ref_forward(token, pos);
+        if (g_f32) ref_forward_f32(token, pos);
+        else if (w4a8) ref_forward_w4a8(token, pos);
+        else ref_forward(token, pos);
         float max_p = -1e9f, second = -INFINITY;
         int next = 0;
         for (int i = 0; i < g_cfg.vocab_size; i++) {

@@ -77,6 +77,17 @@ def tiny_path(built, workdir, golden_tiny):
     return p
 
 
+@pytest.fixture(scope="session")
+def tiny_f32_path(built, workdir, golden_tiny):
+    """The tiny model as an fp32 llama2.c file (the input of quantize.c),
+    checked against the hash recorded with the reference's fixtures."""
+    import aion_b200 as A
+    p = workdir / "tiny_f32.bin"
+    A.synth_checkpoint(p, cases.TINY, cases.SEEDS["tiny"], int4=False)
+    assert hashlib.sha256(p.read_bytes()).hexdigest() == golden_tiny["fp32_sha"]
+    return p
+
+
 def cuda_ok() -> bool:
     try:
         import torch

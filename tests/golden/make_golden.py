@@ -64,6 +64,20 @@ def model_fixture(ref: Reference, path: Path, steps: int, w4a8_steps: int, threa
     return out
 
 
+def f32_fixture(ref: Reference, path: Path, steps: int) -> dict:
+    """The reference's fp32 path on the fp32 file: its CLI (no "int4" flag,
+    one thread) and the same loop through the harness with logits."""
+    r = subprocess.run([str(REF_DIR / "kernel_simd"), str(path), str(steps), "1"], capture_output=True, text=True,
+                       check=True, cwd=tempfile.gettempdir())
+    out = {"f32_cli_tokens": [int(l.split()[1]) for l in r.stdout.strip().splitlines()]}
+    ref.open_f32(path, threads=1)
+    toks, gaps, logits = ref.generate(steps, dump_logits=True)
+    out["f32_tokens"] = toks.tolist()
+    out["f32_gaps"] = [float(g) for g in gaps]
+    out["f32_logits_sha"] = [cases.sha(l) for l in logits]
+    return out
+
+
 def kat_fixture(ref: Reference) -> dict:
     kat: dict = {"quantizer": {}, "actquant": {}, "matvec": {}}
     for name, w in cases.quantizer_kat_inputs().items():
@@ -93,20 +107,38 @@ def main() -> None:
     ap.add_argument("--7b", dest="b7", action="store_true", help="also the 7B stream (needs ~5 GB disk, minutes)")
     ap.add_argument("--threads", type=int, default=7)
     ap.add_argument("--tmp", default=tempfile.gettempdir())
+    ap.add_argument("--f32-only", action="store_true", help="only add the fp32-path keys to tiny.json")
+    ap.add_argument("--f32-child", default=None, help=argparse.SUPPRESS)
     args = ap.parse_args()
     ref = Reference()
     tmp = Path(args.tmp)
+    if args.f32_child:
+        print(json.dumps(f32_fixture(ref, Path(args.f32_child), 256)))
+        return
+    f32 = tmp / "aion_tiny_f32.bin"
+    if args.f32_only:
+        A.synth_checkpoint(f32, cases.TINY, cases.SEEDS["tiny"], int4=False)
+        tiny = json.loads((OUT / "tiny.json").read_text())
+        assert file_sha(f32) == tiny["fp32_sha"]
+        # The reference engine is process-global: the fp32 run goes in a child.
+        r = subprocess.run([sys.executable, __file__, "--f32-child", str(f32)], capture_output=True, text=True,
+                           check=True)
+        tiny.update(json.loads(r.stdout.strip().splitlines()[-1]))
+        (OUT / "tiny.json").write_text(json.dumps(tiny))
+        print("tiny.json fp32 keys written; min gap", min(tiny["f32_gaps"]))
+        return
 
     (OUT / "kat.json").write_text(json.dumps(kat_fixture(ref)))
     print("kat.json written")
 
-    f32 = tmp / "aion_tiny_f32.bin"
     q = tmp / "aion_tiny_int4_ref.bin"
     A.synth_checkpoint(f32, cases.TINY, cases.SEEDS["tiny"], int4=False)
     subprocess.run([str(REF_DIR / "quantize"), str(f32), str(q)], check=True, capture_output=True)
     tiny = {"config": list(cases.TINY), "seed": cases.SEEDS["tiny"], "fp32_sha": file_sha(f32),
             "int4_sha": file_sha(q), "int4_bytes": q.stat().st_size}
     tiny.update(model_fixture(ref, q, 256, 256, args.threads, cli=True))
+    r = subprocess.run([sys.executable, __file__, "--f32-child", str(f32)], capture_output=True, text=True, check=True)
+    tiny.update(json.loads(r.stdout.strip().splitlines()[-1]))
     (OUT / "tiny.json").write_text(json.dumps(tiny))
     print("tiny.json written; min gap", min(tiny["w4a16_gaps"]))
 

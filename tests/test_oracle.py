@@ -86,6 +86,16 @@ def test_tiny_w4a8_stream_and_logits(oracle, tiny_path, golden_tiny):
     m.close()
 
 
+def test_tiny_f32_stream_and_logits(oracle, tiny_f32_path, golden_tiny):
+    """The fp32 path (the reference CLI without "int4"): the oracle's
+    restatement of matmul_block_4x4 gives the reference's logits bit for bit."""
+    m = oracle.open(tiny_f32_path)
+    toks, gaps, logits = m.generate(256, dump_logits=True)
+    assert toks.tolist() == golden_tiny["f32_tokens"] == golden_tiny["f32_cli_tokens"]
+    assert [cases.sha(l) for l in logits] == golden_tiny["f32_logits_sha"]
+    m.close()
+
+
 def test_oracle_matches_live_reference_on_fresh_seeds(oracle):
     """Where the reference build is present, compare on inputs not in the fixtures."""
     from oracle.oracle import Reference, ref_available
