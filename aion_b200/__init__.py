@@ -102,6 +102,7 @@ def lib() -> ctypes.CDLL:
         "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_decode_batch": (I32, [VP, I32, I32, VP, VP, VP, VP]),
+        "aion_get_mode": (I32, [VP]),
         "aion_set_sampler": (I32, [VP, VP]),
         "aion_read_logits": (I32, [VP, VP]),
         "aion_set_sequence": (I32, [VP, I32]),
@@ -205,7 +206,7 @@ class Model:
         cfg = Config()
         _check(L.aion_get_config(self._h, ctypes.byref(cfg)), self._h)
         self.config = cfg
-        self.mode = mode
+        self.mode = {MODE_W4A16: "int4", MODE_W4A8: "w4a8", 2: "f32"}[L.aion_get_mode(self._h)]
         self.tp_size = tp_size
 
     def close(self) -> None:

@@ -2,7 +2,11 @@
  * aion -- command-line driver, a drop-in for the reference CLI
  * (src/kernel_simd.c:1175-1288):
  *
- *   aion <model.int4> <steps> <gpus> [int4] [w4a8] [nograph]
+ *   aion <model> <steps> <gpus> [int4] [w4a8] [nograph]
+ *
+ * The file decides the path: an int4 file (quantize.c) runs the int4
+ * path, an fp32 llama2.c file the fp32 path, as kernel_simd does with and
+ * without "int4".
  *
  * Same argv order as `kernel_simd <model> <steps> <threads> [int4] ...`
  * with the thread count replaced by the GPU count.  Prints "pos token" per
@@ -46,8 +50,10 @@ int main(int argc, char** argv) {
     aion_config cfg;
     aion_get_config(ctx, &cfg);
     if (steps > cfg.seq_len) steps = cfg.seq_len;
+    const int mode = aion_get_mode(ctx);
     fprintf(stderr, "[aion] Mode: %s on B200. GPUs: %d. dim %d, layers %d, vocab %d.\n",
-            opts.mode == AION_MODE_W4A8 ? "W4A8" : "Int4 (W4A16)", gpus, cfg.dim, cfg.n_layers, cfg.vocab_size);
+            mode == AION_MODE_W4A8 ? "W4A8" : mode == AION_MODE_F32 ? "Float32" : "Int4 (W4A16)", gpus, cfg.dim,
+            cfg.n_layers, cfg.vocab_size);
     int* tokens = calloc(steps > 0 ? (size_t)steps : 1, sizeof(int));
     double secs = 0.0;
     s = aion_generate(ctx, 1, steps, tokens, &secs);
@@ -67,8 +73,9 @@ int main(int argc, char** argv) {
         char ts[26];
         ctime_r(&now, ts);
         ts[24] = '\0';
-        fprintf(csv, "%s,%s,%d,%d,%.4f,%.2f\n", ts, opts.mode == AION_MODE_W4A8 ? "B200_W4A8" : "B200_Int4", gpus,
-                steps, secs, tps);
+        fprintf(csv, "%s,%s,%d,%d,%.4f,%.2f\n", ts,
+                mode == AION_MODE_W4A8 ? "B200_W4A8" : mode == AION_MODE_F32 ? "B200_F32" : "B200_Int4", gpus, steps,
+                secs, tps);
         fclose(csv);
     }
     aion_free(ctx);

@@ -136,6 +136,25 @@ static cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
 
 // Source rows hold src_G groups; the tiles take groups [src_g0, src_g0 + m.G)
 // of each (src_G = 0: the tiles' own width).
+// fp32 rows [rows][src_n] (columns from group src_g0) into fp32 tiles.
+static cudaError_t retile_f32(const MatDesc& m, const float* src, long long rows, int row_offset, int interleave,
+                              int slot, int src_n, int src_g0, cudaStream_t st) {
+    RetileF32Args a;
+    a.src = src;
+    a.m = m;
+    a.rows = rows;
+    a.row_offset = row_offset;
+    a.interleave = interleave;
+    a.slot = slot;
+    a.src_n = src_n;
+    a.src_g0 = src_g0;
+    const long long total = rows * m.G * 8;
+    int grid = (int)std::min<long long>((total + 255) / 256, 65535);
+    if (grid < 1) grid = 1;
+    k_retile_f32<<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
 static cudaError_t retile(const MatDesc& m, const float* scales, const uint8_t* packed, long long rows, int row_offset,
                           int interleave, int slot, int inverse, cudaStream_t st, int src_G = 0, int src_g0 = 0) {
     RetileArgs a;
@@ -429,6 +448,11 @@ extern "C" AION_API aion_status aion_get_config(const aion_ctx* ctx, aion_config
 
 extern "C" AION_API const float* aion_logits_dev(const aion_ctx* ctx) { return ctx ? ctx->logits : nullptr; }
 
+extern "C" AION_API int32_t aion_get_mode(const aion_ctx* ctx) {
+    if (!ctx) return -1;
+    return ctx->mode == MODE_F32 ? AION_MODE_F32 : ctx->mode == MODE_W4A8 ? AION_MODE_W4A8 : AION_MODE_W4A16;
+}
+
 extern "C" AION_API void* aion_stream(const aion_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
 // Byte size of an int4 checkpoint for a header, 64-bit.
@@ -504,6 +528,7 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
 }
 
 static cudaError_t launch_decode(aion_ctx* c, int steps) {
+    if (c->mode == MODE_F32) return launch_decode_mode<MODE_F32>(c, steps);
     return c->mode == MODE_W4A8 ? launch_decode_mode<MODE_W4A8>(c, steps) : launch_decode_mode<MODE_W4A16>(c, steps);
 }
 
@@ -582,7 +607,19 @@ static aion_status validate_config(const aion_config& c, std::string* err) {
 
 // Reads and validates the 28-byte header and the file size (64-bit) before
 // any device work: a truncated or inconsistent file fails here.
-static aion_status read_header(const char* path, aion_config* cfg, std::string* err) {
+// Byte size of an fp32 llama2.c file (src/kernel_simd.c:906-936) for a
+// header, 64-bit; a negative vocab_size announces a separate classifier
+// after the RoPE tables, which the reference never reads.
+static long long f32_file_bytes(const aion_config& c, bool wcls) {
+    long long dim = c.dim, hid = c.hidden_dim, L = c.n_layers, nh = c.n_heads, nkv = c.n_kv_heads,
+              vocab = c.vocab_size, seq = c.seq_len;
+    long long hs = dim / nh, kv = dim * nkv / nh;
+    long long f = vocab * dim + L * dim + L * dim * dim + 2 * L * dim * kv + L * dim * dim + L * dim + 3 * L * dim * hid +
+                  dim + 2 * seq * (hs / 2) + (wcls ? vocab * dim : 0);
+    return 28 + 4 * f;
+}
+
+static aion_status read_header(const char* path, aion_config* cfg, std::string* err, bool* f32 = nullptr) {
     int fd = open(path, O_RDONLY);
     if (fd < 0) {
         set_err(err, "cannot open %s: %s", path, strerror(errno));
@@ -596,13 +633,17 @@ static aion_status read_header(const char* path, aion_config* cfg, std::string* 
         s = AION_ERR_FORMAT;
     } else {
         memcpy(cfg, hdr, 28);
+        const bool wcls = cfg->vocab_size < 0;
         if (cfg->vocab_size < 0) cfg->vocab_size = -cfg->vocab_size;  // src/kernel_simd.c:945
         s = validate_config(*cfg, err);
+        if (f32) *f32 = false;
         if (s == AION_OK) {
-            const long long want = int4_file_bytes(*cfg);
-            if (want != (long long)st.st_size) {
-                set_err(err, "%s: header implies %lld bytes for an int4 file, file has %lld", path, want,
-                        (long long)st.st_size);
+            const long long want = int4_file_bytes(*cfg), want_f = f32_file_bytes(*cfg, wcls);
+            if (f32 && want_f == (long long)st.st_size && want != want_f) {
+                *f32 = true;   // the reference's fp32 path (its CLI without "int4")
+            } else if (want != (long long)st.st_size) {
+                set_err(err, "%s: header implies %lld bytes for an int4 file (%lld for fp32), file has %lld", path,
+                        want, want_f, (long long)st.st_size);
                 s = AION_ERR_FORMAT;
             }
         }
@@ -705,9 +746,10 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         // Matrix layouts (pointers filled below).  Under tensor parallelism
         // this rank holds wq/wk/wv/w1/w3 rows [R/N, (R+1)/N) of each and
         // wo/w2 columns [R/N, (R+1)/N) (partial sums, summed across ranks).
-        c->emb = make_desc(nullptr, c->vocab, (int)dim);
-        MatDesc dq = make_desc(nullptr, ql + 2 * kvl, (int)dim), dwo = make_desc(nullptr, dim, (int)ql);
-        MatDesc d13 = make_desc(nullptr, 2 * hl, (int)dim), d2 = make_desc(nullptr, dim, (int)hl);
+        const int gb = c->mode == MODE_F32 ? kGBF : kGB;   // bytes per (tile, group)
+        c->emb = make_desc(nullptr, c->vocab, (int)dim, gb);
+        MatDesc dq = make_desc(nullptr, ql + 2 * kvl, (int)dim, gb), dwo = make_desc(nullptr, dim, (int)ql, gb);
+        MatDesc d13 = make_desc(nullptr, 2 * hl, (int)dim, gb), d2 = make_desc(nullptr, dim, (int)hl, gb);
 
         size_t bytes = align256(desc_bytes(c->emb));
         bytes += L * (align256(desc_bytes(dq)) + align256(desc_bytes(dwo)) + align256(desc_bytes(d13)) +
@@ -726,7 +768,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
 
         c->emb.w = arena_take(c, desc_bytes(c->emb));
         // Classifier rows of this rank: tiles [vocab_off / 16, ...) of the embedding.
-        c->cls = make_desc(c->emb.w + (size_t)(c->vocab_off / kTR) * c->emb.tile_bytes, c->vocab_l, (int)dim);
+        c->cls = make_desc(c->emb.w + (size_t)(c->vocab_off / kTR) * c->emb.tile_bytes, c->vocab_l, (int)dim, gb);
         c->qkv.assign(L, dq); c->wo.assign(L, dwo); c->w13.assign(L, d13); c->w2.assign(L, d2);
         for (long long l = 0; l < L; l++) {
             c->qkv[l].w = arena_take(c, desc_bytes(dq));
@@ -763,6 +805,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
 
         auto qb = [](long long cnt) { return cnt / 32 * 4 + cnt / 2; };
         long long stage = std::max({qb(c->vocab * dim), qb(L * dim * hid), qb(L * dim * dim)}) + 256;
+        if (c->mode == MODE_F32) stage = std::max(c->vocab, hid) * dim * 4 + 256;   // one fp32 matrix at a time
         CK_RET(&c->err, cudaMalloc(&staging, (size_t)stage));
         CK_RET(&c->err, cudaHostAlloc(&pinned[0], chunk, cudaHostAllocDefault));
         CK_RET(&c->err, cudaHostAlloc(&pinned[1], chunk, cudaHostAllocDefault));
@@ -810,6 +853,45 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
                 return cudaSuccess;
             };
         };
+        if (c->mode == MODE_F32) {
+            // The fp32 file (src/kernel_simd.c:924-936): each matrix of each
+            // layer goes through the staging buffer into fp32 tiles; the
+            // classifier stays tied to the embedding, as in the reference.
+            auto fmat = [&](long long rows, long long n, long long r0, long long take, long long g0, const MatDesc& dst,
+                            int row_offset, int interleave, int slot) -> aion_status {
+                aion_status r = upload_range(c, fd, off, rows * n * 4, staging, pinned, ev, chunk);
+                if (r != AION_OK) return r;
+                cudaError_t e = retile_f32(dst, (const float*)staging + r0 * n, take, row_offset, interleave, slot,
+                                           (int)n, (int)g0, c->stream);
+                if (e != cudaSuccess) {
+                    set_err(&c->err, "re-tile failed: %s", cudaGetErrorString(e));
+                    return AION_ERR_CUDA;
+                }
+                off += rows * n * 4;
+                return AION_OK;
+            };
+            auto flayers = [&](long long rows, long long n, long long r0, long long take, long long g0,
+                               std::vector<MatDesc>& dst, int row_offset, int interleave, int slot) -> aion_status {
+                for (long long l = 0; l < L; l++) {
+                    aion_status r = fmat(rows, n, r0, take, g0, dst[l], row_offset, interleave, slot);
+                    if (r != AION_OK) return r;
+                }
+                return AION_OK;
+            };
+            if ((s = fmat(c->vocab, dim, 0, c->vocab, 0, c->emb, 0, 0, 0)) != AION_OK) break;
+            if ((s = ftensor(L * dim, c->rms_att)) != AION_OK) break;
+            if ((s = flayers(dim, dim, 0, ql, 0, c->qkv, 0, 0, 0)) != AION_OK) break;
+            if ((s = flayers(kv, dim, 0, kvl, 0, c->qkv, (int)ql, 0, 0)) != AION_OK) break;
+            if ((s = flayers(kv, dim, 0, kvl, 0, c->qkv, (int)(ql + kvl), 0, 0)) != AION_OK) break;
+            if ((s = flayers(dim, dim, 0, dim, 0, c->wo, 0, 0, 0)) != AION_OK) break;
+            if ((s = ftensor(L * dim, c->rms_ffn)) != AION_OK) break;
+            if ((s = flayers(hid, dim, 0, hl, 0, c->w13, 0, 1, 0)) != AION_OK) break;
+            if ((s = flayers(dim, hid, 0, dim, 0, c->w2, 0, 0, 0)) != AION_OK) break;
+            if ((s = flayers(hid, dim, 0, hl, 0, c->w13, 0, 1, 1)) != AION_OK) break;
+            if ((s = ftensor(dim, c->rms_final)) != AION_OK) break;
+            if ((s = ftensor(c->seq * (c->hs / 2), c->freq_re)) != AION_OK) break;
+            if ((s = ftensor(c->seq * (c->hs / 2), c->freq_im)) != AION_OK) break;
+        } else {
         if ((s = qtensor(c->vocab * dim, [&](const float* sc, const uint8_t* pk) {
                  cudaError_t e = retile(c->emb, sc, pk, c->vocab, 0, 0, 0, 0, c->stream);
                  return e != cudaSuccess ? e : fill_pad(c->emb, c->stream);
@@ -835,6 +917,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
             if (e == cudaSuccess) e = fill_pad(c->w2[l], c->stream);
             CK_RET(&c->err, e);
         }
+        }   // int4 file
 
         // Op table of one token.
         std::vector<OpDesc> ops;
@@ -851,8 +934,9 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         CK_RET(&c->err, cudaMemcpyAsync(c->ops, ops.data(), ops.size() * sizeof(OpDesc), cudaMemcpyHostToDevice,
                                         c->stream));
         const int max_n = (int)std::max(dim, hid);
-        s = c->mode == MODE_W4A8 ? setup_decode_kernel<MODE_W4A8>(c, max_n, max_chunk)
-                                 : setup_decode_kernel<MODE_W4A16>(c, max_n, max_chunk);
+        s = c->mode == MODE_W4A8  ? setup_decode_kernel<MODE_W4A8>(c, max_n, max_chunk)
+            : c->mode == MODE_F32 ? setup_decode_kernel<MODE_F32>(c, max_n, max_chunk)
+                                  : setup_decode_kernel<MODE_W4A16>(c, max_n, max_chunk);
         if (s != AION_OK) break;
         if (c->mode == MODE_W4A8) {   // the bit-exact mode follows the host expf
             const HostExpTable& t = host_exp_table();
@@ -915,10 +999,20 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
     c->nseq = c->opts.max_batch;
     c->mode = c->opts.mode == AION_MODE_W4A8 ? MODE_W4A8 : MODE_W4A16;
     c->dev = c->opts.device;
-    aion_status hs = read_header(path, &c->cfg, &c->err);
+    bool f32 = false;
+    aion_status hs = read_header(path, &c->cfg, &c->err, &f32);
     if (hs != AION_OK) {
         delete c;
         return hs;
+    }
+    if (f32) {
+        if (c->mode == MODE_W4A8 || c->tp_n > 1) {
+            set_err(&c->err, "%s is an fp32 file: it runs the fp32 path on one GPU (no W4A8, no tensor parallelism)",
+                    path);
+            delete c;
+            return AION_ERR_ARG;
+        }
+        c->mode = MODE_F32;
     }
     cudaError_t e = cudaSetDevice(c->dev);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
@@ -1153,8 +1247,8 @@ static aion_status pf_matmul(aion_ctx* c, const MatDesc& w, long long mpad, long
 extern "C" AION_API aion_status aion_prefill(aion_ctx* c, const int32_t* tokens, int32_t n_seq, int32_t n_tok,
                                              float* logits_host) {
     if (!c || !tokens || n_seq < 1 || n_tok < 1) return AION_ERR_ARG;
-    if (c->tp_n > 1) {
-        set_err(&c->err, "aion_prefill is not available with tensor parallelism");
+    if (c->tp_n > 1 || c->mode == MODE_F32) {
+        set_err(&c->err, "aion_prefill needs an int4 file on one GPU");
         return AION_ERR_STATE;
     }
     if (n_seq > c->nseq || n_tok > c->max_pos) {

@@ -90,8 +90,19 @@ struct VecSrc {
     int tok = 0;
 };
 
+// Elements 4i..4i+3 of an fp32 tile row (the fp32 path's embedding row).
+__device__ __forceinline__ float4 emb_load4_f32(const MatDesc& emb, int tok, int i) {
+    const int g = i >> 3, e4 = i & 7;
+    const int rr = tok % kTR, rl = rr & 7, half = rr >> 3;
+    const int q = half * 2 + (e4 & 1), ln = 4 * rl + (e4 >> 1);
+    const float* base = reinterpret_cast<const float*>(emb.w);
+    return __ldg(reinterpret_cast<const float4*>(base + ((size_t)(tok / kTR) * emb.G + g) * 512 + (q * 32 + ln) * 4));
+}
+
+template <int MODE = MODE_W4A16>
 __device__ __forceinline__ float4 src_load4(const VecSrc& s, int i) {
     if (s.p) return __ldcg(reinterpret_cast<const float4*>(s.p) + i);
+    if (MODE == MODE_F32) return emb_load4_f32(s.emb, s.tok, i);
     // elements 4i..4i+3 of row tok: group g, elements k..k+3 of the group
     const int g = i >> 3, k = (i & 7) * 4;
     const long long R = s.tok;
@@ -166,7 +177,7 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
 #pragma unroll
     for (int i = 0; i < NV; i++) {
         const int j = tid + i * kThreads;
-        v[i] = j < nv ? src_load4(s, j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        v[i] = j < nv ? src_load4<MODE>(s, j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (NORM) w[i] = j < nv ? __ldg(reinterpret_cast<const float4*>(norm_w) + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
     if (NORM) {
@@ -206,6 +217,15 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
             v[i].z = __fmul_rn(__fmul_rn(v[i].z, ss), w[i].z);
             v[i].w = __fmul_rn(__fmul_rn(v[i].w, ss), w[i].w);
         }
+    }
+    if (MODE == MODE_F32) {
+        // The fp32 path keeps the input as fp32, [G][32] in the digit area.
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            const int j = tid + i * kThreads;
+            if (j < nv) reinterpret_cast<float4*>(xf)[j] = v[i];
+        }
+        return;
     }
     // W4A16: one exponent for the vector, from its largest magnitude M;
     // vectors with M < 2^-93 count as zero.
@@ -937,7 +957,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
         emb_src.tok = tok;
         if (blockIdx.x == 0)   // x = embedding row, for the residual stream
             for (int i = threadIdx.x; i < a.dim / 4; i += kThreads)
-                __stcg(reinterpret_cast<float4*>(a.x) + i, src_load4(emb_src, i));
+                __stcg(reinterpret_cast<float4*>(a.x) + i, src_load4<MODE>(emb_src, i));
 
         for (int oi = 0; oi < a.nops && ok; oi++) {
             const OpDesc op = ops[oi];

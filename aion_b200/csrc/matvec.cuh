@@ -42,22 +42,29 @@ constexpr int kTargetChunk = 6400;   // bytes per bulk copy, about
 constexpr int kXF = 128;             // bytes of activation digits per group (4 columns)
 constexpr int kMaxLocalTiles = 24;   // tiles of one op per CTA (split mode)
 
-enum Mode { MODE_W4A16 = 0, MODE_W4A8 = 1 };
+enum Mode { MODE_W4A16 = 0, MODE_W4A8 = 1, MODE_F32 = 2 };
+
+// fp32 tiles (the reference's fp32 path): per (tile, group) 4 x 32 float4,
+// entry (q, lane) = row r (q < 2) or r + 8 (q >= 2), columns 8t + 4(q & 1)
+// .. +3 of the group, for lane = 4r + t; 2048 bytes.
+constexpr int kGBF = 2048;
 
 struct MatDesc {
     const uint8_t* w;
-    long long tile_bytes;          // G * 320
+    long long tile_bytes;          // G * gbytes
     int n, G, nch;                 // columns, groups per row, chunks per tile
     int cg, cr;                    // chunk c spans cg groups, one more for c < cr
     int ntiles, d;                 // tiles, logical rows
+    int gbytes;                    // bytes per (tile, group): kGB (int4) or kGBF (fp32)
 };
 
-__host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, int n) {
+__host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, int n, int gbytes = kGB) {
     MatDesc m;
     m.w = w;
     m.n = n;
     m.G = n / 32;
-    m.tile_bytes = (long long)m.G * kGB;
+    m.gbytes = gbytes;
+    m.tile_bytes = (long long)m.G * gbytes;
     m.nch = (int)((m.tile_bytes + kTargetChunk - 1) / kTargetChunk);
     if (m.nch < 1) m.nch = 1;
     if (m.nch > m.G) m.nch = m.G;
@@ -70,7 +77,7 @@ __host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, i
 
 __host__ __device__ inline long long desc_bytes(const MatDesc& m) { return m.tile_bytes * m.ntiles; }
 __host__ __device__ inline int chunk_g0(const MatDesc& m, int c) { return c * m.cg + (c < m.cr ? c : m.cr); }
-__host__ __device__ inline int max_chunk_bytes(const MatDesc& m) { return (m.cg + (m.cr ? 1 : 0)) * kGB; }
+__host__ __device__ inline int max_chunk_bytes(const MatDesc& m) { return (m.cg + (m.cr ? 1 : 0)) * m.gbytes; }
 
 // ---------------------------------------------------------------------------
 // Activation digits in shared memory: group g at g*128: digit column p
@@ -124,6 +131,36 @@ __device__ __forceinline__ void group_accumulate(const int (&d)[4], float2 sw, f
 template <int MODE>
 __device__ __forceinline__ void chunk_mma(const unsigned char* chunk, int ng, int g0, const unsigned char* xf,
                                           const float* xs, float& acc0, float& acc1) {
+    if constexpr (MODE == MODE_F32) {
+        // fp32 tiles on the CUDA cores: lane 4r + t adds rows r and r + 8
+        // over columns 8t..8t+7 of every group; xf holds x as fp32 [G][32].
+        const int ln = threadIdx.x & 31, tq = ln & 3;
+        const float4* wp = reinterpret_cast<const float4*>(chunk) + ln;
+        const float* xp = reinterpret_cast<const float*>(xf) + (size_t)g0 * 32 + 8 * tq;
+#pragma unroll 2
+        for (int k = 0; k < ng; k++) {
+            const float4 w0 = wp[k * 128], w1 = wp[k * 128 + 32], w2 = wp[k * 128 + 64], w3 = wp[k * 128 + 96];
+            const float4 x0 = *reinterpret_cast<const float4*>(xp + k * 32);
+            const float4 x1 = *reinterpret_cast<const float4*>(xp + k * 32 + 4);
+            acc0 = fmaf(w0.x, x0.x, acc0);
+            acc0 = fmaf(w0.y, x0.y, acc0);
+            acc0 = fmaf(w0.z, x0.z, acc0);
+            acc0 = fmaf(w0.w, x0.w, acc0);
+            acc0 = fmaf(w1.x, x1.x, acc0);
+            acc0 = fmaf(w1.y, x1.y, acc0);
+            acc0 = fmaf(w1.z, x1.z, acc0);
+            acc0 = fmaf(w1.w, x1.w, acc0);
+            acc1 = fmaf(w2.x, x0.x, acc1);
+            acc1 = fmaf(w2.y, x0.y, acc1);
+            acc1 = fmaf(w2.z, x0.z, acc1);
+            acc1 = fmaf(w2.w, x0.w, acc1);
+            acc1 = fmaf(w3.x, x1.x, acc1);
+            acc1 = fmaf(w3.y, x1.y, acc1);
+            acc1 = fmaf(w3.z, x1.z, acc1);
+            acc1 = fmaf(w3.w, x1.w, acc1);
+        }
+        return;
+    }
     const int lane = threadIdx.x & 31;
     const int r = lane >> 2;
     const unsigned char* wp = chunk + 8 * lane;
@@ -180,6 +217,12 @@ __device__ __forceinline__ void chunk_mma(const unsigned char* chunk, int ng, in
 // already.
 template <int MODE>
 __device__ __forceinline__ void quad_reduce(float& acc0, float& acc1, float xfactor) {
+    if (MODE == MODE_F32) {
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 2);
+        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 2);
+    }
     if (MODE == MODE_W4A16) {
         const float h0 = __shfl_xor_sync(0xffffffffu, acc0, 1);
         const float h1 = __shfl_xor_sync(0xffffffffu, acc1, 1);
@@ -316,7 +359,7 @@ struct OpWork {
 __device__ __forceinline__ OpWork op_work(const MatDesc& m, int mode) {
     OpWork w;
     const int G = gridDim.x, c = blockIdx.x;
-    w.split = (mode == MODE_W4A16 && m.ntiles >= G && m.ntiles <= (kMaxLocalTiles - 2) * G) ? 1 : 0;
+    w.split = (mode != MODE_W4A8 && m.ntiles >= G && m.ntiles <= (kMaxLocalTiles - 2) * G) ? 1 : 0;
     const long long U = w.split ? (long long)m.ntiles * m.nch : m.ntiles;
     if (U * G < (1LL << 31)) {   // 32-bit division when the products fit
         const uint32_t u = (uint32_t)U;
@@ -364,8 +407,8 @@ __device__ __forceinline__ bool cursor_next(OpCursor& cu, const OpWork& w, const
 
 __device__ __forceinline__ const uint8_t* chunk_src(const MatDesc& m, int tile, int c, int& bytes) {
     const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
-    bytes = (g1 - g0) * kGB;
-    return m.w + (size_t)tile * m.tile_bytes + (size_t)g0 * kGB;
+    bytes = (g1 - g0) * m.gbytes;
+    return m.w + (size_t)tile * m.tile_bytes + (size_t)g0 * m.gbytes;
 }
 
 // ---------------------------------------------------------------------------
@@ -428,6 +471,33 @@ __global__ void k_retile(RetileArgs a) {
             *reinterpret_cast<uint4*>(spk) = *reinterpret_cast<const uint4*>(out);
             *ssc = *dsc;
         }
+    }
+}
+
+// fp32 rows -> fp32 tiles (same row mapping as k_retile).  Thread per
+// (row, group, 4 columns).
+struct RetileF32Args {
+    const float* src;            // [rows][src_n]
+    MatDesc m;
+    long long rows;
+    int row_offset, interleave, slot;
+    int src_n, src_g0;           // source row length, first source group of the tiles' columns
+};
+
+__global__ void k_retile_f32(RetileF32Args a) {
+    const int G = a.m.G;
+    const long long total = a.rows * G * 8;
+    float* base = reinterpret_cast<float*>(const_cast<uint8_t*>(a.m.w));
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / (8LL * G);
+        const int g = (int)((i / 8) % G), e4 = (int)(i % 8);
+        const long long R = a.interleave ? (r / 2) * 4 + (r % 2) + a.slot * 2 : a.row_offset + r;
+        const int rr = (int)(R % kTR), rl = rr & 7, half = rr >> 3;
+        const int q = half * 2 + (e4 & 1), ln = 4 * rl + (e4 >> 1);
+        float* dst = base + ((R / kTR) * G + g) * 512 + (q * 32 + ln) * 4;
+        const float* src = a.src + r * a.src_n + (a.src_g0 + g) * 32 + 4 * e4;
+        *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
     }
 }
 

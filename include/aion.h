@@ -45,7 +45,9 @@ typedef struct aion_config {
     int32_t dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len;
 } aion_config;
 
-enum { AION_MODE_W4A16 = 0, AION_MODE_W4A8 = 1 };
+/* AION_MODE_F32: the reference's fp32 path (its CLI without "int4"); chosen
+ * by aion_load when the file is an fp32 llama2.c checkpoint. */
+enum { AION_MODE_W4A16 = 0, AION_MODE_W4A8 = 1, AION_MODE_F32 = 2 };
 
 typedef struct aion_opts {
     int32_t device;     /* CUDA device ordinal                                        */
@@ -77,7 +79,12 @@ AION_API const char* aion_last_error(const aion_ctx* ctx);
  * (:991-1008).  Validates the file size against the header in 64-bit
  * arithmetic before any upload, uploads every tensor once to HBM re-tiled
  * for the decode kernels, allocates the KV cache and activations, and
- * unmaps the file.  The context owns all device memory. */
+ * unmaps the file.  The context owns all device memory.
+ * An fp32 llama2.c file (load_checkpoint, :906-936; a negative vocab_size
+ * adds a separate classifier that, as in the reference, is not read) runs
+ * the fp32 path: fp32 weights and activations, the classifier tied to the
+ * embedding.  It needs tp_size 1 and a mode other than W4A8; prefill and
+ * batched decode need an int4 file. */
 AION_API aion_status aion_load(const char* int4_path, const aion_opts* opts, aion_ctx** out);
 AION_API aion_status aion_free(aion_ctx* ctx);
 AION_API aion_status aion_get_config(const aion_ctx* ctx, aion_config* out);
@@ -90,6 +97,10 @@ AION_API aion_status aion_forward(aion_ctx* ctx, int32_t token, int32_t pos, flo
 
 /* Device pointer to the logits of the last decode step ([vocab] fp32). */
 AION_API const float* aion_logits_dev(const aion_ctx* ctx);
+
+/* The mode the context runs: AION_MODE_W4A16, AION_MODE_W4A8 or
+ * AION_MODE_F32 (an fp32 file); -1 for NULL. */
+AION_API int32_t aion_get_mode(const aion_ctx* ctx);
 
 /* Replaces the greedy loop of main (src/kernel_simd.c:1223-1258): starts at
  * pos 0 from `bos`, runs `steps` forward steps, picks the first index of the
