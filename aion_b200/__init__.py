@@ -103,6 +103,10 @@ def lib() -> ctypes.CDLL:
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_decode_batch": (I32, [VP, I32, I32, VP, VP, VP, VP]),
         "aion_get_mode": (I32, [VP]),
+        "aion_tokenizer_load": (I32, [ctypes.c_char_p, I32, VP]),
+        "aion_tokenizer_free": (None, [VP]),
+        "aion_encode": (I32, [VP, ctypes.c_char_p, I32, I32, VP, I32, VP]),
+        "aion_decode": (ctypes.c_char_p, [VP, I32, I32]),
         "aion_set_sampler": (I32, [VP, VP]),
         "aion_read_logits": (I32, [VP, VP]),
         "aion_set_sequence": (I32, [VP, I32]),
@@ -175,6 +179,49 @@ def quantize_buffer(w: np.ndarray):
 # ---------------------------------------------------------------------------
 # Model level
 # ---------------------------------------------------------------------------
+class Tokenizer:
+    """llama2.c tokenizer.bin: encode text to token ids, decode ids to text
+    (aion_tokenizer_load / aion_encode / aion_decode)."""
+
+    def __init__(self, path, vocab_size: int):
+        h = ctypes.c_void_p()
+        _check(lib().aion_tokenizer_load(str(path).encode(), vocab_size, ctypes.byref(h)))
+        self._h = h
+
+    def encode(self, text: str, bos: bool = True, eos: bool = False) -> list[int]:
+        raw = text.encode("utf-8")
+        out = np.empty(len(raw) + 3, np.int32)
+        n = ctypes.c_int32()
+        _check(lib().aion_encode(self._h, raw, 1 if bos else 0, 1 if eos else 0, _ptr(out), out.size, ctypes.byref(n)))
+        return out[:n.value].tolist()
+
+    def decode_bytes(self, prev: int, token: int) -> bytes:
+        p = lib().aion_decode(self._h, prev, token)
+        if p is None:
+            raise ValueError(f"token {token} out of range")
+        return p
+
+    def decode(self, tokens) -> str:
+        """Concatenated text of a token stream (BOS and EOS contribute nothing)."""
+        out, prev = b"", -1
+        for t in tokens:
+            if t not in (1, 2):
+                out += self.decode_bytes(prev, t)
+            prev = t
+        return out.decode("utf-8", errors="replace")
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().aion_tokenizer_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def tp_plan(cfg7, tp_size: int, tp_rank: int) -> dict:
     """Rows and columns that rank tp_rank of tp_size holds (aion_tp_plan)."""
     c = Config(*cfg7)

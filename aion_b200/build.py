@@ -30,7 +30,7 @@ CC_FLAGS = ["-O2", "-std=gnu11", "-fPIC", "-fvisibility=hidden", "-ffp-contract=
             "-Wno-unused-result"]
 
 CUDA_SOURCES = ["aion_runtime.cu"]
-C_SOURCES = ["aion_ckpt.c"]
+C_SOURCES = ["aion_ckpt.c", "aion_tok.c"]
 
 
 def _nvcc() -> str:

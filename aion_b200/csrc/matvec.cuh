@@ -65,7 +65,10 @@ __host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, i
     m.G = n / 32;
     m.gbytes = gbytes;
     m.tile_bytes = (long long)m.G * gbytes;
-    m.nch = (int)((m.tile_bytes + kTargetChunk - 1) / kTargetChunk);
+    // fp32 groups are 6.4x larger: about two per copy, so two ring slots per
+    // warp still fit next to an 11008-wide fp32 input.
+    const int target = gbytes == kGB ? kTargetChunk : 2 * gbytes;
+    m.nch = (int)((m.tile_bytes + target - 1) / target);
     if (m.nch < 1) m.nch = 1;
     if (m.nch > m.G) m.nch = m.G;
     m.cg = m.G / m.nch;

@@ -351,6 +351,49 @@ def isolated_matvecs(device: int, reps: int, shapes=None) -> dict:
     return out
 
 
+def run_fp32(args, local: int) -> None:
+    """7B-shape fp32 llama2.c checkpoint (the reference's fp32 path): batch-1
+    greedy decode from BOS, one persistent launch, weights 4 bytes each."""
+    import torch
+    import aion_b200 as A
+    L = args.profile_layers if args.profile_layers > 0 else CFG_7B[2]
+    cfg = (CFG_7B[0], CFG_7B[1], L) + CFG_7B[3:]
+    path = ckpt_dir() / f"llama2_7b_shape_{L}l_seed1.f32"
+    done = path.with_suffix(".done")
+    if not done.exists():
+        tmp = path.with_suffix(".tmp")
+        A.synth_checkpoint(tmp, cfg, SEED_7B, int4=False)
+        tmp.rename(path)
+        done.write_text("ok")
+    model = A.Model(path, device=local, max_pos=args.steps + args.warmup + 1)
+    assert model.mode == "f32"
+    stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{local}")
+    model.decode_async(args.warmup, BOS, 0)
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    model.decode_async(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    dim, hid, vocab = CFG_7B[0], CFG_7B[1], CFG_7B[5]
+    wb = 4 * (L * (4 * dim * dim + 3 * dim * hid) + vocab * dim)
+    gbs = wb * args.steps / (ms * 1e-3) / 1e9
+    peak, kind = hbm_peak()
+    print(json.dumps({
+        "metric": "Llama-2-7B fp32 decode tok/s (batch 1, fp32 checkpoint)", "value": args.steps / (ms * 1e-3),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"llama2-7b-shape fp32 greedy decode from BOS, {L} layers", "layers": L, "seed": 1},
+        "roofline": {"kernel": "k_decode<F32> (persistent decode, fp32 tiles)", "bound": "hbm", "achieved": gbs,
+                     "peak": peak, "peak_kind": kind, "unit": "GB/s", "frac": gbs / peak, "bytes_per_token": wb},
+        "gpu_launches": 1, "clocks": clk, "token_stream_head": model.tokens(16)}), flush=True)
+    model.close()
+
+
 def run_batch(args, local: int) -> None:
     """7B-shape lock-step batched decode: args.batch sequences from BOS,
     args.steps greedy steps each (positions 0..steps-1), one launch."""
@@ -490,6 +533,7 @@ def main() -> None:
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
     ap.add_argument("--tp13b", action="store_true", help="13B shape, tensor-parallel over the launch's ranks")
     ap.add_argument("--batch", type=int, default=0, help="7B lock-step batched decode of this many sequences")
+    ap.add_argument("--fp32", action="store_true", help="7B-shape fp32 checkpoint (the reference's fp32 path)")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling only: 7B shapes truncated to this many layers")
     args = ap.parse_args()
@@ -530,6 +574,11 @@ def main() -> None:
     if args.batch > 0:
         if rank == 0:
             run_batch(args, local)
+        return
+
+    if args.fp32:
+        if rank == 0:
+            run_fp32(args, local)
         return
 
     if args.matvec:

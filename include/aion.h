@@ -212,6 +212,30 @@ AION_API aion_status aion_set_sampler(aion_ctx* ctx, const aion_sampler* sampler
 AION_API aion_status aion_read_logits(aion_ctx* ctx, float* host);
 
 /* ---------------------------------------------------------------------------
+ * Text I/O (no counterpart in the reference, which reads and prints token
+ * ids only, src/kernel_simd.c:1245): llama2.c tokenizer.bin files.
+ * ------------------------------------------------------------------------- */
+typedef struct aion_tokenizer aion_tokenizer;
+
+/* Reads tokenizer.bin (int32 max_token_length, then per token: float score,
+ * int32 length, the bytes) for vocab_size tokens. */
+AION_API aion_status aion_tokenizer_load(const char* path, int32_t vocab_size, aion_tokenizer** out);
+AION_API void aion_tokenizer_free(aion_tokenizer* tok);
+
+/* Byte-pair encoding of UTF-8 text: a leading " " token (dummy prefix) for
+ * non-empty text, one token per code point found in the vocabulary else
+ * byte-fallback tokens (byte + 3), then repeated merges of the adjacent
+ * pair whose concatenation has the highest score.  Optional BOS (1) first
+ * and EOS (2) last.  capacity >= strlen(text) + 3. */
+AION_API aion_status aion_encode(const aion_tokenizer* tok, const char* text, int32_t bos, int32_t eos,
+                                 int32_t* tokens, int32_t capacity, int32_t* n_out);
+
+/* The text of `token` following `prev`: its piece, without the leading
+ * space right after BOS; a byte-fallback piece "<0xHH>" is that byte.
+ * NULL for an id out of range.  The pointer lives as long as tok. */
+AION_API const char* aion_decode(const aion_tokenizer* tok, int32_t prev, int32_t token);
+
+/* ---------------------------------------------------------------------------
  * Kernel level (device pointers; stream = cudaStream_t or NULL)
  * ------------------------------------------------------------------------- */
 
