@@ -250,7 +250,7 @@ def prefill_leg(model, layers: int, stream, device: int) -> dict:
     import torch
     dim, hid, vocab = CFG_7B[0], CFG_7B[1], CFG_7B[5]
     toks = np.random.default_rng(PREFILL_SEED).integers(0, vocab, (PREFILL_SEQ, PREFILL_TOK)).astype(np.int32)
-    model.prefill(toks[:2, :64])          # warm-up: buffers, tensor maps, module load
+    model.prefill(toks)                   # warm-up at full size: buffers, tensor maps, module load
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
