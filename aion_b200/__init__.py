@@ -302,7 +302,7 @@ class Model:
         if f.size != p.size:
             raise ValueError("first_tokens and pos0 differ in length")
         toks = np.empty((steps + 1, f.size), np.int32)
-        lg = np.empty((f.size, self.config.vocab_size), np.float32) if want_logits else None
+        lg = np.empty((f.size, self.config.vocab_size // self.tp_size), np.float32) if want_logits else None
         _check(lib().aion_decode_batch(self._h, f.size, steps, _ptr(f), _ptr(p), _ptr(toks),
                                        _ptr(lg) if lg is not None else None), self._h)
         return toks, lg

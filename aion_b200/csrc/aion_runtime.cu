@@ -265,6 +265,8 @@ struct aion_ctx {
     unsigned char* xr = nullptr;   // exchange region (receive rows, keys, flags)
     size_t xr_bytes = 0;
     int xr_keys_off = 0, xr_flags_off = 0;
+    long long xr_brecv_off = 0, xr_bkeys_off = 0;   // batched decode: partial rows, argmax keys
+    int xr_nbmax = 0;
     std::vector<unsigned char*> peers;           // exchange regions of every rank (IPC-mapped)
     unsigned char** peers_dev = nullptr;         // the same pointers in device memory
     bool tp_connected = false;
@@ -986,11 +988,6 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
     }
     c->tp_n = c->opts.tp_size;
     c->tp_rank = c->opts.tp_rank;
-    if (c->tp_n > 1 && c->opts.max_batch > 1) {
-        set_err(&c->err, "max_batch > 1 (batched prefill) is not available with tensor parallelism");
-        delete c;
-        return AION_ERR_ARG;
-    }
     if (c->opts.max_batch < 1 || c->opts.max_batch > 1024) {
         set_err(&c->err, "max_batch %d out of range [1, 1024]", c->opts.max_batch);
         delete c;
@@ -1025,11 +1022,20 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
     aion_status s = load_impl(c, path);
     if (s == AION_OK && c->tp_n > 1) {
         // Exchange region: tagged receive rows [2][tp_n][dim] u64, keys [tp_n] u64,
-        // flags [tp_n] u32; shared with the other ranks by aion_tp_connect.
+        // flags [tp_n] u32; then the batched decode's receive rows
+        // [2][tp_n][nbmax][dim] u64 (nbmax = min(max_batch, 32)) and keys
+        // [tp_n][32] u64.
+        // Shared with the other ranks by aion_tp_connect.
         const size_t recv = align256((size_t)2 * c->tp_n * c->dim * 8), keys = align256((size_t)c->tp_n * 8);
+        const size_t flags = align256((size_t)c->tp_n * 4);
+        c->xr_nbmax = std::min(c->nseq, kBMaxSeq);
+        const size_t brecv = align256((size_t)2 * c->tp_n * c->xr_nbmax * c->dim * 8);
+        const size_t bkeys = align256((size_t)c->tp_n * kBMaxSeq * 8);
         c->xr_keys_off = (int)recv;
         c->xr_flags_off = (int)(recv + keys);
-        c->xr_bytes = recv + keys + align256((size_t)c->tp_n * 4);
+        c->xr_brecv_off = (long long)(recv + keys + flags);
+        c->xr_bkeys_off = c->xr_brecv_off + (long long)brecv;
+        c->xr_bytes = recv + keys + flags + brecv + bkeys;
         cudaError_t e2 = cudaMalloc(&c->xr, c->xr_bytes);
         if (e2 == cudaSuccess) e2 = cudaMemset(c->xr, 0, c->xr_bytes);
         if (e2 == cudaSuccess) e2 = cudaMalloc(&c->peers_dev, (size_t)c->tp_n * sizeof(unsigned char*));
@@ -1718,6 +1724,15 @@ static aion_status batch_launch(aion_ctx* c, int nb, int steps) {
     a.ops_off = pl.ops_off;
     a.samp = c->samp;
     a.sampling = c->sampling;
+    a.vocab_rows = (int)c->vocab_l;
+    a.vocab_off = (int)c->vocab_off;
+    a.tp_n = c->tp_n;
+    a.tp_rank = c->tp_rank;
+    a.tp_nbmax = c->xr_nbmax;
+    a.tp_peers = c->peers_dev;
+    a.tp_brecv_off = c->xr_brecv_off;
+    a.tp_bkeys_off = c->xr_bkeys_off;
+    a.tp_flags_off = c->xr_flags_off;
     CK_RET(&c->err, cudaMemsetAsync(&c->step->barrier, 0, sizeof(uint32_t), c->stream));
     CK_RET(&c->err, launch_ex(k_decode_batch<NBLK>, dim3(dev_info(c->dev).sms), dim3(kDecodeThreads), (size_t)pl.total,
                               c->stream, false, true, a));
@@ -1727,9 +1742,13 @@ static aion_status batch_launch(aion_ctx* c, int nb, int steps) {
 extern "C" AION_API aion_status aion_decode_batch(aion_ctx* c, int32_t n_seq, int32_t steps, const int32_t* first_tokens,
                                                   const int32_t* pos0, int32_t* tokens, float* logits) {
     if (!c || !first_tokens || !pos0 || !tokens) return AION_ERR_ARG;
-    if (c->mode != MODE_W4A16 || c->tp_n > 1) {
-        set_err(&c->err, "aion_decode_batch runs the W4A16 mode on one GPU");
+    if (c->mode != MODE_W4A16) {
+        set_err(&c->err, "aion_decode_batch runs the W4A16 mode (an int4 file)");
         return AION_ERR_STATE;
+    }
+    {
+        const aion_status ready = tp_ready(c);
+        if (ready != AION_OK) return ready;
     }
     const int cap = std::min(c->nseq, kBMaxSeq);
     if (n_seq < 1 || n_seq > cap || steps < 1) {
@@ -1743,7 +1762,7 @@ extern "C" AION_API aion_status aion_decode_batch(aion_ctx* c, int32_t n_seq, in
                     first_tokens[b], pos0[b], steps);
             return AION_ERR_ARG;
         }
-    if ((c->dim / 32 + dev_info(c->dev).sms - 1) / dev_info(c->dev).sms > kBMaxResGroups || c->vocab % 4) {
+    if ((c->dim / 32 + dev_info(c->dev).sms - 1) / dev_info(c->dev).sms > kBMaxResGroups || c->vocab_l % 4) {
         set_err(&c->err, "aion_decode_batch: dim %lld or vocab %lld unsupported", c->dim, c->vocab);
         return AION_ERR_SHAPE;
     }
@@ -1777,7 +1796,7 @@ extern "C" AION_API aion_status aion_decode_batch(aion_ctx* c, int32_t n_seq, in
     CK_RET(&c->err, cudaMemcpyAsync(tokens, bt.tokens, ((size_t)steps + 1) * n_seq * 4, cudaMemcpyDeviceToHost,
                                     c->stream));
     if (logits)
-        CK_RET(&c->err, cudaMemcpyAsync(logits, bt.logits, (size_t)n_seq * c->vocab * 4, cudaMemcpyDeviceToHost,
+        CK_RET(&c->err, cudaMemcpyAsync(logits, bt.logits, (size_t)n_seq * c->vocab_l * 4, cudaMemcpyDeviceToHost,
                                         c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return check_device_error(c);

@@ -89,6 +89,19 @@ struct BatchArgs {
     int P;                   // ring slots per warp (kBChunkBytes each)
     SamplerParams samp;      // used when sampling != 0 (else the greedy argmax)
     int sampling;
+    int vocab_rows;          // classifier rows this GPU holds (logits stride): vocab, or vocab / tp_n
+    // Tensor parallelism over tp_n GPUs (tp_n == 1: off), as in k_decode:
+    // this rank holds q_dim query rows, kv_dim K/V rows, hidden FFN rows and
+    // classifier rows [vocab_off, vocab_off + vocab_rows); WO and W2 give
+    // partial sums over its slice of their inputs.  tp_peers[j] is rank j's
+    // exchange region: partial rows u64 [2][tp_n][tp_nbmax][dim] at
+    // tp_brecv_off (value | exchange count << 32, slot count & 1), argmax
+    // keys u64 [tp_n][kBMaxSeq] at tp_bkeys_off, flags u32 [tp_n] at
+    // tp_flags_off (shared with k_decode, as is StepState::tp_count).
+    int tp_n, tp_rank, vocab_off, tp_nbmax;
+    unsigned char* const* tp_peers;
+    long long tp_brecv_off, tp_bkeys_off;
+    int tp_flags_off;
     int ring_off, ops_off;   // dynamic shared memory: digits (or attention scratch) at 0
 };
 
@@ -355,12 +368,74 @@ __device__ void bnorm_factors(const BatchArgs& a, float* s_ss) {
     csync();
 }
 
+// Tensor parallelism: this rank's partial rows d (rows row4..row4+3 of
+// sequence b) go, tagged with the exchange count, into slot `count & 1` of
+// every rank's receive rows; then the ranks' partials are summed in rank
+// order as they arrive (bounded waits).  False if a wait gave up.
+__device__ bool btp_sum4(const BatchArgs& a, float4& d, int b, int row4, uint32_t count) {
+    const size_t nbm = (size_t)a.tp_nbmax, dim = (size_t)a.dim;
+    const size_t slot = (size_t)(count & 1u) * a.tp_n;
+    for (int j = 0; j < a.tp_n; j++) {
+        uint64_t* r = reinterpret_cast<uint64_t*>(a.tp_peers[j] + a.tp_brecv_off) + ((slot + a.tp_rank) * nbm + b) * dim + row4;
+        st_relaxed_sys_u64(r, tag_pack(d.x, count));
+        st_relaxed_sys_u64(r + 1, tag_pack(d.y, count));
+        st_relaxed_sys_u64(r + 2, tag_pack(d.z, count));
+        st_relaxed_sys_u64(r + 3, tag_pack(d.w, count));
+    }
+    const uint64_t* own = reinterpret_cast<const uint64_t*>(a.tp_peers[a.tp_rank] + a.tp_brecv_off);
+    float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = 0; j < a.tp_n; j++) {
+        const uint64_t* p = own + ((slot + j) * nbm + b) * dim + row4;
+        for (int k = 0; k < 4; k++) {
+            uint64_t t = ld_relaxed_sys_u64(p + k);
+            for (uint32_t i = 0; tag_ep(t) != count; i++) {
+                if (i > (1u << 22)) return false;
+                t = ld_relaxed_sys_u64(p + k);
+            }
+            sum[k] += tag_val(t);
+        }
+    }
+    d = make_float4(sum[0], sum[1], sum[2], sum[3]);
+    return true;
+}
+
+// The ranks' argmax keys: after a grid barrier CTA 0 raises this rank's flag
+// to `count` in every rank's region and each CTA waits (bounded) until
+// every rank's flag reached it (the keys were stored, fenced, before).
+__device__ bool btp_exchange(const BatchArgs& a, uint32_t& nbar, uint32_t count) {
+    __shared__ int s_xok;
+    if (!grid_barrier(a.step, nbar)) return false;
+    if (threadIdx.x == 0) {
+        if (blockIdx.x == 0)
+            for (int j = 0; j < a.tp_n; j++)
+                st_release_sys_u32(reinterpret_cast<uint32_t*>(a.tp_peers[j] + a.tp_flags_off) + a.tp_rank, count);
+        const volatile uint32_t* fl = reinterpret_cast<const volatile uint32_t*>(a.tp_peers[a.tp_rank] + a.tp_flags_off);
+        int ok = 1;
+        for (int j = 0; j < a.tp_n && ok; j++) {
+            uint32_t i = 0;
+            while ((int32_t)(fl[j] - count) < 0)
+                if (++i > (1u << 24)) {
+                    ok = 0;
+                    break;
+                }
+        }
+        __threadfence_system();
+        if (!ok) set_error(a.step, DEV_BARRIER_TIMEOUT);
+        s_xok = ok;
+    }
+    csync();
+    return s_xok != 0;
+}
+
 // Residual update of this CTA's groups [g0, g1) of the model dimension for
-// every sequence: x = f(b, row4) (float4 of rows row4..row4+3), this CTA's
-// sums of squares per sequence, and the digits of x * nw (the RMSNorm
-// weight of the op that reads x next) into the global digit buffer.
+// every sequence: x = f(b, row4) (float4 of rows row4..row4+3) when
+// xcount == 0, else x + f(b, row4) summed over the ranks by exchange xcount;
+// then this CTA's sums of squares per sequence, and the digits of x * nw
+// (the RMSNorm weight of the op that reads x next) into the global digit
+// buffer.  False if an exchange wait gave up.
 template <int NBLK, class F>
-__device__ void bresidual(const BatchArgs& a, const float* nw, float* s_sq, F f) {
+__device__ bool bresidual(const BatchArgs& a, const float* nw, float* s_sq, uint32_t xcount, F f) {
+    bool ok = true;
     constexpr int NB8 = 8 * NBLK;
     const int G = gridDim.x, c = blockIdx.x, Gd = a.dim / 32;
     const int g0 = (int)((long long)c * Gd / G), g1 = (int)((long long)(c + 1) * Gd / G), ng = g1 - g0;
@@ -373,6 +448,11 @@ __device__ void bresidual(const BatchArgs& a, const float* nw, float* s_sq, F f)
         float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f), v = x;
         if (live) {
             x = f(b, row4);
+            if (xcount) {
+                if (a.tp_n > 1 && !btp_sum4(a, x, b, row4, xcount)) ok = false;
+                const float4 xo = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)b * a.dim + row4));
+                x = make_float4(xo.x + x.x, xo.y + x.y, xo.z + x.z, xo.w + x.w);
+            }
             __stcg(reinterpret_cast<float4*>(a.x + (size_t)b * a.dim + row4), x);
             const float4 w = __ldg(reinterpret_cast<const float4*>(nw + row4));
             v = make_float4(__fmul_rn(x.x, w.x), __fmul_rn(x.y, w.y), __fmul_rn(x.z, w.z), __fmul_rn(x.w, w.w));
@@ -387,12 +467,14 @@ __device__ void bresidual(const BatchArgs& a, const float* nw, float* s_sq, F f)
             bdigit_store<NBLK>(a.dg, g0 + gl, b, q, v, m);
         }
     }
-    csync();
+    const bool bad = csync_or(!ok);
     if (threadIdx.x < a.nb) {
         float s = 0.0f;
         for (int k = 0; k < ng; k++) s += s_sq[threadIdx.x * ng + k];
         __stcg(a.ssq + (size_t)c * a.nb + threadIdx.x, s);
     }
+    if (bad && threadIdx.x == 0) set_error(a.step, DEV_BARRIER_TIMEOUT);
+    return !bad;
 }
 
 // Attention of one layer for every sequence (src/kernel_simd.c:1099-1117):
@@ -557,6 +639,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
     uint32_t nbar = 0, dphase = 0, aphase = 0;
     bool ok = true;
     const int tid = threadIdx.x;
+    __shared__ uint32_t s_xcount;
+    if (tid == 0) s_xcount = *reinterpret_cast<volatile uint32_t*>(&a.step->tp_count);
+    csync();
+    uint32_t xcount = s_xcount;   // tensor-parallel exchanges so far (identical on every rank)
     // A matvec phase: the digits of this CTA's slice (built from att for WO,
     // else copied from the global buffer the previous phase wrote), then its
     // units.
@@ -611,7 +697,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
             a.tokens[(size_t)step * a.nb + tid] = s_tok[tid];
             a.argmax[par * kBMaxSeq + tid] = argmax_key(-1e9f, 0);   // this step's keys start here
         }
-        bresidual<NBLK>(a, a.rms_att, s_sq, [&](int b, int row4) {
+        bresidual<NBLK>(a, a.rms_att, s_sq, 0u, [&](int b, int row4) {
             return make_float4(emb_elem(a.emb, s_tok[b], row4), emb_elem(a.emb, s_tok[b], row4 + 1),
                                emb_elem(a.emb, s_tok[b], row4 + 2), emb_elem(a.emb, s_tok[b], row4 + 3));
         });
@@ -663,11 +749,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
                 // WO; the next layer's QKV, or the classifier, after W2).
                 const float* nw = op.kind == OP_WO ? a.rms_ffn + (size_t)l * a.dim
                                   : (l + 1 < a.n_layers ? a.rms_att + (size_t)(l + 1) * a.dim : a.rms_final);
-                bresidual<NBLK>(a, nw, s_sq, [&](int b, int row4) {
-                    const float4 x = __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)b * a.dim + row4));
-                    const float4 d = bsum4(a.part, S, T, NB8, b, row4);
-                    return make_float4(x.x + d.x, x.y + d.y, x.z + d.z, x.w + d.w);
-                });
+                // x += the op's sums (over the ranks' partials under tensor
+                // parallelism, by exchange ++xcount).
+                if (!bresidual<NBLK>(a, nw, s_sq, ++xcount,
+                                     [&](int b, int row4) { return bsum4(a.part, S, T, NB8, b, row4); })) {
+                    ok = false;
+                    break;
+                }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             } else if (op.kind == OP_W13) {
                 // rows w1[2j], w1[2j+1], w3[2j], w3[2j+1]; SwiGLU (src/kernel_simd.c:836-841),
@@ -698,7 +786,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             } else {   // OP_CLS
                 bnorm_factors(a, s_ss);
-                const int G = gridDim.x, c = blockIdx.x, V4 = a.vocab / 4;
+                const int G = gridDim.x, c = blockIdx.x, V4 = a.vocab_rows / 4;
                 const int q0 = (int)((long long)c * V4 / G), q1 = (int)((long long)(c + 1) * V4 / G);
                 for (int b = warp; b < a.nb; b += kWarps) {
                     const float ss = s_ss[b];
@@ -708,13 +796,13 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
                         const float4 s4 = bsum4(a.part, S, T, NB8, b, 4 * qd);
                         const float v[4] = {__fmul_rn(s4.x, ss), __fmul_rn(s4.y, ss), __fmul_rn(s4.z, ss),
                                             __fmul_rn(s4.w, ss)};
-                        __stcg(reinterpret_cast<float4*>(a.logits + (size_t)b * a.vocab + 4 * qd),
+                        __stcg(reinterpret_cast<float4*>(a.logits + (size_t)b * a.vocab_rows + 4 * qd),
                                make_float4(v[0], v[1], v[2], v[3]));
 #pragma unroll
                         for (int k = 0; k < 4; k++)
                             if (v[k] > best) {
                                 best = v[k];
-                                bi = (uint32_t)(4 * qd + k);
+                                bi = (uint32_t)(a.vocab_off + 4 * qd + k);
                             }
                     }
                     unsigned long long key = best > -1e9f ? argmax_key(best, bi) : 0ull;
@@ -726,12 +814,34 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
                     if (lane == 0 && key) atomicMax(a.argmax + par * kBMaxSeq + b, key);
                 }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                if (a.tp_n > 1) {
+                    // The greedy token of each sequence is the largest of the ranks' keys.
+                    if (blockIdx.x == 0 && tid < a.nb) {
+                        const unsigned long long key = __ldcg(a.argmax + par * kBMaxSeq + tid);
+                        for (int j = 0; j < a.tp_n; j++)
+                            reinterpret_cast<unsigned long long*>(a.tp_peers[j] + a.tp_bkeys_off)[a.tp_rank * kBMaxSeq + tid] = key;
+                        __threadfence_system();
+                    }
+                    if (!btp_exchange(a, nbar, ++xcount)) { ok = false; break; }
+                    if (blockIdx.x == 0 && tid < a.nb) {
+                        const unsigned long long* keys =
+                            reinterpret_cast<const unsigned long long*>(a.tp_peers[a.tp_rank] + a.tp_bkeys_off);
+                        unsigned long long m = 0;
+                        for (int j = 0; j < a.tp_n; j++) {
+                            const unsigned long long k = __ldcg(keys + j * kBMaxSeq + tid);
+                            m = k > m ? k : m;
+                        }
+                        a.argmax[par * kBMaxSeq + tid] = m;
+                        __threadfence();
+                    }
+                    if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                }
                 if (a.sampling) {
                     // CTA b draws sequence b's next token (stream b, its position)
                     // and leaves it in the key slot the next step reads.
                     for (int b = blockIdx.x; b < a.nb; b += gridDim.x) {
                         const float mx = key_value(__ldcg(a.argmax + par * kBMaxSeq + b));
-                        const int t = sample_token(a.logits + (size_t)b * a.vocab, a.vocab, mx, a.samp,
+                        const int t = sample_token(a.logits + (size_t)b * a.vocab_rows, a.vocab_rows, mx, a.samp,
                                                    (unsigned long long)b, (unsigned long long)s_pos[b],
                                                    reinterpret_cast<unsigned long long*>(xd));
                         if (tid == 0) a.argmax[par * kBMaxSeq + b] = argmax_key(0.0f, (uint32_t)t);
@@ -743,6 +853,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
             }
         }
     }
+    if (blockIdx.x == 0 && tid == 0) a.step->tp_count = xcount;
 }
 
 }  // namespace aion

@@ -453,8 +453,7 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
     import aion_b200 as A
     path = ensure_13b(rank)
     barrier()
-    model = A.Model(path, device=local, tp_size=world, tp_rank=rank, max_pos=TP_TOKENS,
-                    max_batch=BATCH_13B if world == 1 else 1)
+    model = A.Model(path, device=local, tp_size=world, tp_rank=rank, max_pos=TP_TOKENS, max_batch=BATCH_13B)
     if world > 1:
         handles = [None] * world
         pg.all_gather_object(handles, model.tp_handle())
@@ -480,19 +479,21 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
     wbytes = int(0.625 * (L * (4 * dim * dim + 3 * dim * hid) + vocab * dim)) // world
     gbs = wbytes * steps / (ms * 1e-3) / 1e9
     peak, kind = hbm_peak()
-    batch = None
-    if world == 1:
-        # Batch-16 decode of the same 256-token workload, all sequences from BOS.
-        model.decode_batch([BOS] * BATCH_13B, [0] * BATCH_13B, 4)   # warm-up
-        torch.cuda.synchronize()
-        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        b0.record(stream)
-        btoks, _ = model.decode_batch([BOS] * BATCH_13B, [0] * BATCH_13B, TP_TOKENS - 1)
-        b1.record(stream)
-        torch.cuda.synchronize()
-        bms = b0.elapsed_time(b1)
+    # Batch-16 decode of the same 256-token workload, all sequences from BOS
+    # (tensor-parallel over the same ranks; per-GPU bytes below).
+    model.decode_batch([BOS] * BATCH_13B, [0] * BATCH_13B, 4)   # warm-up
+    torch.cuda.synchronize()
+    barrier()
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(stream)
+    btoks, _ = model.decode_batch([BOS] * BATCH_13B, [0] * BATCH_13B, TP_TOKENS - 1)
+    b1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    bms = max_over_ranks(b0.elapsed_time(b1))
+    if True:
         nst = TP_TOKENS - 1
-        kvb = sum(kv_step_bytes(L, dim, [i] * BATCH_13B) for i in range(nst))
+        kvb = sum(kv_step_bytes(L, dim, [i] * BATCH_13B) for i in range(nst)) // world
         bgbs = (wbytes * nst + kvb) / (bms * 1e-3) / 1e9
         batch = {"workload": f"batch {BATCH_13B} greedy decode of {TP_TOKENS} tokens from BOS (lock step)",
                  "value": BATCH_13B * nst / (bms * 1e-3), "unit": "tok/s", "ms_per_step": bms / nst,

@@ -171,14 +171,15 @@ AION_API aion_status aion_prefill(aion_ctx* ctx, const int32_t* tokens, int32_t 
                                   float* logits_host);
 
 /* Lock-step greedy decode of sequences 0..n_seq-1 (n_seq <= min(max_batch,
- * 32)), W4A16 on one GPU, one persistent launch.  Step i feeds sequence b
+ * 32)), W4A16, one persistent launch; under tensor parallelism every rank
+ * makes the same call (after aion_tp_connect).  Step i feeds sequence b
  * one token at position pos0[b] + i: first_tokens[b] at step 0, afterwards
  * the first maximum of its previous logits (src/kernel_simd.c:1236-1243).
  * Each step is transformer() (src/kernel_simd.c:1014) of every sequence:
  * it writes the sequence's KV cache at that position.  tokens[(steps + 1)
  * * n_seq] (host) receives row i = the inputs of step i and row steps = the
- * picks after the last step; logits[n_seq][vocab] (host, may be NULL) the
- * last step's logits.  Each weight is read once per step for all sequences.
+ * picks after the last step; logits[n_seq][vocab / tp_size] (host, may be
+ * NULL) the last step's logits (this rank's vocab rows).  Each weight is read once per step for all sequences.
  * Activations enter the integer dot as 24-bit fixed point per group of 32
  * (relative error below 2^-22 of the group's largest value), fp32
  * accumulate.  Needs pos0[b] + steps <= max_pos. */

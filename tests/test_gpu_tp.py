@@ -7,8 +7,9 @@ half of the columns of wo/w2; the decode kernel sums the ranks' partial rows
 over NVLink peer memory and takes the argmax across ranks.  Tolerances: the
 greedy token stream of 32 steps is identical to the single-GPU one and to
 the oracle's; each rank's step-0 logit slice is within 1e-5 relative of the
-single-GPU logits (only the order of the partial sums differs).  Skipped
-with fewer than 2 GPUs.
+single-GPU logits (only the order of the partial sums differs); lock-step
+batched decode of 5 sequences over the two ranks gives the single-GPU
+batch's tokens.  Skipped with fewer than 2 GPUs.
 """
 from __future__ import annotations
 
@@ -24,19 +25,24 @@ SEED = 5
 STEPS = 32
 
 
+FIRST = [1, 7, 100, 2000, 511]
+
+
 def _rank_main(rank: int, path: str, q_out, q_in, res) -> None:
     try:
         import torch
         import aion_b200 as A
         torch.cuda.set_device(rank)
-        m = A.Model(path, device=rank, tp_size=2, tp_rank=rank)
+        m = A.Model(path, device=rank, tp_size=2, tp_rank=rank, max_batch=len(FIRST))
         q_out.put((rank, m.tp_handle()))
         m.tp_connect(q_in.get(timeout=120))
         l0 = m.transformer(1, 0)
         m.reset()
         toks, _ = m.generate(STEPS)
+        # Lock-step batched decode over the same two ranks.
+        bt, _ = m.decode_batch(FIRST, [0] * len(FIRST), STEPS)
         m.close()
-        res.put((rank, toks, l0))
+        res.put((rank, toks, (l0, bt.tolist())))
     except Exception as e:  # reported to the parent
         res.put((rank, "error", repr(e)))
 
@@ -55,10 +61,11 @@ def test_tp2_matches_single_gpu(cuda, oracle, workdir):
     path = workdir / "tp_small.int4"
     if not path.exists():
         A.synth_checkpoint(path, CFG, SEED, int4=True)
-    with A.Model(path) as m1:
+    with A.Model(path, max_batch=len(FIRST)) as m1:
         want_l0 = m1.transformer(1, 0)
         m1.reset()
         want, _ = m1.generate(STEPS)
+        want_bt, _ = m1.decode_batch(FIRST, [0] * len(FIRST), STEPS)
     om = oracle.open(path)
     toks, tok = [], 1
     for pos in range(STEPS):
@@ -85,8 +92,11 @@ def test_tp2_matches_single_gpu(cuda, oracle, workdir):
                 p.terminate()
     half = CFG[5] // 2
     for r in range(2):
-        toks_r, l0 = out[r]
-        assert toks_r != "error", l0
+        toks_r, extra = out[r]
+        assert toks_r != "error", extra
+        l0, bt = extra
         assert toks_r == want
         ref = want_l0[r * half:(r + 1) * half]
         assert np.abs(l0[:half] - ref).max() <= 1e-5 * np.abs(want_l0).max()
+        # Batched decode over the ranks: the single-GPU batch's tokens.
+        assert bt == want_bt.tolist()
