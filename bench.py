@@ -491,15 +491,15 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
     torch.cuda.synchronize()
     barrier()
     bms = max_over_ranks(b0.elapsed_time(b1))
-    if True:
-        nst = TP_TOKENS - 1
-        kvb = sum(kv_step_bytes(L, dim, [i] * BATCH_13B) for i in range(nst)) // world
-        bgbs = (wbytes * nst + kvb) / (bms * 1e-3) / 1e9
-        batch = {"workload": f"batch {BATCH_13B} greedy decode of {TP_TOKENS} tokens from BOS (lock step)",
-                 "value": BATCH_13B * nst / (bms * 1e-3), "unit": "tok/s", "ms_per_step": bms / nst,
-                 "roofline": {"kernel": "k_decode_batch<2>", "bound": "hbm", "achieved": bgbs, "peak": peak,
-                              "peak_kind": kind, "unit": "GB/s", "frac": bgbs / peak},
-                 "same_stream_as_batch1": bool((btoks[:16, 0] == np.array(toks[:16])).all())}
+    nst = TP_TOKENS - 1
+    kvb = sum(kv_step_bytes(L, dim, [i] * BATCH_13B) for i in range(nst)) // world
+    bgbs = (wbytes * nst + kvb) / (bms * 1e-3) / 1e9
+    batch = {"workload": f"batch {BATCH_13B} greedy decode of {TP_TOKENS} tokens from BOS (lock step)",
+             "value": BATCH_13B * nst / (bms * 1e-3), "unit": "tok/s", "ms_per_step": bms / nst,
+             "roofline": {"kernel": "k_decode_batch<2>", "bound": "hbm", "achieved": bgbs, "peak": peak,
+                          "peak_kind": kind, "unit": "GB/s", "frac": bgbs / peak,
+                          "bytes_per_step_per_gpu": wbytes + kvb // nst},
+             "same_stream_as_batch1": bool((btoks[:16, 0] == np.array(toks[:16])).all())}
     if rank == 0:
         print(json.dumps({
             "metric": "Llama-2-13B int4 decode tok/s (batch 1, tensor-parallel)", "value": steps / (ms * 1e-3),
