@@ -390,7 +390,7 @@ def run_fp32(args, local: int) -> None:
         "config": {"workload": f"llama2-7b-shape fp32 greedy decode from BOS, {L} layers", "layers": L, "seed": 1},
         "roofline": {"kernel": "k_decode<F32> (persistent decode, fp32 tiles)", "bound": "hbm", "achieved": gbs,
                      "peak": peak, "peak_kind": kind, "unit": "GB/s", "frac": gbs / peak, "bytes_per_token": wb},
-        "gpu_launches": 1, "clocks": clk, "token_stream_head": model.tokens(16)}), flush=True)
+        "gpu_launches": 1, "clocks": clk, "token_stream_head": model.tokens(min(16, args.warmup + args.steps))}), flush=True)
     model.close()
 
 
