@@ -43,6 +43,56 @@ def test_header_compiles_as_c11(tmp_path):
                    check=True)
 
 
+C_PROGRAM = r"""
+#include <stdio.h>
+#include <string.h>
+#include "aion.h"
+
+int main(int argc, char** argv) {
+    /* the binding src/kernel_simd.c would use: opts, load, errors (no GPU work) */
+    aion_opts o;
+    aion_default_opts(&o);
+    aion_ctx* ctx = NULL;
+    aion_status s = aion_load(argv[1], &o, &ctx);
+    const char* err = aion_last_error(NULL);
+    printf("load %d %d\n", (int)s, err && err[0] ? 1 : 0);
+    /* quantize_buffer's format: one group of 32 values */
+    float w[32];
+    for (int i = 0; i < 32; i++) w[i] = (float)(i - 16) * 0.25f;
+    uint8_t packed[16];
+    float scale;
+    aion_quantize_buffer(w, packed, &scale, 32);
+    printf("scale %.9g first %u\n", scale, (unsigned)packed[0]);
+    const int32_t cfg[7] = {288, 768, 6, 6, 6, 32000, 256};
+    printf("bytes %lld %lld\n", (long long)aion_checkpoint_bytes(cfg, 1), (long long)aion_checkpoint_bytes(cfg, 0));
+    return ctx != NULL;
+}
+"""
+
+
+def test_c_program_links_and_runs(built, tmp_path):
+    """A C11 program binds the library the way the reference's C driver
+    would (header + -laion) and runs its host-side calls."""
+    import aion_b200 as A
+    src = tmp_path / "bind.c"
+    src.write_text(C_PROGRAM)
+    exe = tmp_path / "bind"
+    lib_dir = A.LIB_PATH.parent
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", str(ROOT / "include"), str(src), "-o", str(exe),
+                    "-L", str(lib_dir), "-laion", f"-Wl,-rpath,{lib_dir}"], check=True)
+    out = subprocess.run([str(exe), str(tmp_path / "missing.int4")], capture_output=True, text=True, check=True).stdout
+    lines = dict(l.split(" ", 1) for l in out.strip().splitlines())
+    assert lines["load"] == "1 1"                     # AION_ERR_IO with a message
+    w = (np.arange(32, dtype=np.float32) - 16) * np.float32(0.25)
+    packed = np.zeros(16, np.uint8)
+    scales = np.zeros(1, np.float32)
+    A.lib().aion_quantize_buffer(w.ctypes.data, packed.ctypes.data, scales.ctypes.data, 32)
+    assert lines["scale"] == f"{float(scales[0]):.9g} first {int(packed[0])}"
+    int4, f32 = (int(v) for v in lines["bytes"].split())
+    assert int4 == A.lib().aion_checkpoint_bytes((ctypes.c_int32 * 7)(*cases.TINY), 1)
+    assert f32 == 28 + 4 * (cases.TINY[5] * 288 + 6 * 288 * 2 + 6 * (4 * 288 * 288 + 3 * 288 * 768) + 288 + 256 * 48)
+
+
 def test_default_opts(built):
     import aion_b200 as A
     o = A.Opts()
