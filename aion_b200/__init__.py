@@ -99,6 +99,7 @@ def lib() -> ctypes.CDLL:
         "aion_matvec_w4a16": (I32, [VP, VP, VP, VP]),
         "aion_matvec_w4a8": (I32, [VP, VP, VP, VP]),
         "aion_matvec_w4a16_static": (I32, [VP, VP, VP, VP]),
+        "aion_matvec_status": (I32, [VP, VP]),
         "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_decode_batch": (I32, [VP, I32, I32, VP, VP, VP, VP]),
@@ -408,6 +409,11 @@ class QMatrix:
         """y = W x with per-32 int8 activations (quantize_activations_neon + matmul_w4a8_neon)."""
         _check(lib().aion_matvec_w4a8(self._h, _dev_ptr(x, "torch.float32", self.cols),
                                       _dev_ptr(y, "torch.float32", self.rows), _stream_ptr(stream)))
+
+    def status(self, stream=None) -> None:
+        """Waits for the stream; raises AionError (AION_ERR_TIMEOUT) if a matvec
+        on this matrix gave up a bounded wait since the last check."""
+        _check(lib().aion_matvec_status(self._h, _stream_ptr(stream)))
 
     def free(self) -> None:
         if getattr(self, "_h", None):

@@ -17,6 +17,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 #include <string>
@@ -87,6 +88,24 @@ static const DevInfo& dev_info(int dev) {
 }
 
 static int round128(int b) { return (b + 127) & ~127; }
+
+// Opts a kernel into `bytes` of dynamic shared memory on the current device
+// once per (device, kernel slot); thread-safe.  The attribute belongs to the
+// device's context, so a second device needs its own call; devices beyond
+// the table get the call every time.
+enum AttrSlot { ATTR_MATVEC_W4A16 = 0, ATTR_MATVEC_W4A8 = 1, ATTR_GEMM = 2, ATTR_SLOTS = 3 };
+constexpr int kMaxAttrDevices = 64;
+static cudaError_t ensure_smem_attr(const void* fn, int slot, int dev, int bytes) {
+    static std::mutex mu;
+    static bool done[kMaxAttrDevices][ATTR_SLOTS] = {};
+    if (dev < 0 || dev >= kMaxAttrDevices)
+        return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[dev][slot]) return cudaSuccess;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done[dev][slot] = true;
+    return e;
+}
 
 // Dynamic shared memory plan of the streaming kernels: activation digits
 // (G * 128 bytes) and group factors (G * 4), the op table (decode kernel),
@@ -185,35 +204,33 @@ static cudaError_t fill_pad(const MatDesc& m, cudaStream_t st) {
 // Standalone matvec (kernel-level API)
 // ---------------------------------------------------------------------------
 struct Scratch {
-    float* split_part = nullptr;   // [ntiles][2][16]
-    int* split_cnt = nullptr;      // [ntiles]
+    uint64_t* split_part = nullptr;   // [ntiles][16] tagged partial rows of cut tiles
     int* error = nullptr;
 };
 
+// `epoch` tags this call's cut-tile flags (nonzero, different from the
+// previous call's on the same scratch), so a flag that a call which gave up
+// left behind is never taken for the next call's.
 template <int MODE>
 static cudaError_t launch_standalone(const MatDesc& m, const Scratch& sc, const float* x, float* y, int dev,
-                                     cudaStream_t st) {
-    static bool attr_done[2] = {false, false};
+                                     cudaStream_t st, uint32_t epoch) {
     const DevInfo& di = dev_info(dev);
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, k_matvec<MODE>);
     if (e != cudaSuccess) return e;
     SmemPlan p = plan_smem(m.n, max_chunk_bytes(m), di.smem_optin, (int)fa.sharedSizeBytes);
     if (p.P < 1) return cudaErrorInvalidConfiguration;
-    if (!attr_done[MODE]) {
-        e = cudaFuncSetAttribute(k_matvec<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 di.smem_optin - (int)fa.sharedSizeBytes);
-        if (e != cudaSuccess) return e;
-        attr_done[MODE] = true;
-    }
+    e = ensure_smem_attr((const void*)k_matvec<MODE>, MODE == MODE_W4A8 ? ATTR_MATVEC_W4A8 : ATTR_MATVEC_W4A16, dev,
+                         di.smem_optin - (int)fa.sharedSizeBytes);
+    if (e != cudaSuccess) return e;
     StandaloneArgs a;
+    a.epoch = epoch;
     a.op.m = m;
     a.op.kind = OP_STORE;
     a.op.layer = 0;
     a.x = x;
     a.y = y;
     a.split_part = sc.split_part;
-    a.split_cnt = sc.split_cnt;
     a.error = sc.error;
     a.P = p.P;
     a.slot_bytes = p.slot_bytes;
@@ -282,8 +299,7 @@ struct aion_ctx {
     float* attn_part = nullptr;
     int* attn_cnt = nullptr;
     int max_chunks = 1;
-    float* split_part = nullptr;
-    int* split_cnt = nullptr;
+    uint64_t* split_part = nullptr;
     int max_tiles = 0;
     StepState* step = nullptr;
     unsigned long long* argmax = nullptr;
@@ -508,7 +524,6 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.attn_cnt = c->attn_cnt;
     a.max_chunks = c->max_chunks;
     a.split_part = c->split_part;
-    a.split_cnt = c->split_cnt;
     a.step = c->step;
     a.argmax = c->argmax;
     a.history = c->history;
@@ -797,9 +812,8 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         c->argmax = (unsigned long long*)arena_take(c, 8);
         c->history = (int32_t*)arena_take(c, (size_t)c->max_pos * 4);
         c->ops = (OpDesc*)arena_take(c, (size_t)(4 * L + 1) * sizeof(OpDesc));
-        c->split_part = (float*)arena_take(c, (size_t)c->max_tiles * 2 * kTR * 4);
-        c->split_cnt = (int*)arena_take(c, (size_t)c->max_tiles * 4);
-        if (!c->split_cnt) {
+        c->split_part = (uint64_t*)arena_take(c, (size_t)c->max_tiles * kTR * 8);
+        if (!c->split_part) {
             set_err(&c->err, "internal: arena too small");
             s = AION_ERR_OOM;
             break;
@@ -1190,7 +1204,7 @@ extern "C" AION_API aion_status aion_reset(aion_ctx* c) {
     CK_RET(&c->err, cudaMemsetAsync(c->vcache + (size_t)c->cur_seq * c->kv_seq, 0, kvb, c->stream));
     CK_RET(&c->err, cudaMemsetAsync(&c->step->error, 0, sizeof(int32_t), c->stream));
     CK_RET(&c->err, cudaMemsetAsync(c->attn_cnt, 0, c->nh * 4, c->stream));
-    CK_RET(&c->err, cudaMemsetAsync(c->split_cnt, 0, (size_t)c->max_tiles * 4, c->stream));
+    CK_RET(&c->err, cudaMemsetAsync(c->split_part, 0, (size_t)c->max_tiles * kTR * 8, c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return AION_OK;
 }
@@ -1362,7 +1376,11 @@ extern "C" AION_API aion_status aion_prefill(aion_ctx* c, const int32_t* tokens,
 // ---------------------------------------------------------------------------
 // Kernel-level API
 // ---------------------------------------------------------------------------
+// Cut-tile flag tag of the next standalone call: 1 .. 0x7FFFFFFF, cycling.
+static uint32_t next_epoch(std::atomic<uint32_t>& counter) { return counter.fetch_add(1) % 0x7FFFFFFFu + 1u; }
+
 struct aion_qmatrix {
+    std::atomic<uint32_t> epoch{0};
     int device;
     MatDesc m;
     Scratch sc;
@@ -1402,11 +1420,12 @@ extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const u
         set_err(nullptr, "aion_qmatrix_upload: %s", cudaGetErrorString(e));
         return cuda_status(e);
     }
-    // Scratch of the split-tile combine: partial rows and counters (zero).
-    const size_t pbytes = align256((size_t)m.ntiles * 2 * kTR * 4), cbytes = align256((size_t)m.ntiles * 4);
+    // Scratch of the split-tile combine: tagged partial rows (zero: tag 0
+    // is never used) and the error word.
+    const size_t pbytes = align256((size_t)m.ntiles * kTR * 8);
     uint8_t* scr = nullptr;
-    e = cudaMalloc(&scr, pbytes + cbytes + 256);
-    if (e == cudaSuccess) e = cudaMemset(scr, 0, pbytes + cbytes + 256);
+    e = cudaMalloc(&scr, pbytes + 256);
+    if (e == cudaSuccess) e = cudaMemset(scr, 0, pbytes + 256);
     if (e != cudaSuccess) {
         cudaFree(w);
         if (scr) cudaFree(scr);
@@ -1417,9 +1436,8 @@ extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const u
     q->device = device;
     q->m = m;
     q->scratch_mem = scr;
-    q->sc.split_part = (float*)scr;
-    q->sc.split_cnt = (int*)(scr + pbytes);
-    q->sc.error = (int*)(scr + pbytes + cbytes);
+    q->sc.split_part = (uint64_t*)scr;
+    q->sc.error = (int*)(scr + pbytes);
     *out = q;
     return AION_OK;
 }
@@ -1461,9 +1479,11 @@ static aion_status matvec_api(int mode, const aion_qmatrix* q, const float* x, f
         return AION_ERR_ARG;
     }
     CK_RET(nullptr, cudaSetDevice(q->device));
+    aion_qmatrix* qm = const_cast<aion_qmatrix*>(q);
+    const uint32_t ep = next_epoch(qm->epoch);
     cudaError_t e = mode == MODE_W4A8
-                        ? launch_standalone<MODE_W4A8>(q->m, q->sc, x, y, q->device, (cudaStream_t)stream)
-                        : launch_standalone<MODE_W4A16>(q->m, q->sc, x, y, q->device, (cudaStream_t)stream);
+                        ? launch_standalone<MODE_W4A8>(q->m, q->sc, x, y, q->device, (cudaStream_t)stream, ep)
+                        : launch_standalone<MODE_W4A16>(q->m, q->sc, x, y, q->device, (cudaStream_t)stream, ep);
     CK_RET(nullptr, e);
     return AION_OK;
 }
@@ -1495,14 +1515,14 @@ extern "C" AION_API aion_status aion_matvec_w4a8(const aion_qmatrix* w, const fl
 // make that first call before any stream capture on that device.
 // ---------------------------------------------------------------------------
 constexpr int kStaticScratchTiles = 2048;
-constexpr size_t kStaticPartBytes = (size_t)kStaticScratchTiles * kTR * 4;   // second parts of cut tiles
-constexpr size_t kStaticFlagBytes = (size_t)kStaticScratchTiles * 4;         // cut-tile flags: start at zero
-constexpr size_t kStaticScratchBytes = kStaticPartBytes + kStaticFlagBytes + 256;   // + error word: starts at zero
+constexpr size_t kStaticPartBytes = (size_t)kStaticScratchTiles * kTR * 8;   // tagged second parts of cut tiles
+constexpr size_t kStaticScratchBytes = kStaticPartBytes + 256;               // + error word: starts at zero
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 constexpr int kMaxStaticDevices = 64;
 static std::mutex g_static_mu;
 static unsigned char* g_static_addr[kMaxStaticDevices];
+static std::atomic<uint32_t> g_static_epoch[kMaxStaticDevices];
 
 // Address of this device's g_static_scratch; the device must be current.
 static aion_status static_scratch_addr(int dev, unsigned char** out) {
@@ -1544,14 +1564,46 @@ extern "C" AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, 
     const aion_status st = static_scratch_addr(w->device, &base);
     if (st != AION_OK) return st;
     Scratch sc;
-    sc.split_part = reinterpret_cast<float*>(base);
-    sc.split_cnt = reinterpret_cast<int*>(base + kStaticPartBytes);
-    sc.error = reinterpret_cast<int*>(base + kStaticPartBytes + kStaticFlagBytes);
-    // The flags and the error word must start at zero (a call that gave up
-    // may have left a flag raised); the partials need no initial value.
-    CK_RET(nullptr, cudaMemsetAsync(sc.split_cnt, 0, kStaticFlagBytes + sizeof(int), (cudaStream_t)stream));
-    CK_RET(nullptr, launch_standalone<MODE_W4A16>(w->m, sc, x_dev, y_dev, w->device, (cudaStream_t)stream));
+    sc.split_part = reinterpret_cast<uint64_t*>(base);
+    sc.error = reinterpret_cast<int*>(base + kStaticPartBytes);
+    // Cut-tile parts carry this call's tag, so parts left by an earlier call
+    // need no clearing (the array starts at zero, and tag 0 is never used).
+    // The error word starts at zero and aion_matvec_status reads and clears
+    // it.
+    CK_RET(nullptr, launch_standalone<MODE_W4A16>(w->m, sc, x_dev, y_dev, w->device, (cudaStream_t)stream,
+                                                  next_epoch(g_static_epoch[w->device])));
     return AION_OK;
+}
+
+// Reads and clears one device error word (the stream has been waited for).
+static aion_status take_error_word(int* word, const char* what) {
+    int v = 0;
+    CK_RET(nullptr, cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v == 0) return AION_OK;
+    CK_RET(nullptr, cudaMemset(word, 0, sizeof(int)));
+    set_err(nullptr, "%s: a bounded wait inside the matvec gave up (code %d); its y is invalid", what, v);
+    return AION_ERR_TIMEOUT;
+}
+
+extern "C" AION_API aion_status aion_matvec_status(const aion_qmatrix* w, void* stream) {
+    if (!w) {
+        set_err(nullptr, "aion_matvec_status: null matrix");
+        return AION_ERR_ARG;
+    }
+    CK_RET(nullptr, cudaSetDevice(w->device));
+    CK_RET(nullptr, cudaStreamSynchronize((cudaStream_t)stream));
+    aion_status st = take_error_word(w->sc.error, "aion_matvec_w4a16/_w4a8");
+    unsigned char* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_static_mu);
+        if (w->device >= 0 && w->device < kMaxStaticDevices) base = g_static_addr[w->device];
+    }
+    if (base) {
+        const aion_status s2 =
+            take_error_word(reinterpret_cast<int*>(base + kStaticPartBytes), "aion_matvec_w4a16_static");
+        if (st == AION_OK) st = s2;
+    }
+    return st;
 }
 
 // ---------------------------------------------------------------------------
@@ -1853,11 +1905,7 @@ static aion_status launch_gemm_bf16(const void* a, const void* b, float* c, int6
         set_err(err, "gemm: cuTensorMapEncodeTiled is unavailable or rejected the operands");
         return AION_ERR_CUDA;
     }
-    static bool attr_done[kMaxStaticDevices] = {};
-    if (dev >= 0 && dev < kMaxStaticDevices && !attr_done[dev]) {
-        CK_RET(err, cudaFuncSetAttribute(k_gemm_bf16_tn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
-        attr_done[dev] = true;
-    }
+    CK_RET(err, ensure_smem_attr((const void*)k_gemm_bf16_tn, ATTR_GEMM, dev, kGemmSmem));
     GemmArgs g;
     g.C = c;
     g.M = (int)m;
@@ -1878,7 +1926,11 @@ extern "C" AION_API aion_status aion_gemm_bf16_tn(const void* a_dev, const void*
     }
     int dev = 0;
     CK_RET(nullptr, cudaGetDevice(&dev));
-    if (dev < 0 || dev >= kMaxStaticDevices) return AION_ERR_ARG;
+    if (dev < 0 || dev >= kMaxStaticDevices) {
+        set_err(nullptr, "aion_gemm_bf16_tn: device %d beyond the %d devices this library supports", dev,
+                kMaxStaticDevices);
+        return AION_ERR_ARG;
+    }
     if (!g_gemm_err_dev[dev]) {
         void* p = nullptr;
         CK_RET(nullptr, cudaGetSymbolAddress(&p, g_gemm_err_word));
@@ -1919,3 +1971,23 @@ extern "C" AION_API aion_status aion_quantize_activations(const float* x, int8_t
     CK_RET(nullptr, cudaGetLastError());
     return AION_OK;
 }
+
+#ifdef AION_PHASE_TIMING
+extern "C" AION_API aion_status aion_phase_clear() {
+    const size_t tw = (size_t)kPhaseSteps * kPhaseOps * kPhaseCtas * 8;
+    void* p = nullptr;
+    CK_RET(nullptr, cudaGetSymbolAddress(&p, g_phase_w));
+    CK_RET(nullptr, cudaMemset(p, 0, tw * sizeof(unsigned long long)));
+    return AION_OK;
+}
+// Profiling builds only: copies the phase timestamps of the last decode
+// launch (layout [step][op][cta][slot], see common.cuh) into `host`.
+extern "C" AION_API aion_status aion_phase_dump(unsigned long long* host, size_t n) {
+    const size_t total = (size_t)kPhaseSteps * kPhaseOps * kPhaseCtas * kPhaseSlots;
+    if (!host || n < total) return AION_ERR_ARG;
+    CK_RET(nullptr, cudaMemcpyFromSymbol(host, g_phase, total * sizeof(unsigned long long)));
+    const size_t tw = (size_t)kPhaseSteps * kPhaseOps * kPhaseCtas * 8;
+    if (n >= total + tw) CK_RET(nullptr, cudaMemcpyFromSymbol(host + total, g_phase_w, tw * sizeof(unsigned long long)));
+    return AION_OK;
+}
+#endif

@@ -29,7 +29,7 @@ struct StepState {
     int32_t error;
     uint32_t barrier;        // grid-barrier arrival counter of the persistent decode kernel
     uint32_t tp_count;       // tensor parallelism: exchanges completed so far (same on every rank)
-    int32_t pad;
+    uint32_t op_seq;         // ops run by all decode launches so far (tags of the cut-tile parts)
 };
 
 // Argmax key: (order-preserving float bits << 32) | (0xFFFFFFFF - index).
@@ -63,6 +63,57 @@ __host__ __device__ inline float key_value(unsigned long long k) {
 #endif
     return f;
 }
+
+// ---------------------------------------------------------------------------
+// Phase timestamps (profiling builds only, -DAION_PHASE_TIMING): thread 0 of
+// every CTA records the global timer at fixed points of each op of the
+// first kPhaseSteps steps of a decode launch; aion_phase_dump() copies them
+// out.  Normal builds compile PHASE_T to nothing.
+// ---------------------------------------------------------------------------
+#ifdef AION_PHASE_TIMING
+constexpr int kPhaseSteps = 8, kPhaseOps = 168, kPhaseCtas = 160, kPhaseSlots = 12;
+__device__ unsigned long long g_phase[(size_t)kPhaseSteps * kPhaseOps * kPhaseCtas * kPhaseSlots];
+// per (step, op, cta): ring-wait ns and group-dot ns summed over the warps,
+// chunks, then the latest loop end, loop start and per-warp busy time
+__device__ unsigned long long g_phase_w[(size_t)kPhaseSteps * kPhaseOps * kPhaseCtas * 8];
+__device__ __forceinline__ unsigned long long global_timer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define PHASE_T(step, op, slot)                                                                               \
+    do {                                                                                                      \
+        if (threadIdx.x == 0 && (step) < kPhaseSteps && (op) < kPhaseOps && blockIdx.x < kPhaseCtas)          \
+            g_phase[(((size_t)(step) * kPhaseOps + (op)) * kPhaseCtas + blockIdx.x) * kPhaseSlots + (slot)] = \
+                global_timer();                                                                               \
+    } while (0)
+#define PHASE_LOOP_START(step, op)                                                              \
+    do {                                                                                        \
+        if ((threadIdx.x & 31) == 0 && (step) < kPhaseSteps && (op) < kPhaseOps && blockIdx.x < kPhaseCtas) \
+            atomicMax(g_phase_w + (((size_t)(step) * kPhaseOps + (op)) * kPhaseCtas + blockIdx.x) * 8 + 4, global_timer()); \
+    } while (0)
+#define PHASE_W(step, op, wait_ns, mma_ns, n)                                                  \
+    do {                                                                                        \
+        if ((threadIdx.x & 31) == 0 && (step) < kPhaseSteps && (op) < kPhaseOps && blockIdx.x < kPhaseCtas) { \
+            unsigned long long* w_ = g_phase_w + (((size_t)(step) * kPhaseOps + (op)) * kPhaseCtas + blockIdx.x) * 8; \
+            atomicAdd(w_, (wait_ns));                                                          \
+            atomicAdd(w_ + 1, (mma_ns));                                                       \
+            atomicAdd(w_ + 2, (n));                                                            \
+            atomicMax(w_ + 3, global_timer());                                                 \
+            atomicMax(w_ + 5, (wait_ns) + (mma_ns));                                           \
+        }                                                                                       \
+    } while (0)
+#else
+#define PHASE_W(step, op, wait_ns, mma_ns, n) \
+    do {                                      \
+    } while (0)
+#define PHASE_LOOP_START(step, op) \
+    do {                           \
+    } while (0)
+#define PHASE_T(step, op, slot) \
+    do {                        \
+    } while (0)
+#endif
 
 // ---------------------------------------------------------------------------
 // Programmatic dependent launch.
@@ -111,6 +162,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Non-blocking probe of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
         : "r"(bar), "r"(parity)
@@ -169,6 +232,14 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
     uint64_t v;
     asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
     asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");

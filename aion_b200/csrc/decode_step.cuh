@@ -53,8 +53,7 @@ struct DecodeArgs {
     float* attn_part;              // [n_heads][max_chunks][head_size + 2]
     int* attn_cnt;                 // [n_heads], zero between uses
     int max_chunks;
-    float* split_part;             // [max_tiles][2][16] partial rows of tiles cut by CTA boundaries
-    int* split_cnt;                // [max_tiles], zero between uses
+    uint64_t* split_part;          // [max_tiles][16] tagged partial rows of tiles cut by CTA boundaries
     StepState* step;
     unsigned long long* argmax;
     int32_t* history;              // [max_pos]
@@ -349,10 +348,41 @@ struct OpSmem {
     int state[2];
 };
 
+// Split mode, a CTA whose range starts inside tile tf (it holds the
+// tile's second part): every warp with units in tf arrives once it has
+// left the tile, and the last of the n0 such warps sums the warps' partial
+// rows (in warp order, as the full reduction does) and publishes them as
+// 16 tagged 8-byte words (fp32 bits, the op's tag): one relaxed store each,
+// read whole, so no fence or flag is needed.  The partner CTA thus finds
+// the part as soon as this CTA's first tile is done, not after its op.
+__device__ __forceinline__ void publish_cut_tile(OpSmem& os, int n0, int tf, uint64_t* split_part, uint32_t tag) {
+    const int lane = threadIdx.x & 31;
+    __threadfence_block();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&os.state[1], 1) == n0 - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence_block();
+    if (lane < kTR) {
+        float v = 0.0f;
+        for (int k = 0; k < kWarps; k++) v += os.part[k * kTR + lane];
+        st_relaxed_u64(split_part + (size_t)tf * kTR + lane, tag_pack(v, tag));
+    }
+}
+
+// Clears the per-op shared state for the next op: run_op needs OpSmem::part
+// zero and the counters reset on entry (kernels call this before their
+// first op; run_op calls it on its way out).
+__device__ __forceinline__ void reset_opsmem(OpSmem& os) {
+    for (int i = threadIdx.x; i < kMaxLocalTiles * kWarps * kTR; i += kThreads) os.part[i] = 0.0f;
+    if (threadIdx.x == 0) os.state[0] = os.state[1] = 0;
+}
+
 template <int MODE, bool PROD, class Epi>
 __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, Seq& seq, const OpDesc* ops, int nops,
-                       int steps, const unsigned char* xf, const float* xs, OpSmem& os, float* split_part,
-                       int* split_cnt, Epi& epi) {
+                       int steps, const unsigned char* xf, const float* xs, OpSmem& os, uint64_t* split_part,
+                       uint32_t tag, Epi& epi, int pstep = 1 << 30, int pop = 0) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const float xfac = MODE == MODE_W4A16 ? xs[0] : 0.0f;
     const OpWork w = op_work(m, MODE);
@@ -361,12 +391,17 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
     bool more = cursor_begin(cu, w, m, warp);
     if (w.split) {
         const int tf = w.u0 / m.nch, tl = (w.u1 - 1) / m.nch, ntl = tl - tf + 1;
-        for (int i = tid; i < ntl * kWarps * kTR; i += kThreads) os.part[i] = 0.0f;
-        if (tid == 0) os.state[0] = 0;
+        const bool cut0 = (w.u0 % m.nch) != 0, cut1 = (w.u1 % m.nch) != 0;
+        const int n0 = min(kWarps, min((tf + 1) * m.nch, w.u1) - w.u0);   // warps with units in tile tf
+        // OpSmem was reset at the end of the previous op (or at kernel
+        // start) and a CTA barrier has passed since, so no barrier here.
         epi.prefetch(tf * kTR, ntl * kTR, os.pre);
-        csync();
         float a0 = 0.0f, a1 = 0.0f;
         int cur = -1;
+#ifdef AION_PHASE_TIMING
+        unsigned long long tw_ = 0, tm_ = 0, nc_ = 0;
+        PHASE_LOOP_START(pstep, pop);
+#endif
         while (more) {
             const int tile = cu.tile, c = cu.c;
             if (tile != cur) {
@@ -377,15 +412,27 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
                         p[lane >> 2] = a0;
                         p[(lane >> 2) + 8] = a1;
                     }
+                    if (cut0 && cur == tf) publish_cut_tile(os, n0, tf, split_part, tag);
                 }
                 a0 = a1 = 0.0f;
                 cur = tile;
             }
+#ifdef AION_PHASE_LOOP
+            const unsigned long long q0_ = global_timer();
+#endif
             const unsigned char* ch = ring_wait(ring, ring_base);
             if (!ch) { ok = false; break; }
+#ifdef AION_PHASE_LOOP
+            const unsigned long long q1_ = global_timer();
+#endif
             const int g0 = chunk_g0(m, c), g1 = chunk_g0(m, c + 1);
             chunk_mma<MODE>(ch, g1 - g0, g0, xf, xs, a0, a1);
             __syncwarp();
+#ifdef AION_PHASE_LOOP
+            tw_ += q1_ - q0_;
+            tm_ += global_timer() - q1_;
+            nc_++;
+#endif
             if (PROD) {
                 ring_release(ring, true);
             } else {
@@ -394,6 +441,9 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             }
             more = cursor_next(cu, w, m);
         }
+#ifdef AION_PHASE_TIMING
+        PHASE_W(pstep, pop, tw_, tm_, nc_);
+#endif
         if (ok && cur >= 0) {
             quad_reduce<MODE>(a0, a1, xfac);
             if ((lane & 3) == 0) {
@@ -401,9 +451,17 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
                 p[lane >> 2] = a0;
                 p[(lane >> 2) + 8] = a1;
             }
+            if (cut0 && cur == tf) publish_cut_tile(os, n0, tf, split_part, tag);
         }
         cp_async_wait_all();
         if (csync_or(!ok)) return false;
+        PHASE_T(pstep, pop, 2);
+        // Last local tile cut by the CTA boundary (this CTA has its first
+        // part): warp 1's lanes 0..15 fetch the partner's tagged part now,
+        // so the load's latency overlaps the reduction below.
+        const bool cutw = cut1 && tid >= 32 && tid < 32 + kTR;
+        const uint64_t* cut_src = split_part + (size_t)tl * kTR + (tid - 32);
+        uint64_t cut_word = cutw ? ld_relaxed_u64(cut_src) : 0ull;
         for (int i = tid; i < ntl * kTR; i += kThreads) {
             const int lt = i / kTR, r = i % kTR;
             float v = 0.0f;
@@ -411,37 +469,33 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             os.vals[i] = v;
         }
         csync();
+        for (int i = tid; i < ntl * kWarps * kTR; i += kThreads) os.part[i] = 0.0f;
+        PHASE_T(pstep, pop, 7);
         // Tiles cut by a CTA boundary: local tile 0 when u0 is inside a tile
-        // (this CTA has the tile's second part), the last local tile when u1
-        // is (this CTA has the first part).  The CTA with the second part
-        // publishes it and raises the tile's flag; the CTA with the first
-        // part waits for the flag, adds first + second, lowers the flag and
-        // finishes the tile.  Publishing never waits, so the waits form a
-        // chain towards higher CTAs and always end.
-        const bool cut0 = (w.u0 % m.nch) != 0, cut1 = (w.u1 % m.nch) != 0;
-        if (cut0 && tid < kTR) {
-            __stcg(split_part + (size_t)tf * kTR + tid, os.vals[tid]);
-            __syncwarp(0xFFFFu);
-            if (tid == 0) st_release_u32(reinterpret_cast<uint32_t*>(split_cnt) + tf, 1u);
-        }
-        if (cut1 && tid >= 32 && tid < 32 + kTR) {
-            int ok1 = 1;
-            if (tid == 32) {
-                uint32_t i = 0;
-                while (ld_acquire_u32(reinterpret_cast<const uint32_t*>(split_cnt) + tl) == 0u)
-                    if (++i > (1u << 24)) { ok1 = 0; break; }
+        // (this CTA has the tile's second part, published above as soon as
+        // its warps left the tile), the last local tile when u1 is (this CTA
+        // has the first part).  The CTA with the first part waits for the
+        // flag, adds first + second, lowers the flag and finishes the tile.
+        // Publishing never waits, so the waits always end.
+        if (cutw) {
+            // The partner published its part as soon as its first tile was
+            // done; wait (bounded) only if the fetched word is not yet this
+            // op's, then add first + second in that order.
+            uint32_t spins = 0;
+            while (tag_ep(cut_word) != tag) {
+                if (++spins > (1u << 22)) break;
+                cut_word = ld_relaxed_u64(cut_src);
             }
-            ok1 = __shfl_sync(0xFFFFu, ok1, 0);
-            __syncwarp(0xFFFFu);
-            if (ok1) {
-                const float second = __ldcg(split_part + (size_t)tl * kTR + tid - 32);
-                os.vals[(ntl - 1) * kTR + tid - 32] = os.vals[(ntl - 1) * kTR + tid - 32] + second;
-                if (tid == 32) split_cnt[tl] = 0;
-            } else if (tid == 32) {
+            if (tag_ep(cut_word) == tag) {
+                const int k = (ntl - 1) * kTR + tid - 32;
+                os.vals[k] = os.vals[k] + tag_val(cut_word);
+            } else {
                 os.state[0] = 1;
             }
         }
         if (cut1 && csync_or(os.state[0] != 0)) return false;
+        if (tid == 0) os.state[0] = os.state[1] = 0;
+        PHASE_T(pstep, pop, 8);
         const bool skip0 = cut0;
         for (int i = tid; i < ntl * (kTR / kRB); i += kThreads) {
             const int lt = i / (kTR / kRB), q = i % (kTR / kRB);
@@ -478,6 +532,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             more = cursor_next(cu, w, m);
         }
         if (csync_or(!ok)) return false;
+        for (int i = tid; i < kWarps * kTR; i += kThreads) os.part[i] = 0.0f;   // the warps' stages
     }
     return true;
 }
@@ -597,92 +652,167 @@ struct DecodeEpi {
 constexpr int kAttnUnit = 16;
 constexpr int kQ4 = kMaxHead / 16;     // float4 of K per lane per position
 
+// One attention unit on one warp: scores of positions [t0, t0 + n) of
+// head h against q, their max m, l = sum of e^(s - m), and o = sum of
+// e^(s - m) v_t (4 head elements per lane: 4 * lane .. + 3, when vl).
+struct AttnPart {
+    float m, l;
+    float4 o;
+};
+
+__device__ __forceinline__ AttnPart attn_unit(const DecodeArgs& a, const float* kc, const float* vc, int h, int t0, int n) {
+    const int hs = a.head_size, lane = threadIdx.x & 31;
+    const int hq = hs / 4, sub = lane & 3, pg = lane >> 2;
+    const int kvh = h / a.kv_mul;
+    const float rs = sqrtf((float)hs);
+    const bool vl = 4 * lane < hs;
+    const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float* qp = a.q + h * hs + sub * hq;
+    const float* kr0 = kc + (size_t)(t0 + pg) * a.kv_dim + kvh * hs + sub * hq;
+    const float* kr1 = kr0 + (size_t)8 * a.kv_dim;
+    float4 qv[kQ4], k0[kQ4], k1[kQ4];
+#pragma unroll
+    for (int j = 0; j < kQ4; j++) {
+        const bool in = 4 * j < hq;
+        qv[j] = in ? __ldcg(reinterpret_cast<const float4*>(qp + 4 * j)) : z4;
+        k0[j] = (in && pg < n) ? __ldcg(reinterpret_cast<const float4*>(kr0 + 4 * j)) : z4;
+        k1[j] = (in && pg + 8 < n) ? __ldcg(reinterpret_cast<const float4*>(kr1 + 4 * j)) : z4;
+    }
+    float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kQ4; j++) {
+        d0 = fmaf(qv[j].x, k0[j].x, d0);
+        d0 = fmaf(qv[j].y, k0[j].y, d0);
+        d0 = fmaf(qv[j].z, k0[j].z, d0);
+        d0 = fmaf(qv[j].w, k0[j].w, d0);
+        d1 = fmaf(qv[j].x, k1[j].x, d1);
+        d1 = fmaf(qv[j].y, k1[j].y, d1);
+        d1 = fmaf(qv[j].z, k1[j].z, d1);
+        d1 = fmaf(qv[j].w, k1[j].w, d1);
+    }
+    d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+    d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
+    d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+    float sc[kAttnUnit];
+#pragma unroll
+    for (int pp = 0; pp < 8; pp++) {
+        sc[pp] = __shfl_sync(0xffffffffu, d0, pp * 4);
+        sc[8 + pp] = __shfl_sync(0xffffffffu, d1, pp * 4);
+    }
+    const float* vr = vc + (size_t)t0 * a.kv_dim + kvh * hs + 4 * lane;
+    float4 vv[kAttnUnit];
+#pragma unroll
+    for (int p = 0; p < kAttnUnit; p++)
+        vv[p] = (p < n && vl) ? __ldcg(reinterpret_cast<const float4*>(vr + (size_t)p * a.kv_dim)) : z4;
+    float m = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < kAttnUnit; p++) {
+        sc[p] = p < n ? __fdiv_rn(sc[p], rs) : -INFINITY;
+        m = fmaxf(m, sc[p]);
+    }
+    float l = 0.0f;
+#pragma unroll
+    for (int p = 0; p < kAttnUnit; p++) {
+        sc[p] = p < n ? expf(sc[p] - m) : 0.0f;
+        l += sc[p];
+    }
+    float4 o = z4;
+#pragma unroll
+    for (int p = 0; p < kAttnUnit; p++) {
+        o.x = fmaf(sc[p], vv[p].x, o.x);
+        o.y = fmaf(sc[p], vv[p].y, o.y);
+        o.z = fmaf(sc[p], vv[p].z, o.z);
+        o.w = fmaf(sc[p], vv[p].w, o.w);
+    }
+    return AttnPart{m, l, o};
+}
+
+// Merges nch partials laid out [m, l, -, -, o[0..hs)] at stride pstride
+// (chunk order; read through `ld`) into att[h]: the warp's lanes hold 32
+// chunks' max and sum per pass.
+template <class Ld>
+__device__ __forceinline__ void attn_merge(const DecodeArgs& a, int h, const float* ph, int nch, int pstride, Ld ld) {
+    const int hs = a.head_size, lane = threadIdx.x & 31;
+    const bool vl = 4 * lane < hs;
+    float M = -INFINITY;
+    for (int c0 = 0; c0 < nch; c0 += 32)
+        if (c0 + lane < nch) M = fmaxf(M, ld(ph + (size_t)(c0 + lane) * pstride));
+    M = warp_max(M);
+    float L = 0.0f;
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int c0 = 0; c0 < nch; c0 += 32) {
+        const int cn = min(32, nch - c0);
+        float wl = 0.0f, ll = 0.0f;
+        if (lane < cn) {
+            wl = expf(ld(ph + (size_t)(c0 + lane) * pstride) - M);
+            ll = ld(ph + (size_t)(c0 + lane) * pstride + 1);
+        }
+        for (int c = 0; c < cn; c++) {
+            const float wgt = __shfl_sync(0xffffffffu, wl, c);
+            const float lc = __shfl_sync(0xffffffffu, ll, c);
+            L = fmaf(lc, wgt, L);
+            if (vl) {
+                const float* oc = ph + (size_t)(c0 + c) * pstride + 4 + 4 * lane;
+                acc.x = fmaf(ld(oc), wgt, acc.x);
+                acc.y = fmaf(ld(oc + 1), wgt, acc.y);
+                acc.z = fmaf(ld(oc + 2), wgt, acc.z);
+                acc.w = fmaf(ld(oc + 3), wgt, acc.w);
+            }
+        }
+    }
+    const float inv = 1.0f / L;
+    if (vl) __stcg(reinterpret_cast<float4*>(a.att + h * hs + 4 * lane),
+                   make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+}
+
+// Asks L2 for the K and V rows [0, pos) of a layer (written by earlier
+// steps, evicted by the weight stream since): spread over every compute
+// thread of the grid, issued when the layer's QKV op starts so that its
+// attention finds them in L2 instead of paying HBM latency under load.
+__device__ __forceinline__ void prefetch_kv_l2(const DecodeArgs& a, int layer, int pos) {
+    const size_t lkv = (size_t)layer * a.max_pos * a.kv_dim;
+    const size_t bytes = (size_t)pos * a.kv_dim * 4;   // rows [0, pos) are contiguous
+    const size_t lines = (bytes + 127) / 128;
+    const char* kb = reinterpret_cast<const char*>(a.kcache + lkv);
+    const char* vb = reinterpret_cast<const char*>(a.vcache + lkv);
+    for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < lines; i += (size_t)gridDim.x * kThreads) {
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(kb + 128 * i));
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(vb + 128 * i));
+    }
+}
+
+// Attention of one layer (src/kernel_simd.c:1099-1117, softmax :816-826),
+// split into warp units: unit (head h, chunk k) covers positions [16k,
+// 16k+16) ∩ [0, pos], one warp each, spread over every warp of the grid
+// (unit u on CTA u mod G, warp u div G).  With a single chunk the warp
+// writes att[h] directly; otherwise it writes a partial and the last warp
+// of a head (atomic count) merges the partials in chunk order.
 __device__ void attention_layer(const DecodeArgs& a, int layer, int pos) {
     const int hs = a.head_size, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int hq = hs / 4, sub = lane & 3, pg = lane >> 2;
     const int nch = pos / kAttnUnit + 1;
-    const int units = a.n_heads * nch;
     const size_t lkv = (size_t)layer * a.max_pos * a.kv_dim;
     const float* kc = a.kcache + lkv;
     const float* vc = a.vcache + lkv;
-    const float rs = sqrtf((float)hs);
     const int pstride = hs + 4;
-    const int nw = gridDim.x * kWarps;
     const bool vl = 4 * lane < hs;
-    const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const int units = a.n_heads * nch;
+    const int nw = gridDim.x * kWarps;
     for (int u = warp * gridDim.x + blockIdx.x; u < units; u += nw) {
         const int h = u / nch, k = u - (u / nch) * nch;
-        const int kvh = h / a.kv_mul;
         const int t0 = k * kAttnUnit, n = min(kAttnUnit, pos + 1 - t0);
-        const float* qp = a.q + h * hs + sub * hq;
-        const float* kr0 = kc + (size_t)(t0 + pg) * a.kv_dim + kvh * hs + sub * hq;
-        const float* kr1 = kr0 + (size_t)8 * a.kv_dim;
-        float4 qv[kQ4], k0[kQ4], k1[kQ4];
-#pragma unroll
-        for (int j = 0; j < kQ4; j++) {
-            const bool in = 4 * j < hq;
-            qv[j] = in ? __ldcg(reinterpret_cast<const float4*>(qp + 4 * j)) : z4;
-            k0[j] = (in && pg < n) ? __ldcg(reinterpret_cast<const float4*>(kr0 + 4 * j)) : z4;
-            k1[j] = (in && pg + 8 < n) ? __ldcg(reinterpret_cast<const float4*>(kr1 + 4 * j)) : z4;
-        }
-        float d0 = 0.0f, d1 = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kQ4; j++) {
-            d0 = fmaf(qv[j].x, k0[j].x, d0);
-            d0 = fmaf(qv[j].y, k0[j].y, d0);
-            d0 = fmaf(qv[j].z, k0[j].z, d0);
-            d0 = fmaf(qv[j].w, k0[j].w, d0);
-            d1 = fmaf(qv[j].x, k1[j].x, d1);
-            d1 = fmaf(qv[j].y, k1[j].y, d1);
-            d1 = fmaf(qv[j].z, k1[j].z, d1);
-            d1 = fmaf(qv[j].w, k1[j].w, d1);
-        }
-        d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
-        d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
-        d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
-        d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
-        float sc[kAttnUnit];
-#pragma unroll
-        for (int pp = 0; pp < 8; pp++) {
-            sc[pp] = __shfl_sync(0xffffffffu, d0, pp * 4);
-            sc[8 + pp] = __shfl_sync(0xffffffffu, d1, pp * 4);
-        }
-        const float* vr = vc + (size_t)t0 * a.kv_dim + kvh * hs + 4 * lane;
-        float4 vv[kAttnUnit];
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++)
-            vv[p] = (p < n && vl) ? __ldcg(reinterpret_cast<const float4*>(vr + (size_t)p * a.kv_dim)) : z4;
-        float m = -INFINITY;
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++) {
-            sc[p] = p < n ? __fdiv_rn(sc[p], rs) : -INFINITY;
-            m = fmaxf(m, sc[p]);
-        }
-        float l = 0.0f;
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++) {
-            sc[p] = p < n ? expf(sc[p] - m) : 0.0f;
-            l += sc[p];
-        }
-        float4 o = z4;
-#pragma unroll
-        for (int p = 0; p < kAttnUnit; p++) {
-            o.x = fmaf(sc[p], vv[p].x, o.x);
-            o.y = fmaf(sc[p], vv[p].y, o.y);
-            o.z = fmaf(sc[p], vv[p].z, o.z);
-            o.w = fmaf(sc[p], vv[p].w, o.w);
-        }
+        const AttnPart p = attn_unit(a, kc, vc, h, t0, n);
         if (nch == 1) {
-            const float inv = 1.0f / l;
+            const float inv = 1.0f / p.l;
             if (vl) __stcg(reinterpret_cast<float4*>(a.att + h * hs + 4 * lane),
-                           make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv));
+                           make_float4(p.o.x * inv, p.o.y * inv, p.o.z * inv, p.o.w * inv));
             continue;
         }
         float* part = a.attn_part + ((size_t)h * a.max_chunks + k) * pstride;
-        if (vl) __stcg(reinterpret_cast<float4*>(part + 4 + 4 * lane), o);
+        if (vl) __stcg(reinterpret_cast<float4*>(part + 4 + 4 * lane), p.o);
         if (lane == 0) {
-            __stcg(part, m);
-            __stcg(part + 1, l);
+            __stcg(part, p.m);
+            __stcg(part + 1, p.l);
         }
         __threadfence();
         __syncwarp();
@@ -691,37 +821,8 @@ __device__ void attention_layer(const DecodeArgs& a, int layer, int pos) {
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
-        // Merge: lane c holds chunk c's max and sum (32 chunks per pass).
-        const float* ph = a.attn_part + (size_t)h * a.max_chunks * pstride;
-        float M = -INFINITY;
-        for (int c0 = 0; c0 < nch; c0 += 32)
-            if (c0 + lane < nch) M = fmaxf(M, __ldcg(ph + (size_t)(c0 + lane) * pstride));
-        M = warp_max(M);
-        float L = 0.0f;
-        float4 acc = z4;
-        for (int c0 = 0; c0 < nch; c0 += 32) {
-            const int cn = min(32, nch - c0);
-            float wl = 0.0f, ll = 0.0f;
-            if (lane < cn) {
-                wl = expf(__ldcg(ph + (size_t)(c0 + lane) * pstride) - M);
-                ll = __ldcg(ph + (size_t)(c0 + lane) * pstride + 1);
-            }
-            for (int c = 0; c < cn; c++) {
-                const float wgt = __shfl_sync(0xffffffffu, wl, c);
-                const float lc = __shfl_sync(0xffffffffu, ll, c);
-                L = fmaf(lc, wgt, L);
-                if (vl) {
-                    const float4 oc = __ldcg(reinterpret_cast<const float4*>(ph + (size_t)(c0 + c) * pstride + 4 + 4 * lane));
-                    acc.x = fmaf(oc.x, wgt, acc.x);
-                    acc.y = fmaf(oc.y, wgt, acc.y);
-                    acc.z = fmaf(oc.z, wgt, acc.z);
-                    acc.w = fmaf(oc.w, wgt, acc.w);
-                }
-            }
-        }
-        const float inv = 1.0f / L;
-        if (vl) __stcg(reinterpret_cast<float4*>(a.att + h * hs + 4 * lane),
-                       make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+        attn_merge(a, h, a.attn_part + (size_t)h * a.max_chunks * pstride, nch, pstride,
+                   [](const float* x) { return __ldcg(x); });
         if (lane == 0) a.attn_cnt[h] = 0;
     }
 }
@@ -913,18 +1014,25 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
         reinterpret_cast<int*>(ops)[i] = __ldg(reinterpret_cast<const int*>(a.ops) + i);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     Ring ring;
-    if (warp < kWarps) ring_init(ring, ring_base, bars, a.P, a.slot_bytes, warp, lane == 0);
+    if (warp < kWarps) {
+        ring_init(ring, ring_base, bars, a.P, a.slot_bytes, warp, lane == 0);
+        reset_opsmem(os);
+    }
     fence_mbar_init();
-    __syncthreads();   // all kDecodeThreads: the op table and the barriers are ready
+    __syncthreads();   // all kDecodeThreads: the op table, the barriers and OpSmem are ready
     if (warp == kWarps) {
         if (lane < kWarps) produce(a, ops, ring_base, bars, lane, MODE);
         return;
     }
     Seq seq;   // unused: the producer warp issues every chunk
-    __shared__ uint32_t s_xcount;
-    if (threadIdx.x == 0) s_xcount = *reinterpret_cast<volatile uint32_t*>(&a.step->tp_count);
+    __shared__ uint32_t s_xcount, s_opseq;
+    if (threadIdx.x == 0) {
+        s_xcount = *reinterpret_cast<volatile uint32_t*>(&a.step->tp_count);
+        s_opseq = *reinterpret_cast<volatile uint32_t*>(&a.step->op_seq);
+    }
     csync();
     uint32_t xcount = s_xcount;   // tensor-parallel exchanges so far (identical on every rank)
+    const uint32_t op_seq = s_opseq;
 
     uint32_t nbar = 0;
     bool ok = true;
@@ -978,16 +1086,23 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
             } else {
                 src.p = op.kind == OP_WO ? a.att : a.hb;
             }
+            PHASE_T(step, oi, 0);
+            if (op.kind == OP_QKV && MODE != MODE_W4A8) prefetch_kv_l2(a, op.layer, pos);
             build_input<MODE>(xf, xs, src, op.m.n, nw, red);
             csync();
+            PHASE_T(step, oi, 1);
             DecodeEpi epi{&a, &op, pos, s_freq, -1e9f, 0u};
             if (a.tp_n > 1 && (op.kind == OP_WO || op.kind == OP_W2)) epi.xcount = ++xcount;
-            if (!run_op<MODE, true>(op.m, ring, ring_base, seq, ops, a.nops, a.steps, xf, xs, os, a.split_part, a.split_cnt,
-                              epi)) {
+            // Cut-tile tag of this op: unique over every decode launch of the
+            // context (op_seq counts all ops before this launch), never 0.
+            const uint32_t ctag = (op_seq + (uint32_t)(step * a.nops + oi)) % 0xFFFFFFFFu + 1u;
+            if (!run_op<MODE, true>(op.m, ring, ring_base, seq, ops, a.nops, a.steps, xf, xs, os, a.split_part, ctag,
+                                    epi, step, oi)) {
                 set_error(a.step, DEV_COPY_TIMEOUT);
                 ok = false;
                 break;
             }
+            PHASE_T(step, oi, 3);
             if (op.kind == OP_CLS) cta_argmax(a.argmax, epi.best, epi.best_i, red64);
             if (a.tp_n > 1 && (op.kind == OP_WO || op.kind == OP_W2)) {
                 // Sum the ranks' partial rows into the residual stream.
@@ -1033,6 +1148,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
             }
             if (oi == a.nops - 1 && step == a.steps - 1) break;   // nothing after the last classifier
             if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+            PHASE_T(step, oi, 4);
             if (op.kind == OP_QKV) {
                 if (op.layer == 0 && blockIdx.x == 0 && threadIdx.x == 0) {
                     // Every CTA has read the step state and the argmax key.
@@ -1049,11 +1165,16 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
                     attention_layer_exact(a, op.layer, pos, reinterpret_cast<float*>(xf), red);
                 else
                     attention_layer(a, op.layer, pos);
+                PHASE_T(step, oi, 5);
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
+                PHASE_T(step, oi, 6);
             }
         }
     }
-    if (blockIdx.x == 0 && threadIdx.x == 0) a.step->tp_count = xcount;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        a.step->tp_count = xcount;
+        a.step->op_seq = op_seq + (uint32_t)(a.steps * a.nops);   // every tag this launch could have used
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1061,11 +1182,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
 // and epilogue machinery as one op of the decode kernel.
 // ---------------------------------------------------------------------------
 struct StandaloneArgs {
+    uint32_t epoch;                // tag of this call's cut-tile flags (nonzero)
     OpDesc op;
     const float* x;
     float* y;
-    float* split_part;
-    int* split_cnt;
+    uint64_t* split_part;
     int P, slot_bytes, xbytes, xs_off;
     int* error;
 };
@@ -1092,6 +1213,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_matvec(StandaloneArgs a) {
     if (threadIdx.x == 0) s_op = a.op;
     Ring ring;
     ring_init(ring, ring_base, bars, a.P, a.slot_bytes, threadIdx.x >> 5, (threadIdx.x & 31) == 0);
+    reset_opsmem(os);
     fence_mbar_init();
     csync();
     Seq seq;
@@ -1107,7 +1229,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_matvec(StandaloneArgs a) {
     build_input<MODE>(xf, xs, src, s_op.m.n, nullptr, red);
     csync();
     StoreEpi epi{a.y, a.op.m.d};
-    if (!run_op<MODE, false>(s_op.m, ring, ring_base, seq, &s_op, 1, 1, xf, xs, os, a.split_part, a.split_cnt, epi))
+    if (!run_op<MODE, false>(s_op.m, ring, ring_base, seq, &s_op, 1, 1, xf, xs, os, a.split_part, a.epoch, epi))
         if (threadIdx.x == 0) atomicCAS(a.error, 0, DEV_COPY_TIMEOUT);
     ring_drain(ring);
 }

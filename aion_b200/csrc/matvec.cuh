@@ -359,9 +359,8 @@ struct OpWork {
     int u0, u1;          // split: unit range; whole: tile range
 };
 
-__device__ __forceinline__ OpWork op_work(const MatDesc& m, int mode) {
+__host__ __device__ inline OpWork op_work_at(const MatDesc& m, int mode, int c, int G) {
     OpWork w;
-    const int G = gridDim.x, c = blockIdx.x;
     w.split = (mode != MODE_W4A8 && m.ntiles >= G && m.ntiles <= (kMaxLocalTiles - 2) * G) ? 1 : 0;
     const long long U = w.split ? (long long)m.ntiles * m.nch : m.ntiles;
     if (U * G < (1LL << 31)) {   // 32-bit division when the products fit
@@ -374,6 +373,7 @@ __device__ __forceinline__ OpWork op_work(const MatDesc& m, int mode) {
     }
     return w;
 }
+__device__ __forceinline__ OpWork op_work(const MatDesc& m, int mode) { return op_work_at(m, mode, blockIdx.x, gridDim.x); }
 
 // Position in a warp's chunk sequence of one op: unit index a (split) or
 // tile index (whole), and the tile / chunk it stands for.

@@ -69,9 +69,9 @@ def weight_bytes_per_token(layers: int) -> int:
     return int(0.625 * (layers * (4 * dim * dim + 3 * dim * hid) + vocab * dim))
 MATVEC_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes per token of the decode kernel's weight stream, from one ncu
-# capture (dram__bytes_read.sum + dram__bytes_write.sum of an 8-step 7B
-# launch, minus its K/V reads; profiles/k_decode_7b_dram.md).
+# DRAM bytes per token of the decode kernel's weight stream, measured once
+# with ncu (dram__bytes_read.sum + dram__bytes_write.sum of an 8-step 7B
+# launch, minus its K/V reads): 1.0001 x the algorithmic weight bytes.
 DRAM_WEIGHT_BYTES_PER_TOKEN = 4.1296e9
 
 
@@ -96,22 +96,38 @@ def ckpt_dir() -> Path:
     return d
 
 
-def ensure_7b(rank: int, layers: int = 0) -> Path:
+def ensure_7b(rank: int, layers: int = 0, writer: str = "aion") -> Path:
     """Writes the seeded 7B int4 checkpoint once per host (rank 0); with
-    layers > 0, the same shapes truncated to that many layers."""
-    import aion_b200 as A
+    layers > 0, the same shapes truncated to that many layers.  writer
+    "aion" uses the library's synthesizer; "reference" runs
+    oracle/_ref/synth_ckpt, the same generator feeding the reference's own
+    quantize_buffer (quantize.c), so the reference arm loads nothing of the
+    product library.  Both write identical bytes (tests/test_oracle.py)."""
     cfg = CFG_7B if layers <= 0 else (CFG_7B[0], CFG_7B[1], layers) + CFG_7B[3:]
     name = "llama2_7b_seed1.int4" if layers <= 0 else f"llama2_7b_shape_{layers}l_seed1.int4"
     path = ckpt_dir() / name
     done = path.with_suffix(".done")
     if rank == 0 and not done.exists():
         tmp = path.with_suffix(".tmp")
-        A.synth_checkpoint(tmp, cfg, SEED_7B, int4=True)
+        if writer == "reference":
+            subprocess.run([str(ROOT / "oracle" / "_ref" / "synth_ckpt"), str(tmp), *map(str, cfg), str(SEED_7B)],
+                           check=True)
+        else:
+            import aion_b200 as A
+            A.synth_checkpoint(tmp, cfg, SEED_7B, int4=True)
         tmp.rename(path)
         done.write_text("ok")
     while not done.exists():
         time.sleep(1.0)
     return path
+
+
+def config_7b(world: int, layers: int = 0) -> dict:
+    """The workload's config dict, identical in both arms."""
+    return {"workload": "llama2-7b-shape W4A16 greedy decode, batch 1, 512-token workload",
+            "dim": CFG_7B[0], "hidden": CFG_7B[1], "layers": layers if layers > 0 else CFG_7B[2],
+            "heads": CFG_7B[3], "vocab": CFG_7B[5], "seed": SEED_7B, "parallelism": f"replicas x{world}",
+            "l2": "weights 4.13 GB/token > L2 (no flush needed)"}
 
 
 def ensure_13b(rank: int) -> Path:
@@ -176,15 +192,24 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_reference_decode(path: Path, warmup: int, max_tokens: int, budget_s: float) -> dict:
+_REF_ENGINE = None
+
+
+def cpu_reference_decode(path: Path, warmup: int, max_tokens: int, budget_s: float, w4a8: bool = False) -> dict:
     """The reference's own CPU int4 path (scalar int4 kernel, pthread pool)
-    on the 7B checkpoint: tokens/s over a bounded sample of the workload."""
+    on the 7B checkpoint: tokens/s over a bounded sample of the workload.
+    w4a8: the reference's quantize_activations_neon + matmul_w4a8_neon
+    wired into its forward pass by oracle/ref_harness.c (through the scalar
+    NEON shim on x86 hosts)."""
+    global _REF_ENGINE
     from oracle.oracle import REF_DIR, Oracle, Reference
     cores = os.cpu_count() or 1
     threads = max(1, cores - 1)       # T = cores oversubscribes the spin barrier
     if (REF_DIR / "libaionref.so").exists():
-        ref = Reference().open(path, threads=threads, scalar=True)
-        fwd = ref.L.ref_forward
+        if _REF_ENGINE is None:       # the reference engine is process-global: open once
+            _REF_ENGINE = Reference().open(path, threads=threads, scalar=True)
+        ref = _REF_ENGINE
+        fwd = ref.L.ref_forward_w4a8 if w4a8 else ref.L.ref_forward
         logits = lambda: np.ctypeslib.as_array(ref.L.ref_logits(), (CFG_7B[5],))  # noqa: E731
         kind = "reference"
     else:
@@ -206,9 +231,11 @@ def cpu_reference_decode(path: Path, warmup: int, max_tokens: int, budget_s: flo
         pos += 1
         n += 1
     secs = time.perf_counter() - t0
+    what = ("reference W4A8 functions (quantize_activations_neon + matmul_w4a8_neon via the scalar NEON shim)"
+            if w4a8 else "reference scalar int4 path")
     return {"value": n / secs, "unit": "tok/s", "cores": threads, "kind": kind, "tokens": n, "seconds": secs,
-            "sample": f"7B W4A16 greedy decode from BOS, {n} tokens at positions {warmup}..{warmup + n - 1} "
-                      f"after {warmup} warm-up tokens; reference scalar int4 path, {threads} pthreads on "
+            "sample": f"7B {'W4A8' if w4a8 else 'W4A16'} greedy decode from BOS, {n} tokens at positions "
+                      f"{warmup}..{warmup + n - 1} after {warmup} warm-up tokens; {what}, {threads} pthreads on "
                       f"{cores} host cores"}
 
 
@@ -216,14 +243,13 @@ def run_reference_arm(args) -> None:
     world, rank, _ = dist_setup()
     if rank != 0:
         return
-    path = ensure_7b(0)
-    cb = cpu_reference_decode(path, min(args.warmup, 3), args.steps, budget_s=args.ref_budget)
+    path = ensure_7b(0, writer="reference")
+    cb = cpu_reference_decode(path, args.warmup, args.steps, budget_s=args.ref_budget)
     line = {"metric": "Llama-2-7B int4 decode tok/s (batch 1)", "value": cb["value"], "unit": "tok/s",
-            "n_gpus": world, "steps": cb["tokens"], "warmup": min(args.warmup, 3),
+            "n_gpus": world, "steps": cb["tokens"], "warmup": args.warmup,
             "ms_per_step": 1000.0 / cb["value"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int4 weights, fp32 activations", "data": "synthetic",
-            "config": {"workload": "llama2-7b-shape W4A16 greedy decode, batch 1, 512-token workload",
-                       "dim": 4096, "hidden": 11008, "layers": 32, "vocab": 32000, "seed": SEED_7B},
+            "config": config_7b(world),
             "impl": "reference",
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -520,6 +546,50 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
         pg.destroy_process_group()
 
 
+def w4a8_leg(path: Path, device: int, steps: int, warmup: int, cpu: bool) -> dict:
+    """7B W4A8 greedy decode, batch 1 (activations quantized per group of 32
+    to int8 before every matmul, as the reference's W4A8 functions): the same
+    persistent launch and timing as the W4A16 headline, its own roofline, and
+    the reference's W4A8 path on the host cores beside it."""
+    import torch
+    import aion_b200 as A
+    steps = min(steps, WORKLOAD_TOKENS - warmup)
+    model = A.Model(path, device=device, mode="w4a8", max_pos=WORKLOAD_TOKENS)
+    stream = torch.cuda.ExternalStream(model.stream_ptr(), device=f"cuda:{device}")
+    model.decode_async(warmup, BOS, 0)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    model.decode_async(steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    toks = model.tokens(warmup + steps)
+    model.close()
+    L = CFG_7B[2]
+    wb = weight_bytes_per_token(L)
+    gbs = wb * steps / (ms * 1e-3) / 1e9
+    peak, kind = hbm_peak()
+    parity = None
+    gold = ROOT / "tests" / "golden" / "7b.json"
+    if gold.exists():
+        want = json.loads(gold.read_text()).get("w4a8_tokens", [])
+        k = min(len(want), len(toks))
+        parity = {"tokens_compared": k, "identical": toks[:k] == want[:k]}
+    out = {"workload": f"llama2-7b-shape W4A8 greedy decode from BOS, batch 1, positions {warmup}..{warmup + steps - 1}",
+           "value": steps / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms / steps, "steps": steps,
+           "warmup": warmup,
+           "dtype": "s4 weights x s8 activations (reference per-group quantization), int32 group dots, fp32 row sums",
+           "roofline": {"kernel": "k_decode<W4A8> (persistent decode, all steps)", "bound": "hbm", "achieved": gbs,
+                        "peak": peak, "peak_kind": kind, "unit": "GB/s", "frac": gbs / peak,
+                        "bytes_per_token": wb},
+           "gpu_launches": 1, "parity": parity}
+    if cpu:
+        cb = cpu_reference_decode(path, 2, 200, budget_s=15.0, w4a8=True)
+        out["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -531,6 +601,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-matvec", action="store_true", help="skip the isolated matvec shapes")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill leg")
+    ap.add_argument("--no-w4a8", action="store_true", help="skip the W4A8 decode leg")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
     ap.add_argument("--tp13b", action="store_true", help="13B shape, tensor-parallel over the launch's ranks")
     ap.add_argument("--batch", type=int, default=0, help="7B lock-step batched decode of this many sequences")
@@ -692,6 +763,11 @@ def main() -> None:
         cb = cpu_reference_decode(path, 2, 1000, budget_s=20.0)
         cpu = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
+    w4a8 = None
+    if rank == 0 and world == 1 and not args.no_w4a8 and args.profile_layers <= 0:
+        model.close()
+        w4a8 = w4a8_leg(path, local, args.steps, args.warmup, cpu=not args.no_cpu)
+
     if rank == 0:
         line = {
             "metric": "Llama-2-7B int4 decode tok/s (batch 1)",
@@ -699,9 +775,7 @@ def main() -> None:
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "s4 weights x s8 activation digits (int32 tensor-core dot), fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": "llama2-7b-shape W4A16 greedy decode, batch 1, 512-token workload",
-                       "dim": dim, "hidden": hid, "layers": L, "heads": 32, "vocab": vocab, "seed": SEED_7B,
-                       "parallelism": f"replicas x{world}", "l2": "weights 4.13 GB/token > L2 (no flush needed)"},
+            "config": config_7b(world, args.profile_layers),
             "roofline": roofline, "matvec": matvec,
             "gpu_launches": launches,
             "clocks": clk,
@@ -710,6 +784,7 @@ def main() -> None:
             "cpu_baseline": cpu,
             "parity": parity,
             "prefill": prefill,
+            "w4a8": w4a8,
         }
         print(json.dumps(line), flush=True)
     model.close()

@@ -273,6 +273,17 @@ AION_API aion_status aion_matvec_w4a8(const aion_qmatrix* w, const float* x_dev,
  * before any stream capture on that device. */
 AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, const float* x_dev, float* y_dev, void* stream);
 
+/* Waits for `stream`, then reports whether a matvec on `w` enqueued before
+ * it (aion_matvec_w4a16 / _w4a8 on the matrix's scratch, or
+ * aion_matvec_w4a16_static on this device's array) gave up one of its
+ * bounded waits: AION_ERR_TIMEOUT means that call's y is invalid.  Clears
+ * the record.  The reference's matmul has no failure mode (it spins in its
+ * barrier, src/kernel_simd.c:93-106); this is the status-never-abort
+ * contract's read-out for the asynchronous kernel-level calls.  Calls on
+ * one matrix's scratch that overlap on the GPU (different streams) race, as
+ * calls of the static variant do. */
+AION_API aion_status aion_matvec_status(const aion_qmatrix* w, void* stream);
+
 /* Dense GEMM on the tensor cores: C[m][n] (fp32) = A[m][k] * B[n][k]^T with
  * A and B bf16 (K contiguous), all device memory, on the current device.
  * The building block of the batched prefill, where B holds int4 weights

@@ -9,6 +9,7 @@ and bench.py's CPU-baseline leg use this module, as the checker.
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
@@ -22,9 +23,19 @@ _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 
 
+# Where this build recipe reads the reference sources from: AION_REFERENCE,
+# else the container's read-only checkout when it is there (the GPU box has
+# none and uses the prebuilt _ref/).
+REFERENCE_TREE = os.environ.get("AION_REFERENCE") or ("/root/reference" if Path("/root/reference/quantize.c").exists()
+                                                      else "")
+
+
 def build() -> None:
     """Builds liboracle.so (and _ref/ where the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", str(HERE)], check=True, capture_output=True)
+    cmd = ["make", "-s", "-C", str(HERE)]
+    if REFERENCE_TREE:
+        cmd.append(f"REF={REFERENCE_TREE}")
+    subprocess.run(cmd, check=True, capture_output=True)
 
 
 def _np(a) -> int:

@@ -4,8 +4,10 @@ allocation) against aion_matvec_w4a16 on the same matrix, through the C ABI.
 The static variant runs the same kernel with its scratch in a fixed device
 array, so its results equal the handle-based entry point's; the check
 allows 1e-6 relative all the same.  Two calls in a row exercise the
-scratch's reset between calls.  The file name makes it collect last, so it
-also runs after every other GPU test of the session.
+per-call tags of the scratch's cut-tile flags, and a loop of calls leaves
+the device's free memory unchanged: the call path allocates nothing.  The
+file name makes it collect last, so it also runs after every other GPU test
+of the session.
 """
 from __future__ import annotations
 
@@ -48,6 +50,17 @@ def test_static_scratch_matvec_matches(cuda, shape):
         g, w = got.cpu().numpy(), want.cpu().numpy()
         assert np.isfinite(g).all()
         assert np.abs(g - w).max() <= 1e-6 * scale
+    assert L.aion_matvec_status(q._h, None) == 0, L.aion_last_error(None)
+    # No allocation on the call path: free device memory is unchanged by a
+    # run of calls (the first call on the device above resolved the array).
+    got = torch.empty(d, device="cuda")
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(20):
+        assert L.aion_matvec_w4a16_static(q._h, _vp(x), _vp(got), None) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
     q.free()
 
 
