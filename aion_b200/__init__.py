@@ -65,7 +65,8 @@ class Config(ctypes.Structure):
 class Opts(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("mode", ctypes.c_int32), ("max_batch", ctypes.c_int32),
                 ("max_pos", ctypes.c_int32), ("tp_size", ctypes.c_int32), ("tp_rank", ctypes.c_int32),
-                ("nccl_id", ctypes.c_void_p), ("use_graph", ctypes.c_int32), ("reserved", ctypes.c_int32 * 7)]
+                ("nccl_id", ctypes.c_void_p), ("use_graph", ctypes.c_int32), ("wait_ms", ctypes.c_int32),
+                ("reserved", ctypes.c_int32 * 6)]
 
 
 _lib = None
@@ -237,7 +238,7 @@ class Model:
     reference (src/kernel_simd.c:941-1008), on one B200."""
 
     def __init__(self, path, device: int = 0, mode: str = "int4", max_pos: int = 0, use_graph: bool = True,
-                 max_batch: int = 1, tp_size: int = 1, tp_rank: int = 0):
+                 max_batch: int = 1, tp_size: int = 1, tp_rank: int = 0, wait_ms: int = 0):
         L = lib()
         o = Opts()
         L.aion_default_opts(ctypes.byref(o))
@@ -248,6 +249,7 @@ class Model:
         o.max_batch = max_batch
         o.tp_size = tp_size
         o.tp_rank = tp_rank
+        o.wait_ms = wait_ms
         h = ctypes.c_void_p()
         _check(L.aion_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)))
         self._h = h

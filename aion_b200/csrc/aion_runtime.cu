@@ -536,6 +536,8 @@ static cudaError_t launch_decode_mode(aion_ctx* c, int steps) {
     a.exp_host.x = c->exp_tab;
     a.exp_host.n = c->exp_n;
     a.exp_host.delta = c->exp_delta;
+    a.cr_exp = MODE != MODE_W4A16;
+    a.wait_ns = (unsigned long long)(c->opts.wait_ms > 0 ? c->opts.wait_ms : 2000) * 1000000ull;
     a.samp = c->samp;
     a.sampling = c->sampling;
     // The grid-barrier counter starts from zero in every launch.
@@ -778,7 +780,7 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         bytes += align256(sizeof(StepState)) + align256(8) + align256((size_t)c->max_pos * 4);
         bytes += align256((size_t)(4 * L + 1) * sizeof(OpDesc));
         c->max_tiles = std::max({c->emb.ntiles, dq.ntiles, dwo.ntiles, d13.ntiles, d2.ntiles});
-        bytes += align256((size_t)c->max_tiles * 2 * kTR * 4) + align256((size_t)c->max_tiles * 4);
+        bytes += align256((size_t)c->max_tiles * kTR * 8);
         c->arena_bytes = bytes + 4096;
         CK_RET(&c->err, cudaMalloc(&c->arena, c->arena_bytes));
         CK_RET(&c->err, cudaMemsetAsync(c->arena, 0, c->arena_bytes, c->stream));

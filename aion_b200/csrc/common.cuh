@@ -70,17 +70,18 @@ __host__ __device__ inline float key_value(unsigned long long k) {
 // first kPhaseSteps steps of a decode launch; aion_phase_dump() copies them
 // out.  Normal builds compile PHASE_T to nothing.
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ unsigned long long global_timer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
 #ifdef AION_PHASE_TIMING
 constexpr int kPhaseSteps = 8, kPhaseOps = 168, kPhaseCtas = 160, kPhaseSlots = 12;
 __device__ unsigned long long g_phase[(size_t)kPhaseSteps * kPhaseOps * kPhaseCtas * kPhaseSlots];
 // per (step, op, cta): ring-wait ns and group-dot ns summed over the warps,
 // chunks, then the latest loop end, loop start and per-warp busy time
 __device__ unsigned long long g_phase_w[(size_t)kPhaseSteps * kPhaseOps * kPhaseCtas * 8];
-__device__ __forceinline__ unsigned long long global_timer() {
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 #define PHASE_T(step, op, slot)                                                                               \
     do {                                                                                                      \
         if (threadIdx.x == 0 && (step) < kPhaseSteps && (op) < kPhaseOps && blockIdx.x < kPhaseCtas)          \

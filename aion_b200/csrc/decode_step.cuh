@@ -61,6 +61,7 @@ struct DecodeArgs {
     int P, slot_bytes, xbytes, xs_off;
     int ops_off;                   // shared-memory copy of ops[] (xbytes = ring offset)
     ExpTable exp_host;             // the host expf's deviations (W4A8), or empty
+    int cr_exp;                    // SwiGLU's exp: 1 correctly rounded / host-table (W4A8, fp32), 0 CUDA expf (W4A16)
     SamplerParams samp;            // used when sampling != 0 (else the greedy argmax)
     int sampling;
     // Tensor parallelism over tp_n GPUs (tp_n == 1: off).  This rank holds
@@ -74,6 +75,7 @@ struct DecodeArgs {
     // next partial rows, so no row is overwritten before it is read.
     int q_dim;
     int tp_n, tp_rank, vocab_off;
+    unsigned long long wait_ns;    // bound of each wait on another rank (global timer ns)
     unsigned char* const* tp_peers;
     int tp_keys_off, tp_flags_off;
 };
@@ -616,7 +618,8 @@ struct DecodeEpi {
             for (int r = 0; r < 2; r++)
                 if (h0 + r < A.hidden) {
                     const float g = v[r];
-                    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf_host(-g, A.exp_host)));
+                    const float e = A.cr_exp ? expf_host(-g, A.exp_host) : expf(-g);
+                    const float s = __fdiv_rn(g, __fadd_rn(1.0f, e));
                     __stcg(A.hb + h0 + r, __fmul_rn(s, v[2 + r]));
                 }
             break;
@@ -921,10 +924,11 @@ __device__ bool tp_exchange(const DecodeArgs& a, uint32_t& nbar, uint32_t count)
                 st_release_sys_u32(reinterpret_cast<uint32_t*>(a.tp_peers[j] + a.tp_flags_off) + a.tp_rank, count);
         const volatile uint32_t* fl = reinterpret_cast<const volatile uint32_t*>(a.tp_peers[a.tp_rank] + a.tp_flags_off);
         int ok = 1;
+        const unsigned long long t0 = global_timer();
         for (int j = 0; j < a.tp_n && ok; j++) {
             uint32_t i = 0;
             while ((int32_t)(fl[j] - count) < 0)
-                if (++i > (1u << 24)) {
+                if ((++i & 255u) == 0 && global_timer() - t0 > a.wait_ns) {
                     ok = 0;
                     break;
                 }
@@ -944,12 +948,13 @@ __device__ bool tp_reduce_residual(const DecodeArgs& a, uint32_t count) {
     const uint64_t* recv =
         reinterpret_cast<const uint64_t*>(a.tp_peers[a.tp_rank]) + (size_t)(count & 1u) * a.tp_n * a.dim;
     bool ok = true;
+    const unsigned long long t0 = global_timer();
     for (int row = blockIdx.x * kThreads + threadIdx.x; row < a.dim && ok; row += gridDim.x * kThreads) {
         float sum = 0.0f;
         for (int j = 0; j < a.tp_n && ok; j++) {
             uint64_t t = ld_relaxed_sys_u64(recv + (size_t)j * a.dim + row);
             for (uint32_t i = 0; tag_ep(t) != count; i++) {
-                if (i > (1u << 22)) {
+                if ((i & 63u) == 63u && global_timer() - t0 > a.wait_ns) {
                     ok = false;
                     break;
                 }
@@ -1087,15 +1092,15 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
                 src.p = op.kind == OP_WO ? a.att : a.hb;
             }
             PHASE_T(step, oi, 0);
+            // Tag of this op's cut-tile parts: unique over every decode launch
+            // of the context (op_seq counts all ops before this launch), never 0.
+            const uint32_t ctag = (op_seq + (uint32_t)(step * a.nops + oi)) % 0xFFFFFFFFu + 1u;
             if (op.kind == OP_QKV && MODE != MODE_W4A8) prefetch_kv_l2(a, op.layer, pos);
             build_input<MODE>(xf, xs, src, op.m.n, nw, red);
             csync();
             PHASE_T(step, oi, 1);
             DecodeEpi epi{&a, &op, pos, s_freq, -1e9f, 0u};
             if (a.tp_n > 1 && (op.kind == OP_WO || op.kind == OP_W2)) epi.xcount = ++xcount;
-            // Cut-tile tag of this op: unique over every decode launch of the
-            // context (op_seq counts all ops before this launch), never 0.
-            const uint32_t ctag = (op_seq + (uint32_t)(step * a.nops + oi)) % 0xFFFFFFFFu + 1u;
             if (!run_op<MODE, true>(op.m, ring, ring_base, seq, ops, a.nops, a.steps, xf, xs, os, a.split_part, ctag,
                                     epi, step, oi)) {
                 set_error(a.step, DEV_COPY_TIMEOUT);

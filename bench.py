@@ -473,8 +473,10 @@ def run_batch(args, local: int) -> None:
     model.close()
 
 
-def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
-    """13B-shape decode, tensor-parallel over the launch's ranks."""
+def tp13b_leg(args, world, rank, local, pg, barrier, max_over_ranks):
+    """13B-shape decode, tensor-parallel over the launch's ranks (TP = N,
+    one process per GPU): batch 1 and batch 16 over the 256-token workload.
+    Returns the sub-object of the JSON line on rank 0 (None elsewhere)."""
     import torch
     import aion_b200 as A
     path = ensure_13b(rank)
@@ -526,24 +528,22 @@ def run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks) -> None:
                           "peak_kind": kind, "unit": "GB/s", "frac": bgbs / peak,
                           "bytes_per_step_per_gpu": wbytes + kvb // nst},
              "same_stream_as_batch1": bool((btoks[:16, 0] == np.array(toks[:16])).all())}
-    if rank == 0:
-        print(json.dumps({
-            "metric": "Llama-2-13B int4 decode tok/s (batch 1, tensor-parallel)", "value": steps / (ms * 1e-3),
-            "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "s4 weights x s8 activation digits (int32 tensor-core dot), fp32 accumulate",
-            "data": "synthetic",
-            "config": {"workload": f"llama2-13b-shape W4A16 greedy decode, batch 1, {TP_TOKENS}-token workload",
-                       "dim": dim, "hidden": hid, "layers": L, "vocab": vocab, "seed": SEED_13B,
-                       "parallelism": f"tp{world}"},
-            "roofline": {"kernel": "k_decode<W4A16> (persistent decode, in-kernel NVLink exchange)", "bound": "hbm",
-                         "achieved": gbs, "peak": peak, "peak_kind": kind, "unit": "GB/s",
-                         "frac": gbs / peak, "bytes_per_token_per_gpu": wbytes},
-            "gpu_launches": 1, "clocks": clk,
-            "token_stream_head": toks[:16], "batch16": batch}), flush=True)
     model.close()
-    if pg:
-        pg.destroy_process_group()
+    if rank != 0:
+        return None
+    return {
+        "metric": "Llama-2-13B int4 decode tok/s (batch 1, tensor-parallel)", "value": steps / (ms * 1e-3),
+        "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup, "ms_per_step": ms / steps,
+        "higher_is_better": True, "scaling": "strong",
+        "dtype": "s4 weights x s8 activation digits (int32 tensor-core dot), fp32 accumulate",
+        "config": {"workload": f"llama2-13b-shape W4A16 greedy decode, batch 1, {TP_TOKENS}-token workload",
+                   "dim": dim, "hidden": hid, "layers": L, "vocab": vocab, "seed": SEED_13B,
+                   "parallelism": f"tp{world}"},
+        "roofline": {"kernel": "k_decode<W4A16> (persistent decode, in-kernel NVLink exchange)", "bound": "hbm",
+                     "achieved": gbs, "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                     "frac": gbs / peak, "bytes_per_token_per_gpu": wbytes},
+        "gpu_launches": 1, "clocks": clk,
+        "token_stream_head": toks[:16], "batch16": batch}
 
 
 def w4a8_leg(path: Path, device: int, steps: int, warmup: int, cpu: bool) -> dict:
@@ -602,6 +602,7 @@ def main() -> None:
     ap.add_argument("--no-matvec", action="store_true", help="skip the isolated matvec shapes")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-prefill leg")
     ap.add_argument("--no-w4a8", action="store_true", help="skip the W4A8 decode leg")
+    ap.add_argument("--no-tp13b", action="store_true", help="skip the 13B tensor-parallel leg")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="seconds of timed reference decode")
     ap.add_argument("--tp13b", action="store_true", help="13B shape, tensor-parallel over the launch's ranks")
     ap.add_argument("--batch", type=int, default=0, help="7B lock-step batched decode of this many sequences")
@@ -640,7 +641,13 @@ def main() -> None:
         return float(t.item())
 
     if args.tp13b:
-        run_tp13b(args, world, rank, local, pg, barrier, max_over_ranks)
+        res = tp13b_leg(args, world, rank, local, pg, barrier, max_over_ranks)
+        if rank == 0:
+            res["data"] = "synthetic"
+            res["vs_baseline"] = None
+            print(json.dumps(res), flush=True)
+        if pg:
+            pg.destroy_process_group()
         return
 
     if args.batch > 0:
@@ -768,6 +775,13 @@ def main() -> None:
         model.close()
         w4a8 = w4a8_leg(path, local, args.steps, args.warmup, cpu=not args.no_cpu)
 
+    # 13B tensor parallelism over every rank of this launch (TP = N).
+    tp13b = None
+    if not args.no_tp13b and args.profile_layers <= 0:
+        model.close()
+        barrier()
+        tp13b = tp13b_leg(args, world, rank, local, pg, barrier, max_over_ranks)
+
     if rank == 0:
         line = {
             "metric": "Llama-2-7B int4 decode tok/s (batch 1)",
@@ -785,6 +799,7 @@ def main() -> None:
             "parity": parity,
             "prefill": prefill,
             "w4a8": w4a8,
+            "tp13b": tp13b,
         }
         print(json.dumps(line), flush=True)
     model.close()

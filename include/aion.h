@@ -59,7 +59,10 @@ typedef struct aion_opts {
     int32_t tp_rank;    /* this rank, 0 <= tp_rank < tp_size                           */
     const void* nccl_id;/* reserved (the ranks exchange IPC handles, see aion_tp_*)    */
     int32_t use_graph;  /* 1 (default): replay one CUDA graph per decode step          */
-    int32_t reserved[7];
+    int32_t wait_ms;    /* bound of each wait on another GPU inside the decode kernels,
+                           in milliseconds (0: 2000).  A wait that runs out makes the
+                           call return AION_ERR_TIMEOUT; aion_reset clears it.        */
+    int32_t reserved[6];
 } aion_opts;
 
 typedef struct aion_ctx aion_ctx;

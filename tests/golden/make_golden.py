@@ -151,7 +151,7 @@ def main() -> None:
         # The reference engine is process-global: run the 7B model in a child.
         code = ("import sys, json; sys.path.insert(0, %r); sys.path.insert(0, %r);"
                 "from tests.golden.make_golden import model_fixture; from oracle.oracle import Reference;"
-                "print(json.dumps(model_fixture(Reference(), %r, 64, 32, %d, cli=False)))"
+                "print(json.dumps(model_fixture(Reference(), %r, 64, 64, %d, cli=False)))"
                 % (str(ROOT), str(ROOT / "tests"), str(p7), args.threads))
         r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
         b7.update(json.loads(r.stdout.strip().splitlines()[-1]))
