@@ -53,7 +53,7 @@ struct MatDesc {
     const uint8_t* w;
     long long tile_bytes;          // G * gbytes
     int n, G, nch;                 // columns, groups per row, chunks per tile
-    int cg, cr;                    // chunk c spans cg groups, one more for c < cr
+    int cg, cr, gq;                // chunk c spans gq * cg groups, gq more for c < cr
     int ntiles, d;                 // tiles, logical rows
     int gbytes;                    // bytes per (tile, group): kGB (int4) or kGBF (fp32)
 };
@@ -66,21 +66,25 @@ __host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, i
     m.gbytes = gbytes;
     m.tile_bytes = (long long)m.G * gbytes;
     // fp32 groups are 6.4x larger: about two per copy, so two ring slots per
-    // warp still fit next to an 11008-wide fp32 input.
+    // warp still fit next to an 11008-wide fp32 input.  int4 chunks are cut
+    // in whole quads of groups where G allows it (the group dot takes four
+    // groups per step, so no step of a chunk is padded).
     const int target = gbytes == kGB ? kTargetChunk : 2 * gbytes;
+    m.gq = (gbytes == kGB && m.G % 4 == 0) ? 4 : 1;
+    const int Q = m.G / m.gq;
     m.nch = (int)((m.tile_bytes + target - 1) / target);
     if (m.nch < 1) m.nch = 1;
-    if (m.nch > m.G) m.nch = m.G;
-    m.cg = m.G / m.nch;
-    m.cr = m.G % m.nch;
+    if (m.nch > Q) m.nch = Q;
+    m.cg = Q / m.nch;
+    m.cr = Q % m.nch;
     m.ntiles = (int)((rows + kTR - 1) / kTR);
     m.d = (int)rows;
     return m;
 }
 
 __host__ __device__ inline long long desc_bytes(const MatDesc& m) { return m.tile_bytes * m.ntiles; }
-__host__ __device__ inline int chunk_g0(const MatDesc& m, int c) { return c * m.cg + (c < m.cr ? c : m.cr); }
-__host__ __device__ inline int max_chunk_bytes(const MatDesc& m) { return (m.cg + (m.cr ? 1 : 0)) * m.gbytes; }
+__host__ __device__ inline int chunk_g0(const MatDesc& m, int c) { return m.gq * (c * m.cg + (c < m.cr ? c : m.cr)); }
+__host__ __device__ inline int max_chunk_bytes(const MatDesc& m) { return m.gq * (m.cg + (m.cr ? 1 : 0)) * m.gbytes; }
 
 // ---------------------------------------------------------------------------
 // Activation digits in shared memory: group g at g*128: digit column p
