@@ -646,10 +646,14 @@ struct DecodeEpi {
 // a single chunk the warp writes att[h] directly, otherwise it writes a
 // partial and the last warp to finish a head merges the partials in chunk
 // order.  Unit u runs on CTA u mod G, warp u div G, so short contexts put one
-// unit on each SM.  A unit makes two dependent trips to memory: q with all
-// of its K rows (4 lanes per position, a quarter of the head each, 8
-// positions per pass), then all of its V rows (4 consecutive elements of the
-// head per lane).
+// unit on each SM.  q and the unit's K rows are loaded into registers (4
+// lanes per position, a quarter of the head each, 8 positions per pass); its
+// V rows (4 consecutive elements of the head per lane) go by asynchronous
+// copies into the warp's slice of the idle activation-digit buffer, issued
+// with the K loads, so the unit makes one trip to memory (a warp whose slice
+// does not fit loads V after the scores instead).  Lane p of the warp takes
+// position p's score, scaling and exponential; the sum of the exponentials
+// and the weighted V sum run over the positions in order, in every lane.
 // Partial layout per (head, chunk): [max, sum, -, -, o[0..hs)].
 // ---------------------------------------------------------------------------
 constexpr int kAttnUnit = 16;
@@ -663,13 +667,17 @@ struct AttnPart {
     float4 o;
 };
 
-__device__ __forceinline__ AttnPart attn_unit(const DecodeArgs& a, const float* kc, const float* vc, int h, int t0, int n) {
+__device__ __forceinline__ AttnPart attn_unit(const DecodeArgs& a, const float* kc, const float* vc, int h, int t0, int n,
+                                              float4* vstage) {
     const int hs = a.head_size, lane = threadIdx.x & 31;
     const int hq = hs / 4, sub = lane & 3, pg = lane >> 2;
     const int kvh = h / a.kv_mul;
     const float rs = sqrtf((float)hs);
     const bool vl = 4 * lane < hs;
     const float4 z4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const float* vr = vc + (size_t)t0 * a.kv_dim + kvh * hs + 4 * lane;
+    if (vstage && vl)
+        for (int p = 0; p < n; p++) cp_async16(vstage + p * 32 + lane, vr + (size_t)p * a.kv_dim);
     const float* qp = a.q + h * hs + sub * hq;
     const float* kr0 = kc + (size_t)(t0 + pg) * a.kv_dim + kvh * hs + sub * hq;
     const float* kr1 = kr0 + (size_t)8 * a.kv_dim;
@@ -697,36 +705,36 @@ __device__ __forceinline__ AttnPart attn_unit(const DecodeArgs& a, const float* 
     d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
     d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
     d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
-    float sc[kAttnUnit];
+    // Lane p (and p + 16) takes position p: quad p % 8 holds its dot, in d0
+    // for p < 8, in d1 above.
+    const int pl = lane & 15;
+    const float s0 = __shfl_sync(0xffffffffu, d0, (pl & 7) * 4), s1 = __shfl_sync(0xffffffffu, d1, (pl & 7) * 4);
+    const float sc = pl < n ? __fdiv_rn(pl < 8 ? s0 : s1, rs) : -INFINITY;
+    float m = sc;
 #pragma unroll
-    for (int pp = 0; pp < 8; pp++) {
-        sc[pp] = __shfl_sync(0xffffffffu, d0, pp * 4);
-        sc[8 + pp] = __shfl_sync(0xffffffffu, d1, pp * 4);
-    }
-    const float* vr = vc + (size_t)t0 * a.kv_dim + kvh * hs + 4 * lane;
+    for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float e = pl < n ? expf(sc - m) : 0.0f;
     float4 vv[kAttnUnit];
+    if (vstage) {
+        cp_async_wait_all();
+        __syncwarp();
 #pragma unroll
-    for (int p = 0; p < kAttnUnit; p++)
-        vv[p] = (p < n && vl) ? __ldcg(reinterpret_cast<const float4*>(vr + (size_t)p * a.kv_dim)) : z4;
-    float m = -INFINITY;
+        for (int p = 0; p < kAttnUnit; p++) vv[p] = (p < n && vl) ? vstage[p * 32 + lane] : z4;
+    } else {
 #pragma unroll
-    for (int p = 0; p < kAttnUnit; p++) {
-        sc[p] = p < n ? __fdiv_rn(sc[p], rs) : -INFINITY;
-        m = fmaxf(m, sc[p]);
+        for (int p = 0; p < kAttnUnit; p++)
+            vv[p] = (p < n && vl) ? __ldcg(reinterpret_cast<const float4*>(vr + (size_t)p * a.kv_dim)) : z4;
     }
     float l = 0.0f;
-#pragma unroll
-    for (int p = 0; p < kAttnUnit; p++) {
-        sc[p] = p < n ? expf(sc[p] - m) : 0.0f;
-        l += sc[p];
-    }
     float4 o = z4;
 #pragma unroll
     for (int p = 0; p < kAttnUnit; p++) {
-        o.x = fmaf(sc[p], vv[p].x, o.x);
-        o.y = fmaf(sc[p], vv[p].y, o.y);
-        o.z = fmaf(sc[p], vv[p].z, o.z);
-        o.w = fmaf(sc[p], vv[p].w, o.w);
+        const float w = __shfl_sync(0xffffffffu, e, p);
+        l += w;
+        o.x = fmaf(w, vv[p].x, o.x);
+        o.y = fmaf(w, vv[p].y, o.y);
+        o.z = fmaf(w, vv[p].z, o.z);
+        o.w = fmaf(w, vv[p].w, o.w);
     }
     return AttnPart{m, l, o};
 }
@@ -791,8 +799,13 @@ __device__ __forceinline__ void prefetch_kv_l2(const DecodeArgs& a, int layer, i
 // (unit u on CTA u mod G, warp u div G).  With a single chunk the warp
 // writes att[h] directly; otherwise it writes a partial and the last warp
 // of a head (atomic count) merges the partials in chunk order.
-__device__ void attention_layer(const DecodeArgs& a, int layer, int pos) {
+// `stage`: the activation-digit buffer (stage_bytes), idle between the QKV
+// op and the WO op's input build; warp w stages V in bytes
+// [w, w + 1) * kAttnUnit * 512 of it when they fit.
+__device__ void attention_layer(const DecodeArgs& a, int layer, int pos, unsigned char* stage, int stage_bytes) {
     const int hs = a.head_size, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kStage = kAttnUnit * 32 * 16;   // bytes of V per warp
+    float4* vstage = (warp + 1) * kStage <= stage_bytes ? reinterpret_cast<float4*>(stage + warp * kStage) : nullptr;
     const int nch = pos / kAttnUnit + 1;
     const size_t lkv = (size_t)layer * a.max_pos * a.kv_dim;
     const float* kc = a.kcache + lkv;
@@ -804,7 +817,7 @@ __device__ void attention_layer(const DecodeArgs& a, int layer, int pos) {
     for (int u = warp * gridDim.x + blockIdx.x; u < units; u += nw) {
         const int h = u / nch, k = u - (u / nch) * nch;
         const int t0 = k * kAttnUnit, n = min(kAttnUnit, pos + 1 - t0);
-        const AttnPart p = attn_unit(a, kc, vc, h, t0, n);
+        const AttnPart p = attn_unit(a, kc, vc, h, t0, n, vstage);
         if (nch == 1) {
             const float inv = 1.0f / p.l;
             if (vl) __stcg(reinterpret_cast<float4*>(a.att + h * hs + 4 * lane),
@@ -1169,7 +1182,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
                 if (MODE == MODE_W4A8)
                     attention_layer_exact(a, op.layer, pos, reinterpret_cast<float*>(xf), red);
                 else
-                    attention_layer(a, op.layer, pos);
+                    attention_layer(a, op.layer, pos, xf, a.ops_off);
                 PHASE_T(step, oi, 5);
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
                 PHASE_T(step, oi, 6);

@@ -270,6 +270,29 @@ def bf16_peak() -> tuple[float, str]:
     return 1400.0, "fallback (sustained)"
 
 
+def prefill_parity(model) -> dict | None:
+    """The short-prefix case of this leg against the reference (committed
+    fixture from the reference engine, tests/golden/7b.json "prefill_short"):
+    the first tokens of sequences 0 and 1 of the prefill workload through
+    model.prefill, then lock-step greedy steps; the last-position logits at
+    the fixture's probe indices within 1e-3 of max |logit|, and every
+    token identical.  Runs after the timed regions."""
+    fx = json.loads((ROOT / "tests" / "golden" / "7b.json").read_text()).get("prefill_short")
+    if not fx:
+        return None
+    seqs, n, extra = fx["sequences"], fx["prompt_tokens"], fx["extra_steps"]
+    logits = model.prefill(np.array([q["prompt"] for q in seqs], np.int32))
+    first = np.argmax(logits, axis=1).astype(np.int32)
+    toks, _ = model.decode_batch(first, np.full(len(seqs), n, np.int32), extra)
+    idx = np.array(fx["probe_index"])
+    err = max(float(np.abs(logits[i][idx] - np.array(q["probe"], np.float32)).max() / q["max_abs"])
+              for i, q in enumerate(seqs))
+    return {"case": f"{len(seqs)} sequences x {n} prompt tokens of the workload, then {extra} greedy steps",
+            "tokens_compared": (extra + 1) * len(seqs),
+            "identical": all(toks[:, i].tolist() == q["tokens"] for i, q in enumerate(seqs)),
+            "logit_rel_err_max": err, "logit_rel_tol": 1e-3}
+
+
 def prefill_leg(model, layers: int, stream, device: int) -> dict:
     """32 x 512 prefill then 128 decode steps per sequence, timed with CUDA
     events on the model's stream."""
@@ -315,7 +338,8 @@ def prefill_leg(model, layers: int, stream, device: int) -> dict:
                                 "achieved": dgbs, "peak": hpeak, "peak_kind": hkind, "unit": "GB/s",
                                 "frac": dgbs / hpeak, "weight_bytes_per_step": wb,
                                 "kv_bytes_per_step_avg": kvb / PREFILL_DECODE},
-            "decode_stream_head": toks_out[:8, 0].tolist()}
+            "decode_stream_head": toks_out[:8, 0].tolist(),
+            "parity": prefill_parity(model) if layers == CFG_7B[2] else None}
 
 
 def kv_step_bytes(layers: int, kv_dim: int, positions) -> int:

@@ -102,6 +102,38 @@ def kat_fixture(ref: Reference) -> dict:
     return kat
 
 
+# Short-prefix prefill case of bench.py's prefill leg: the first PROMPT_TOK
+# tokens of its sequences 0 and 1 (uniform random tokens, seed 2), then
+# PREFILL_EXTRA greedy steps.  The reference runs them as forced decode
+# steps (transformer() at positions 0.. of one KV cache per sequence).
+PREFILL_SEED, PREFILL_SEQ, PREFILL_TOK, PROMPT_TOK, PREFILL_EXTRA = 2, 32, 512, 8, 3
+N_PROBE = 64
+
+
+def prefill_fixture(ref: Reference, path: Path, threads: int) -> dict:
+    ref.open(path, threads=threads, scalar=True)
+    vocab = ref.vocab
+    prompts = np.random.default_rng(PREFILL_SEED).integers(0, vocab, (PREFILL_SEQ, PREFILL_TOK)).astype(np.int32)
+    probe = np.random.default_rng(7).choice(vocab, N_PROBE, replace=False)
+    logits = lambda: np.ctypeslib.as_array(ref.L.ref_logits(), (vocab,)).copy()  # noqa: E731
+    out = {"prompt_tokens": PROMPT_TOK, "extra_steps": PREFILL_EXTRA, "seed": PREFILL_SEED,
+           "probe_index": [int(i) for i in probe], "sequences": []}
+    for s in range(2):
+        p = prompts[s, :PROMPT_TOK]
+        for pos, t in enumerate(p):
+            ref.L.ref_forward(int(t), pos)
+        lg = logits()
+        srt = np.sort(lg)
+        toks = [int(np.argmax(lg))]
+        for i in range(PREFILL_EXTRA):
+            ref.L.ref_forward(toks[-1], PROMPT_TOK + i)
+            toks.append(int(np.argmax(logits())))
+        out["sequences"].append({"prompt": p.tolist(), "tokens": toks, "logits_sha": cases.sha(lg),
+                                 "max_abs": float(np.abs(lg).max()), "gap": float(srt[-1] - srt[-2]),
+                                 "probe": [float(lg[i]) for i in probe]})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--7b", dest="b7", action="store_true", help="also the 7B stream (needs ~5 GB disk, minutes)")
@@ -109,11 +141,28 @@ def main() -> None:
     ap.add_argument("--tmp", default=tempfile.gettempdir())
     ap.add_argument("--f32-only", action="store_true", help="only add the fp32-path keys to tiny.json")
     ap.add_argument("--f32-child", default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--7b-prefill", dest="b7_prefill", action="store_true",
+                    help="only (re)write the short-prefix prefill case of 7b.json")
     args = ap.parse_args()
     ref = Reference()
     tmp = Path(args.tmp)
     if args.f32_child:
         print(json.dumps(f32_fixture(ref, Path(args.f32_child), 256)))
+        return
+    if args.b7_prefill:
+        p7 = tmp / "aion_7b_int4.bin"
+        if not p7.exists():
+            A.synth_checkpoint(p7, cases.LLAMA7B, cases.SEEDS["7b"], int4=True)
+        b7 = json.loads((OUT / "7b.json").read_text())
+        assert file_sha(p7) == b7["int4_sha"]
+        code = ("import sys, json; sys.path.insert(0, %r); sys.path.insert(0, %r);"
+                "from tests.golden.make_golden import prefill_fixture; from oracle.oracle import Reference;"
+                "print(json.dumps(prefill_fixture(Reference(), %r, %d)))"
+                % (str(ROOT), str(ROOT / "tests"), str(p7), args.threads))
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, check=True)
+        b7["prefill_short"] = json.loads(r.stdout.strip().splitlines()[-1])
+        (OUT / "7b.json").write_text(json.dumps(b7))
+        print("7b.json prefill_short written; gaps", [q["gap"] for q in b7["prefill_short"]["sequences"]])
         return
     f32 = tmp / "aion_tiny_f32.bin"
     if args.f32_only:

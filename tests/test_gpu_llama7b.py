@@ -10,7 +10,10 @@ are pinned to the reference's by their hashes in the fixture), W4A8 step-0
 logits bit-identical.  The batched prefill at the 7B shapes (K = 4096 and
 11008, causal attention over 32 positions) gives the oracle's last-position
 logits within 1e-3 and, continued greedily from the caches it wrote, the
-oracle's next 8 tokens.
+oracle's next 8 tokens.  The short prefix of the bench's prefill workload
+(two 8-token prompts) gives the reference's last-position logits at 64 probe
+indices within 1e-3 of max |logit| and its next 3 greedy tokens, through
+the lock-step batched decode.
 """
 from __future__ import annotations
 
@@ -85,3 +88,18 @@ def test_7b_prefill_matches_oracle(ckpt7b, oracle):
             m.set_sequence(s)
             m.decode_async(extra, int(np.argmax(logits[s])), n_tok)
             assert m.tokens(n_tok + extra)[n_tok:] == cont
+
+
+def test_7b_prefill_short_prefix_matches_reference(ckpt7b, golden_7b):
+    import aion_b200 as A
+    fx = golden_7b["prefill_short"]
+    seqs, n, extra = fx["sequences"], fx["prompt_tokens"], fx["extra_steps"]
+    idx = np.array(fx["probe_index"])
+    with A.Model(ckpt7b, max_batch=len(seqs), max_pos=n + extra + 1) as m:
+        logits = m.prefill(np.array([q["prompt"] for q in seqs], np.int32))
+        first = np.argmax(logits, axis=1).astype(np.int32)
+        toks, _ = m.decode_batch(first, np.full(len(seqs), n, np.int32), extra)
+    for i, q in enumerate(seqs):
+        err = float(np.abs(logits[i][idx] - np.array(q["probe"], np.float32)).max() / q["max_abs"])
+        assert err <= REL, (i, err)
+        assert toks[:, i].tolist() == q["tokens"], i
