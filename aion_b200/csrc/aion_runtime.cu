@@ -128,6 +128,43 @@ static SmemPlan plan_smem(int max_n, int max_chunk_bytes, int smem_optin, int st
     return p;
 }
 
+// Chunk count of a matrix streamed by the decode / matvec kernels in split
+// mode: among the cuts into nch0 .. 3 nch0 chunks per tile whose largest
+// chunk is no larger than the default cut's (the ring slot), the one whose
+// busiest warp of any CTA has the least work under the kernels' own split,
+// counting a chunk as kChunkCost groups more than its groups (its ring round
+// trip and bookkeeping).  Ties keep fewer chunks.  With 7B shapes on 148
+// SMs: QKV 7 -> 8, WO 7 -> 11, W2 18 -> 19, classifier 7 -> 8, W13 stays 7.
+constexpr int kChunkCost = 4;
+
+static void tune_chunks(MatDesc& m, int mode, int grid) {
+    if (grid <= 0 || !op_work_at(m, mode, 0, grid).split) return;   // whole tiles: the cut does not split the work
+    const int nch0 = m.nch, max_bytes = max_chunk_bytes(m);
+    int best = nch0;
+    long long best_cost = -1;
+    for (int nch = nch0; nch <= 3 * nch0; nch++) {
+        MatDesc t = m;
+        set_chunks(t, nch);
+        if (t.nch != nch || max_chunk_bytes(t) > max_bytes) continue;
+        long long worst = 0;
+        for (int c = 0; c < grid; c++) {
+            const OpWork w = op_work_at(t, mode, c, grid);
+            for (int k = 0; k < kWarps; k++) {
+                OpCursor cu;
+                long long cost = 0;
+                for (bool more = cursor_begin(cu, w, t, k); more; more = cursor_next(cu, w, t))
+                    cost += chunk_g0(t, cu.c + 1) - chunk_g0(t, cu.c) + kChunkCost;
+                worst = std::max(worst, cost);
+            }
+        }
+        if (best_cost < 0 || worst < best_cost) {
+            best_cost = worst;
+            best = nch;
+        }
+    }
+    set_chunks(m, best);
+}
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
                              bool coop, Args&&... args) {
@@ -788,6 +825,8 @@ static aion_status load_impl(aion_ctx* c, const char* path) {
         c->emb.w = arena_take(c, desc_bytes(c->emb));
         // Classifier rows of this rank: tiles [vocab_off / 16, ...) of the embedding.
         c->cls = make_desc(c->emb.w + (size_t)(c->vocab_off / kTR) * c->emb.tile_bytes, c->vocab_l, (int)dim, gb);
+        // The decode kernel's grid is one CTA per SM (setup_decode_kernel).
+        for (MatDesc* d : {&dq, &dwo, &d13, &d2, &c->cls}) tune_chunks(*d, c->mode, dev_info(c->dev).sms);
         c->qkv.assign(L, dq); c->wo.assign(L, dwo); c->w13.assign(L, d13); c->w2.assign(L, d2);
         for (long long l = 0; l < L; l++) {
             c->qkv[l].w = arena_take(c, desc_bytes(dq));
@@ -1399,6 +1438,7 @@ extern "C" AION_API aion_status aion_qmatrix_upload(const float* scales, const u
     *out = nullptr;
     CK_RET(nullptr, cudaSetDevice(device));
     MatDesc m = make_desc(nullptr, rows, (int)cols);
+    tune_chunks(m, MODE_W4A16, dev_info(device).sms);
     uint8_t* w = nullptr;
     cudaError_t e = cudaMalloc(&w, (size_t)desc_bytes(m));
     if (e != cudaSuccess) {

@@ -58,6 +58,15 @@ struct MatDesc {
     int gbytes;                    // bytes per (tile, group): kGB (int4) or kGBF (fp32)
 };
 
+// Cuts every tile into nch chunks of whole granules (gq groups); the tile
+// layout in memory does not depend on it.
+__host__ __device__ inline void set_chunks(MatDesc& m, int nch) {
+    const int Q = m.G / m.gq;
+    m.nch = nch < 1 ? 1 : nch > Q ? Q : nch;
+    m.cg = Q / m.nch;
+    m.cr = Q % m.nch;
+}
+
 __host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, int n, int gbytes = kGB) {
     MatDesc m;
     m.w = w;
@@ -71,14 +80,9 @@ __host__ __device__ inline MatDesc make_desc(const uint8_t* w, long long rows, i
     // groups per step, so no step of a chunk is padded).
     const int target = gbytes == kGB ? kTargetChunk : 2 * gbytes;
     m.gq = (gbytes == kGB && m.G % 4 == 0) ? 4 : 1;
-    const int Q = m.G / m.gq;
-    m.nch = (int)((m.tile_bytes + target - 1) / target);
-    if (m.nch < 1) m.nch = 1;
-    if (m.nch > Q) m.nch = Q;
-    m.cg = Q / m.nch;
-    m.cr = Q % m.nch;
     m.ntiles = (int)((rows + kTR - 1) / kTR);
     m.d = (int)rows;
+    set_chunks(m, (int)((m.tile_bytes + target - 1) / target));
     return m;
 }
 
@@ -385,7 +389,7 @@ struct OpCursor {
     int a, tile, c;
 };
 
-__device__ __forceinline__ bool cursor_begin(OpCursor& cu, const OpWork& w, const MatDesc& m, int warp) {
+__host__ __device__ inline bool cursor_begin(OpCursor& cu, const OpWork& w, const MatDesc& m, int warp) {
     cu.a = w.u0 + warp;
     if (w.split) {
         cu.tile = cu.a / m.nch;
@@ -396,7 +400,7 @@ __device__ __forceinline__ bool cursor_begin(OpCursor& cu, const OpWork& w, cons
     }
     return cu.a < w.u1;
 }
-__device__ __forceinline__ bool cursor_next(OpCursor& cu, const OpWork& w, const MatDesc& m) {
+__host__ __device__ inline bool cursor_next(OpCursor& cu, const OpWork& w, const MatDesc& m) {
     if (w.split) {
         cu.a += kWarps;
         cu.c += kWarps;
