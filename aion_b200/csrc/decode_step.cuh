@@ -458,52 +458,55 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
         cp_async_wait_all();
         if (csync_or(!ok)) return false;
         PHASE_T(pstep, pop, 2);
-        // Last local tile cut by the CTA boundary (this CTA has its first
-        // part): warp 1's lanes 0..15 fetch the partner's tagged part now,
-        // so the load's latency overlaps the reduction below.
-        const bool cutw = cut1 && tid >= 32 && tid < 32 + kTR;
-        const uint64_t* cut_src = split_part + (size_t)tl * kTR + (tid - 32);
-        uint64_t cut_word = cutw ? ld_relaxed_u64(cut_src) : 0ull;
-        for (int i = tid; i < ntl * kTR; i += kThreads) {
-            const int lt = i / kTR, r = i % kTR;
-            float v = 0.0f;
-            for (int k = 0; k < kWarps; k++) v += os.part[(lt * kWarps + k) * kTR + r];
-            os.vals[i] = v;
-        }
-        csync();
-        for (int i = tid; i < ntl * kWarps * kTR; i += kThreads) os.part[i] = 0.0f;
         PHASE_T(pstep, pop, 7);
-        // Tiles cut by a CTA boundary: local tile 0 when u0 is inside a tile
-        // (this CTA has the tile's second part, published above as soon as
-        // its warps left the tile), the last local tile when u1 is (this CTA
-        // has the first part).  The CTA with the first part waits for the
-        // flag, adds first + second, lowers the flag and finishes the tile.
-        // Publishing never waits, so the waits always end.
-        if (cutw) {
-            // The partner published its part as soon as its first tile was
-            // done; wait (bounded) only if the fetched word is not yet this
-            // op's, then add first + second in that order.
-            uint32_t spins = 0;
-            while (tag_ep(cut_word) != tag) {
-                if (++spins > (1u << 22)) break;
-                cut_word = ld_relaxed_u64(cut_src);
-            }
-            if (tag_ep(cut_word) == tag) {
-                const int k = (ntl - 1) * kTR + tid - 32;
-                os.vals[k] = os.vals[k] + tag_val(cut_word);
-            } else {
-                os.state[0] = 1;
-            }
-        }
-        if (cut1 && csync_or(os.state[0] != 0)) return false;
-        if (tid == 0) os.state[0] = os.state[1] = 0;
-        PHASE_T(pstep, pop, 8);
-        const bool skip0 = cut0;
+        // The CTA's tiles are finished by quads of rows, one quad a thread:
+        // the thread sums the warps' partials of its rows in warp order
+        // (clearing them for the next op as it reads them), adds the
+        // partner's part when the CTA boundary cuts the tile, and runs the
+        // epilogue.  Tiles cut by a CTA boundary: local tile 0 when u0 is
+        // inside a tile (this CTA has the tile's second part, published as
+        // soon as its warps left the tile; the partner finishes the tile),
+        // the last local tile when u1 is (this CTA has the first part: it
+        // waits, bounded, for the partner's tagged words and adds first +
+        // second in that order).  Publishing never waits, so the waits end.
+        bool bad = false;
         for (int i = tid; i < ntl * (kTR / kRB); i += kThreads) {
             const int lt = i / (kTR / kRB), q = i % (kTR / kRB);
-            if (lt == 0 && skip0) continue;
-            epi((tf + lt) * kTR + q * kRB, os.vals + lt * kTR + q * kRB);
+            float* p = os.part + lt * kWarps * kTR + q * kRB;
+            if (lt == 0 && cut0) {
+                for (int k = 0; k < kWarps; k++)
+#pragma unroll
+                    for (int r = 0; r < kRB; r++) p[k * kTR + r] = 0.0f;
+                continue;
+            }
+            const bool cutq = cut1 && lt == ntl - 1;
+            const uint64_t* cut_src = split_part + (size_t)tl * kTR + q * kRB;
+            uint64_t w[kRB];
+#pragma unroll
+            for (int r = 0; r < kRB; r++) w[r] = cutq ? ld_relaxed_u64(cut_src + r) : 0ull;   // early: overlaps the sums
+            float v[kRB];
+#pragma unroll
+            for (int r = 0; r < kRB; r++) v[r] = 0.0f;
+            for (int k = 0; k < kWarps; k++)
+#pragma unroll
+                for (int r = 0; r < kRB; r++) {
+                    v[r] += p[k * kTR + r];
+                    p[k * kTR + r] = 0.0f;
+                }
+            if (cutq) {
+#pragma unroll
+                for (int r = 0; r < kRB; r++) {
+                    uint32_t spins = 0;
+                    while (tag_ep(w[r]) != tag && ++spins <= (1u << 22)) w[r] = ld_relaxed_u64(cut_src + r);
+                    if (tag_ep(w[r]) == tag) v[r] = v[r] + tag_val(w[r]);
+                    else bad = true;
+                }
+            }
+            epi((tf + lt) * kTR + q * kRB, v);
         }
+        if (cut1 && csync_or(bad)) return false;
+        if (tid == 0) os.state[0] = os.state[1] = 0;
+        PHASE_T(pstep, pop, 8);
     } else {
         float a0 = 0.0f, a1 = 0.0f;
         float* stage = os.part + warp * kTR;
