@@ -1036,8 +1036,10 @@ extern "C" AION_API aion_status aion_load(const char* path, const aion_opts* opt
         delete c;
         return AION_ERR_ARG;
     }
-    if (c->opts.tp_size < 1 || c->opts.tp_size > 64 || c->opts.tp_rank < 0 || c->opts.tp_rank >= c->opts.tp_size) {
-        set_err(&c->err, "tp_size %d / tp_rank %d out of range", c->opts.tp_size, c->opts.tp_rank);
+    if (c->opts.tp_size < 1 || c->opts.tp_size > kMaxTpRanks || c->opts.tp_rank < 0 ||
+        c->opts.tp_rank >= c->opts.tp_size) {
+        set_err(&c->err, "tp_size %d / tp_rank %d out of range (1 <= tp_size <= %d: the GPUs of one NVLink node)",
+                c->opts.tp_size, c->opts.tp_rank, kMaxTpRanks);
         delete c;
         return AION_ERR_ARG;
     }

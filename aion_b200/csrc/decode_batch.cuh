@@ -385,14 +385,19 @@ __device__ bool btp_sum4(const BatchArgs& a, float4& d, int b, int row4, uint32_
     const uint64_t* own = reinterpret_cast<const uint64_t*>(a.tp_peers[a.tp_rank] + a.tp_brecv_off);
     float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     for (int j = 0; j < a.tp_n; j++) {
+        // the rank's four words are loaded together, then only the untagged
+        // ones polled again
         const uint64_t* p = own + ((slot + j) * nbm + b) * dim + row4;
+        uint64_t t[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) t[k] = ld_relaxed_sys_u64(p + k);
+#pragma unroll
         for (int k = 0; k < 4; k++) {
-            uint64_t t = ld_relaxed_sys_u64(p + k);
-            for (uint32_t i = 0; tag_ep(t) != count; i++) {
+            for (uint32_t i = 0; tag_ep(t[k]) != count; i++) {
                 if (i > (1u << 22)) return false;
-                t = ld_relaxed_sys_u64(p + k);
+                t[k] = ld_relaxed_sys_u64(p + k);
             }
-            sum[k] += tag_val(t);
+            sum[k] += tag_val(t[k]);
         }
     }
     d = make_float4(sum[0], sum[1], sum[2], sum[3]);

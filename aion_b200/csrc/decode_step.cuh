@@ -959,26 +959,31 @@ __device__ bool tp_exchange(const DecodeArgs& a, uint32_t& nbar, uint32_t count)
 
 // x[row] += sum over ranks j (in rank order) of their partial rows, each
 // read once its tag shows exchange `count` (bounded wait); rows are spread
-// over all threads of the grid.  False if a wait gave up.
+// over all threads of the grid.  A thread issues the loads of all ranks'
+// words of its row at once and re-polls only those not yet tagged, so the
+// waits overlap instead of following one another.  False if a wait gave up.
+constexpr int kMaxTpRanks = 8;
 __device__ bool tp_reduce_residual(const DecodeArgs& a, uint32_t count) {
     const uint64_t* recv =
         reinterpret_cast<const uint64_t*>(a.tp_peers[a.tp_rank]) + (size_t)(count & 1u) * a.tp_n * a.dim;
     bool ok = true;
     const unsigned long long t0 = global_timer();
     for (int row = blockIdx.x * kThreads + threadIdx.x; row < a.dim && ok; row += gridDim.x * kThreads) {
+        uint64_t t[kMaxTpRanks];
+#pragma unroll
+        for (int j = 0; j < kMaxTpRanks; j++)
+            t[j] = j < a.tp_n ? ld_relaxed_sys_u64(recv + (size_t)j * a.dim + row) : ((uint64_t)count << 32);
+        const float xr = __ldcg(a.x + row);
         float sum = 0.0f;
-        for (int j = 0; j < a.tp_n && ok; j++) {
-            uint64_t t = ld_relaxed_sys_u64(recv + (size_t)j * a.dim + row);
-            for (uint32_t i = 0; tag_ep(t) != count; i++) {
-                if ((i & 63u) == 63u && global_timer() - t0 > a.wait_ns) {
-                    ok = false;
-                    break;
-                }
-                t = ld_relaxed_sys_u64(recv + (size_t)j * a.dim + row);
+#pragma unroll
+        for (int j = 0; j < kMaxTpRanks; j++) {
+            for (uint32_t i = 0; ok && tag_ep(t[j]) != count; i++) {
+                if ((i & 63u) == 63u && global_timer() - t0 > a.wait_ns) ok = false;
+                else t[j] = ld_relaxed_sys_u64(recv + (size_t)j * a.dim + row);
             }
-            sum += tag_val(t);
+            if (j < a.tp_n) sum += tag_val(t[j]);
         }
-        __stcg(a.x + row, __ldcg(a.x + row) + sum);
+        __stcg(a.x + row, xr + sum);
     }
     if (!ok) set_error(a.step, DEV_BARRIER_TIMEOUT);
     return ok;

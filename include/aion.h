@@ -55,7 +55,8 @@ typedef struct aion_opts {
     int32_t max_batch;  /* sequences (KV caches) held, for aion_prefill and
                            aion_decode_batch (default 1)                            */
     int32_t max_pos;    /* KV positions allocated (0 = header seq_len; <= seq_len)     */
-    int32_t tp_size;    /* tensor-parallel ranks, one process per GPU (default 1)      */
+    int32_t tp_size;    /* tensor-parallel ranks, one process per GPU of one node
+                           (1 <= tp_size <= 8; default 1)                          */
     int32_t tp_rank;    /* this rank, 0 <= tp_rank < tp_size                           */
     const void* nccl_id;/* reserved (the ranks exchange IPC handles, see aion_tp_*)    */
     int32_t use_graph;  /* 1 (default): replay one CUDA graph per decode step          */
