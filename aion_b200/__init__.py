@@ -101,6 +101,7 @@ def lib() -> ctypes.CDLL:
         "aion_matvec_w4a8": (I32, [VP, VP, VP, VP]),
         "aion_matvec_w4a16_static": (I32, [VP, VP, VP, VP]),
         "aion_matvec_status": (I32, [VP, VP]),
+        "aion_matvec_inject_timeout": (I32, [VP]),
         "aion_gemm_bf16_tn": (I32, [VP, VP, VP, I64, I64, I64, VP]),
         "aion_prefill": (I32, [VP, VP, I32, I32, VP]),
         "aion_decode_batch": (I32, [VP, I32, I32, VP, VP, VP, VP]),

@@ -1650,6 +1650,17 @@ extern "C" AION_API aion_status aion_matvec_status(const aion_qmatrix* w, void* 
     return st;
 }
 
+extern "C" AION_API aion_status aion_matvec_inject_timeout(const aion_qmatrix* w) {
+    if (!w) {
+        set_err(nullptr, "aion_matvec_inject_timeout: null matrix");
+        return AION_ERR_ARG;
+    }
+    CK_RET(nullptr, cudaSetDevice(w->device));
+    const int code = DEV_COPY_TIMEOUT;
+    CK_RET(nullptr, cudaMemcpy(w->sc.error, &code, sizeof(int), cudaMemcpyHostToDevice));
+    return AION_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Sampling beyond greedy (no counterpart in the reference, whose loop takes
 // the argmax): the decode kernels draw each next token on the device.

@@ -344,10 +344,12 @@ __device__ __forceinline__ void seq_issue_next(Seq& s, Ring& r, const OpDesc* op
 // `epi(first_row, values[4])`.  Returns false if a wait gave up.
 // ---------------------------------------------------------------------------
 struct OpSmem {
+    uint64_t cutw[kTR];                          // split: the partner's tagged words of the last cut tile, fetched early
     float part[kMaxLocalTiles * kWarps * kTR];   // split: warp partials per local tile
     float vals[kMaxLocalTiles * kTR];            // split: finished rows per local tile
     float pre[kMaxLocalTiles * kTR];             // split: epilogue operands fetched ahead
     int state[2];
+    int done;                                    // split: warps that have left the op's loop
 };
 
 // Split mode, a CTA whose range starts inside tile tf (it holds the
@@ -378,7 +380,7 @@ __device__ __forceinline__ void publish_cut_tile(OpSmem& os, int n0, int tf, uin
 // first op; run_op calls it on its way out).
 __device__ __forceinline__ void reset_opsmem(OpSmem& os) {
     for (int i = threadIdx.x; i < kMaxLocalTiles * kWarps * kTR; i += kThreads) os.part[i] = 0.0f;
-    if (threadIdx.x == 0) os.state[0] = os.state[1] = 0;
+    if (threadIdx.x == 0) os.state[0] = os.state[1] = os.done = 0;
 }
 
 template <int MODE, bool PROD, class Epi>
@@ -455,6 +457,16 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             }
             if (cut0 && cur == tf) publish_cut_tile(os, n0, tf, split_part, tag);
         }
+        if (ok && cut1) {
+            // The first warp out of the loop fetches the partner's tagged
+            // words of the last tile (published once the partner's warps
+            // left that tile, long before) while the other warps compute,
+            // so the epilogue seldom waits for them.
+            int first = 0;
+            if (lane == 0) first = atomicAdd(&os.done, 1) == 0;
+            first = __shfl_sync(0xffffffffu, first, 0);
+            if (first && lane < kTR) os.cutw[lane] = ld_relaxed_u64(split_part + (size_t)tl * kTR + lane);
+        }
         cp_async_wait_all();
         if (csync_or(!ok)) return false;
         PHASE_T(pstep, pop, 2);
@@ -483,7 +495,12 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             const uint64_t* cut_src = split_part + (size_t)tl * kTR + q * kRB;
             uint64_t w[kRB];
 #pragma unroll
-            for (int r = 0; r < kRB; r++) w[r] = cutq ? ld_relaxed_u64(cut_src + r) : 0ull;   // early: overlaps the sums
+            for (int r = 0; r < kRB; r++) {
+                // fetched as the first warp left the loop; if it was not this
+                // op's yet, fetch again now, so the load overlaps the sums
+                w[r] = cutq ? os.cutw[q * kRB + r] : 0ull;
+                if (cutq && tag_ep(w[r]) != tag) w[r] = ld_relaxed_u64(cut_src + r);
+            }
             float v[kRB];
 #pragma unroll
             for (int r = 0; r < kRB; r++) v[r] = 0.0f;
@@ -505,7 +522,7 @@ __device__ bool run_op(const MatDesc& m, Ring& ring, unsigned char* ring_base, S
             epi((tf + lt) * kTR + q * kRB, v);
         }
         if (cut1 && csync_or(bad)) return false;
-        if (tid == 0) os.state[0] = os.state[1] = 0;
+        if (tid == 0) os.state[0] = os.state[1] = os.done = 0;
         PHASE_T(pstep, pop, 8);
     } else {
         float a0 = 0.0f, a1 = 0.0f;

@@ -288,6 +288,18 @@ AION_API aion_status aion_matvec_w4a16_static(const aion_qmatrix* w, const float
  * calls of the static variant do. */
 AION_API aion_status aion_matvec_status(const aion_qmatrix* w, void* stream);
 
+/* Diagnostic, for tests of the failure path: records in w's scratch the
+ * same error a matvec on w records when one of its bounded waits gives up,
+ * so that the next aion_matvec_status reports AION_ERR_TIMEOUT (and clears
+ * it) without any wait being made to run out on the GPU. */
+AION_API aion_status aion_matvec_inject_timeout(const aion_qmatrix* w);
+
+/* Device resets: the static variant keeps its array's device address for
+ * the life of the process, and matrices and contexts hold device memory, so
+ * a cudaDeviceReset (or a recreated primary context) invalidates them; the
+ * library does not support it while any of its objects or the static
+ * variant is in use on that device. */
+
 /* Dense GEMM on the tensor cores: C[m][n] (fp32) = A[m][k] * B[n][k]^T with
  * A and B bf16 (K contiguous), all device memory, on the current device.
  * The building block of the batched prefill, where B holds int4 weights

@@ -136,3 +136,50 @@ def test_matvec_on_a_side_stream(cuda, oracle, mats):
     s.synchronize()
     ref = oracle.matvec_w4a16(x, scales, packed, n, d)
     assert np.abs(y.cpu().numpy() - ref).max() <= 2e-5 * np.abs(ref).max()
+
+
+def test_matvec_on_the_second_device(cuda, mats):
+    """The kernel-level matvec sets its shared-memory opt-in per device: a
+    call on device 1 after calls on device 0 gives device 0's result."""
+    import aion_b200 as A
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    d, n = 11008, 4096
+    seed, packed, scales = mats[(d, n)]
+    x = cases.vector(n, seed)
+    out = []
+    for dev in (0, 1, 0, 1):
+        with torch.cuda.device(dev):
+            q = A.QMatrix(scales, packed, d, n, device=dev)
+            xt = torch.from_numpy(x).to(f"cuda:{dev}")
+            y = torch.full((d,), float("nan"), device=f"cuda:{dev}")
+            q.matvec_w4a16(xt, y)
+            q.status()
+            out.append(y.cpu().numpy())
+            q.free()
+    for y in out[1:]:
+        assert (y.view(np.uint32) == out[0].view(np.uint32)).all()
+
+
+def test_matvec_status_reports_a_timeout(cuda, mats):
+    """A matvec whose bounded wait gave up leaves its error word set;
+    aion_matvec_status reports it once (AION_ERR_TIMEOUT, y invalid) and
+    clears it.  The error is recorded from the host, not provoked on the GPU."""
+    import aion_b200 as A
+    torch = cuda
+    L = A.lib()
+    d, n = 4096, 4096
+    seed, packed, scales = mats[(d, n)]
+    q = A.QMatrix(scales, packed, d, n)
+    xt = torch.from_numpy(cases.vector(n, seed)).cuda()
+    y = torch.empty(d, device="cuda")
+    q.matvec_w4a16(xt, y)
+    assert L.aion_matvec_status(q._h, None) == 0
+    assert L.aion_matvec_inject_timeout(q._h) == 0
+    assert L.aion_matvec_status(q._h, None) == 7          # AION_ERR_TIMEOUT
+    assert b"gave up" in L.aion_last_error(None)
+    assert L.aion_matvec_status(q._h, None) == 0          # cleared
+    q.matvec_w4a16(xt, y)                                 # the matrix stays usable
+    assert L.aion_matvec_status(q._h, None) == 0
+    q.free()
