@@ -822,7 +822,12 @@ __device__ __forceinline__ void prefetch_kv_l2(const DecodeArgs& a, int layer, i
 // `stage`: the activation-digit buffer (stage_bytes), idle between the QKV
 // op and the WO op's input build; warp w stages V in bytes
 // [w, w + 1) * kAttnUnit * 512 of it when they fit.
-__device__ void attention_layer(const DecodeArgs& a, int layer, int pos, unsigned char* stage, int stage_bytes) {
+// `scratch`: zeroed shared memory (the op's warp partials, idle between
+// ops) of scratch_floats; a head with 2..kWarps units runs them on warps
+// 0..nch-1 of one CTA and merges their partials there, in chunk order, with
+// no global round trips; the slots are zeroed again afterwards.
+__device__ void attention_layer(const DecodeArgs& a, int layer, int pos, unsigned char* stage, int stage_bytes,
+                                float* scratch, int scratch_floats) {
     const int hs = a.head_size, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kStage = kAttnUnit * 32 * 16;   // bytes of V per warp
     float4* vstage = (warp + 1) * kStage <= stage_bytes ? reinterpret_cast<float4*>(stage + warp * kStage) : nullptr;
@@ -832,6 +837,28 @@ __device__ void attention_layer(const DecodeArgs& a, int layer, int pos, unsigne
     const float* vc = a.vcache + lkv;
     const int pstride = hs + 4;
     const bool vl = 4 * lane < hs;
+    if (nch >= 2 && nch <= kWarps && nch * pstride <= scratch_floats) {
+        for (int h = blockIdx.x; h < a.n_heads; h += gridDim.x) {   // uniform in the CTA
+            if (warp < nch) {
+                const int t0 = warp * kAttnUnit, n = min(kAttnUnit, pos + 1 - t0);
+                const AttnPart p = attn_unit(a, kc, vc, h, t0, n, vstage);
+                float* sp = scratch + warp * pstride;
+                if (vl) *reinterpret_cast<float4*>(sp + 4 + 4 * lane) = p.o;
+                if (lane == 0) {
+                    sp[0] = p.m;
+                    sp[1] = p.l;
+                }
+            }
+            csync();
+            if (warp == 0) {
+                attn_merge(a, h, scratch, nch, pstride, [](const float* x) { return *x; });
+                __syncwarp();
+                for (int i = lane; i < nch * pstride; i += 32) scratch[i] = 0.0f;
+            }
+            csync();
+        }
+        return;
+    }
     const int units = a.n_heads * nch;
     const int nw = gridDim.x * kWarps;
     for (int u = warp * gridDim.x + blockIdx.x; u < units; u += nw) {
@@ -1207,7 +1234,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode(DecodeArgs a) {
                 if (MODE == MODE_W4A8)
                     attention_layer_exact(a, op.layer, pos, reinterpret_cast<float*>(xf), red);
                 else
-                    attention_layer(a, op.layer, pos, xf, a.ops_off);
+                    attention_layer(a, op.layer, pos, xf, a.ops_off, os.part, kMaxLocalTiles * kWarps * kTR);
                 PHASE_T(step, oi, 5);
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
                 PHASE_T(step, oi, 6);
