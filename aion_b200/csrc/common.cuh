@@ -309,6 +309,21 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     float t = (lane < kComputeThreads / 32) ? red[lane] : 0.0f;
     return warp_sum(t);
 }
+// Sum of s and max of m over the compute threads in one exchange (red
+// holds at least 16 + kComputeThreads / 32 floats).
+__device__ __forceinline__ float2 block_sum_max(float s, float m, float* red) {
+    s = warp_sum(s);
+    m = warp_max(m);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    csync();
+    if (lane == 0) {
+        red[warp] = s;
+        red[16 + warp] = m;
+    }
+    csync();
+    const bool in = lane < kComputeThreads / 32;
+    return make_float2(warp_sum(in ? red[lane] : 0.0f), warp_max(in ? red[16 + lane] : -INFINITY));
+}
 __device__ __forceinline__ float block_max(float v, float* red) {
     v = warp_max(v);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

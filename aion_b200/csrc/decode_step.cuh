@@ -175,6 +175,7 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
     const int tid = threadIdx.x;
     const int nv = n / 4;
     float4 v[NV], w[NORM ? NV : 1];
+    float norm_max = 0.0f;   // W4A16 with RMSNorm: max |input| from the fused reduction
 #pragma unroll
     for (int i = 0; i < NV; i++) {
         const int j = tid + i * kThreads;
@@ -204,6 +205,21 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
             const float sum = __fadd_rn(__fadd_rn(red[0], red[1]), __fadd_rn(red[2], red[3]));
             ss = 1.0f / sqrtf(__fdiv_rn(sum, (float)n) + 1e-5f);
             csync();
+        } else if (MODE == MODE_W4A16) {
+            // The sum of squares and max |x w| in one CTA exchange; max
+            // |(x ss) w| is then max |x w| * ss to within two roundings, so
+            // the exponent below is the exact one or one off, either way
+            // with max |X| inside the four digits' range.
+            float acc = 0.0f, mw = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV; i++) {
+                acc += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+                mw = fmaxf(mw, fmaxf(fmaxf(fabsf(__fmul_rn(v[i].x, w[i].x)), fabsf(__fmul_rn(v[i].y, w[i].y))),
+                                     fmaxf(fabsf(__fmul_rn(v[i].z, w[i].z)), fabsf(__fmul_rn(v[i].w, w[i].w)))));
+            }
+            const float2 r = block_sum_max(acc, mw, red);
+            ss = 1.0f / sqrtf(__fdiv_rn(r.x, (float)n) + 1e-5f);
+            norm_max = __fmul_rn(r.y, ss);
         } else {
             float acc = 0.0f;
 #pragma unroll
@@ -235,10 +251,14 @@ __device__ __forceinline__ void build_digits(unsigned char* xf, float* xs, const
     float sa = 0.0f, sb = 0.0f;
     if (MODE == MODE_W4A16) {
         float mx = 0.0f;
+        if (NORM) {
+            mx = norm_max;
+        } else {
 #pragma unroll
-        for (int i = 0; i < NV; i++)
-            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
-        mx = block_max(mx, red);
+            for (int i = 0; i < NV; i++)
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+            mx = block_max(mx, red);
+        }
         const int ebits = (int)((__float_as_uint(mx) >> 23) & 0xFF);
         live = ebits >= 34;
         E = 156 - ebits;                                   // M * 2^E in [2^29, 2^30)
