@@ -366,7 +366,6 @@ __device__ __forceinline__ void seq_issue_next(Seq& s, Ring& r, const OpDesc* op
 struct OpSmem {
     uint64_t cutw[kTR];                          // split: the partner's tagged words of the last cut tile, fetched early
     float part[kMaxLocalTiles * kWarps * kTR];   // split: warp partials per local tile
-    float vals[kMaxLocalTiles * kTR];            // split: finished rows per local tile
     float pre[kMaxLocalTiles * kTR];             // split: epilogue operands fetched ahead
     int state[2];
     int done;                                    // split: warps that have left the op's loop
