@@ -1759,6 +1759,10 @@ static aion_status batch_plan(aion_ctx* c) {
     cudaFuncAttributes fa;
     CK_RET(&c->err, cudaFuncGetAttributes(&fa, k_decode_batch<NBLK>));
     const int digits = (int)align256(std::max((size_t)gs * NBLK * kBGroupBytes, (size_t)kBAttnScratch));
+    if ((size_t)grid * kBMaxSeq * sizeof(float) > (size_t)digits) {   // the norm factors' staging area
+        set_err(&c->err, "batched decode: %d CTAs' norm partial sums do not fit the digit buffer", grid);
+        return AION_ERR_SHAPE;
+    }
     const int opsb = (int)align256(ops.size() * sizeof(BOpDesc));
     const int avail = di.smem_optin - (int)fa.sharedSizeBytes - digits - opsb - 1024;
     const int P = std::min(8, avail / (kWarps * kBChunkBytes));

@@ -357,11 +357,17 @@ __device__ __forceinline__ float emb_elem(const MatDesc& emb, int tok, int i) {
 // RMSNorm factors of every sequence from the per-CTA sums of squares
 // (fixed reduction order): s_ss[b] = 1 / sqrtf(sum / dim + 1e-5)
 // (src/kernel_simd.c:793-813).
-__device__ void bnorm_factors(const BatchArgs& a, float* s_ss) {
+// The CTAs' partial sums ([grid][nb]) are staged into `scratch` (idle
+// shared memory, grid * nb floats) in one coalesced pass, so the per-sequence
+// sums below take no further L2 round trips; the order of the sums is fixed.
+__device__ void bnorm_factors(const BatchArgs& a, float* s_ss, float* scratch) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = (int)gridDim.x * a.nb;
+    for (int i = threadIdx.x; i < n; i += kThreads) scratch[i] = __ldcg(a.ssq + i);
+    csync();
     for (int b = warp; b < a.nb; b += kWarps) {
         float v = 0.0f;
-        for (int c = lane; c < (int)gridDim.x; c += 32) v += __ldcg(a.ssq + (size_t)c * a.nb + b);
+        for (int c = lane; c < (int)gridDim.x; c += 32) v += scratch[c * a.nb + b];
         v = warp_sum(v);
         if (lane == 0) s_ss[b] = 1.0f / sqrtf(__fdiv_rn(v, (float)a.dim) + 1e-5f);
     }
@@ -715,12 +721,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
             if (!(ok = matvec(op))) break;
             if (op.kind == OP_QKV) {
                 // q, k, v rows: RoPE on adjacent pairs (src/kernel_simd.c:1068-1085), KV append.
-                bnorm_factors(a, s_ss);
+                bnorm_factors(a, s_ss, reinterpret_cast<float*>(xd));   // the slice's digits are used up
                 const int nq = (a.q_dim + 2 * a.kv_dim) / 4, h2 = a.head_size / 2;
-                for (int i = blockIdx.x * kThreads + tid; i < a.nb * nq; i += gridDim.x * kThreads) {
+                const int nitems = a.nb * nq, gstride = gridDim.x * kThreads;
+                auto rope_kv = [&](int i, float4 v) {
                     const int b = i / nq, row = 4 * (i - b * nq);
                     const float ss = s_ss[b];
-                    float4 v = bsum4(a.part, S, T, NB8, b, row);
                     v = make_float4(__fmul_rn(v.x, ss), __fmul_rn(v.y, ss), __fmul_rn(v.z, ss), __fmul_rn(v.w, ss));
                     const int pos = s_pos[b];
                     const size_t lkv = (size_t)b * a.kv_seq + (size_t)l * a.max_pos * a.kv_dim + (size_t)pos * a.kv_dim;
@@ -741,6 +747,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
                     } else {
                         __stcg(reinterpret_cast<float4*>(a.vcache + lkv + (row - a.q_dim - a.kv_dim)), v);
                     }
+                };
+                // Two items a pass: both items' partial sums are loaded before
+                // either's stores, so their L2 round trips overlap.
+                for (int i = blockIdx.x * kThreads + tid; i < nitems; i += 2 * gstride) {
+                    const int j = i + gstride;
+                    const int b0 = i / nq, b1 = j / nq;
+                    const float4 v0 = bsum4(a.part, S, T, NB8, b0, 4 * (i - b0 * nq));
+                    const float4 v1 = j < nitems ? bsum4(a.part, S, T, NB8, b1, 4 * (j - b1 * nq))
+                                                 : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    rope_kv(i, v0);
+                    if (j < nitems) rope_kv(j, v1);
                 }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
                 if (csync_or(!battention(a, l, s_pos, xd, s_abar, aphase))) {
@@ -765,7 +782,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
             } else if (op.kind == OP_W13) {
                 // rows w1[2j], w1[2j+1], w3[2j], w3[2j+1]; SwiGLU (src/kernel_simd.c:836-841),
                 // straight into the digits of W2's input.
-                bnorm_factors(a, s_ss);
+                bnorm_factors(a, s_ss, reinterpret_cast<float*>(xd));   // the slice's digits are used up
                 const int Gh = a.hidden / 32, total = Gh * NB8 * 8;
                 for (int base = 0; base < total; base += gridDim.x * kThreads) {
                     const int i = base + blockIdx.x * kThreads + tid;
@@ -790,7 +807,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) k_decode_batch(BatchArgs a)
                 }
                 if (!grid_barrier(a.step, nbar)) { ok = false; break; }
             } else {   // OP_CLS
-                bnorm_factors(a, s_ss);
+                bnorm_factors(a, s_ss, reinterpret_cast<float*>(xd));   // the slice's digits are used up
                 const int G = gridDim.x, c = blockIdx.x, V4 = a.vocab_rows / 4;
                 const int q0 = (int)((long long)c * V4 / G), q1 = (int)((long long)(c + 1) * V4 / G);
                 for (int b = warp; b < a.nb; b += kWarps) {

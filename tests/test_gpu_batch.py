@@ -89,9 +89,15 @@ def test_batch_rejects_bad_calls(cuda, tiny_path):
 
 
 def test_batch_7b_matches_reference_stream(ckpt7b, golden_7b):
+    """The first 64 tokens against the reference's stream; then 200 tokens
+    against the batch-1 path, so that each head's positions span several
+    rounds of the attention warps (8 positions x 11 warps a round) and each
+    CTA takes several (sequence, head) units."""
     import aion_b200 as A
     want = golden_7b["w4a16_tokens"][:64]
-    with A.Model(ckpt7b, max_batch=9, max_pos=128) as m:
-        toks, _ = m.decode_batch([1] * 9, [0] * 9, 63)
+    with A.Model(ckpt7b, max_batch=9, max_pos=256) as m:
+        toks, _ = m.decode_batch([1] * 9, [0] * 9, 199)
+        one, _ = m.generate(200)
     for b in range(9):
-        assert list(toks[:, b]) == want, b
+        assert list(toks[:64, b]) == want, b
+        assert list(toks[:200, b]) == one, b
