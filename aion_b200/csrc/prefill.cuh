@@ -153,14 +153,27 @@ __global__ void k_pf_rope_kv(PfRopeArgs a) {
     for (int i = threadIdx.x; i < a.kv_dim; i += blockDim.x) vc[i] = cr[a.dim + a.kv_dim + i];
 }
 
-// Causal attention of every (sequence, head) over its T positions, online
-// softmax, fp32 on the CUDA cores; the output goes straight into the A
-// operand of WO.  CTA = (query block of 32, head, sequence); warp w takes
-// queries 4w..4w+3 of the block; keys come in blocks of 32 through shared
-// memory (K rows padded by one float against bank conflicts).  Dynamic
-// shared memory: kPfAttnSmem bytes.
-constexpr int kPfQB = 32, kPfKB = 32;
-constexpr int kPfAttnSmem = (kPfQB * kMaxHead + kPfKB * (kMaxHead + 1) + kPfKB * kMaxHead) * 4;
+// Causal attention of every (sequence, head) over its T positions
+// (src/kernel_simd.c:1099-1117: scores q.k / sqrt(hs), softmax over
+// positions 0..t, weighted sum of V rows), on the tensor cores.  The output
+// goes straight into the A operand of WO.
+//
+// CTA = (query block of 64, head, sequence), longest blocks first; warp w
+// holds rows 16w..16w+15 of the block.  Keys come in blocks of 64: the CTA
+// converts the block's fp32 K rows to bf16 hi/lo parts in shared memory as
+// [key][d] and its V rows as [d][key], so both are B operands of
+// mma.sync.m16n8k16 read with 32-bit loads (row strides padded by 8
+// elements: the quad lanes of the 8 fragment rows hit 32 distinct banks).
+// Each product takes three MMAs, hi.hi + lo.hi + hi.lo, as in the prefill
+// GEMMs (lo.lo, about 2^-16 of a product, is left out): S = Q K^T with Q's
+// fragments held in registers, then an online softmax in fp32 on the S
+// fragments (rows g and g + 8 of a lane, the quad's four lanes reduced by
+// shuffles), then O += P V with P's fragments taken straight from S's
+// accumulator layout.
+constexpr int kPfTQ = 64, kPfTK = 64;
+constexpr int kPfKs = kMaxHead + 8;   // K row stride (bf16 elements)
+constexpr int kPfVs = kPfTK + 8;      // V^T row stride
+constexpr int kPfAttnSmem = 2 * (kPfTK * kPfKs + kMaxHead * kPfVs) * 2;
 struct PfAttnArgs {
     const float* q;                   // [mrows][dim]
     const float *kcache, *vcache;     // sequence 0, layer l
@@ -169,77 +182,197 @@ struct PfAttnArgs {
     int kp;
     __nv_bfloat16* out;               // [mpad][3*kp]
 };
-__global__ void __launch_bounds__(256) k_pf_attention(PfAttnArgs a) {
-    extern __shared__ float pf_smem[];
-    float(*sq)[kMaxHead] = reinterpret_cast<float(*)[kMaxHead]>(pf_smem);
-    float(*sk)[kMaxHead + 1] = reinterpret_cast<float(*)[kMaxHead + 1]>(pf_smem + kPfQB * kMaxHead);
-    float(*sv)[kMaxHead] = reinterpret_cast<float(*)[kMaxHead]>(pf_smem + kPfQB * kMaxHead + kPfKB * (kMaxHead + 1));
-    const int qb = blockIdx.x, h = blockIdx.y, s = blockIdx.z;
-    const int hs = a.hs, kvh = h / a.kv_mul;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t_first = qb * kPfQB, t_last = min(a.T, t_first + kPfQB) - 1;
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// (x, y) as packed bf16 pairs: hi = bf16(v), lo = bf16(v - hi); x in the low half.
+__device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+__global__ void __launch_bounds__(128, 2) k_pf_attention(PfAttnArgs a) {
+    constexpr int NK = kMaxHead / 16, ND = kMaxHead / 8, NT = kPfTK / 8;
+    extern __shared__ __align__(16) unsigned char pf_smem[];
+    __nv_bfloat16* kh = reinterpret_cast<__nv_bfloat16*>(pf_smem);   // [key][kPfKs]
+    __nv_bfloat16* kl = kh + kPfTK * kPfKs;
+    __nv_bfloat16* vh = kl + kPfTK * kPfKs;                          // [d][kPfVs]
+    __nv_bfloat16* vl = vh + kMaxHead * kPfVs;
+    const int nqb = (a.T + kPfTQ - 1) / kPfTQ;
+    const int qb = nqb - 1 - (int)blockIdx.x, h = blockIdx.y, s = blockIdx.z;
+    const int hs = a.hs, nk = hs / 16, nd = hs / 8, h4 = hs / 4, kvh = h / a.kv_mul;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int q0 = qb * kPfTQ;
+    const int r0 = q0 + 16 * warp + g, r1 = r0 + 8;   // this lane's rows (positions)
+    const int t_last = min(a.T, q0 + kPfTQ) - 1;      // the last key any row of the CTA sees
     const float* kc = a.kcache + s * a.seq_stride + (size_t)kvh * hs;
     const float* vc = a.vcache + s * a.seq_stride + (size_t)kvh * hs;
-    for (int i = threadIdx.x; i < kPfQB * hs; i += blockDim.x) {
-        const int r = i / hs, d = i % hs, t = t_first + r;
-        sq[r][d] = t < a.T ? a.q[((size_t)s * a.T + t) * a.dim + h * hs + d] : 0.0f;
+    const float2 z2 = make_float2(0.0f, 0.0f);
+
+    uint32_t qh[NK][4], ql[NK][4];
+    {
+        const float* q0p = a.q + ((size_t)s * a.T + min(r0, a.T - 1)) * a.dim + h * hs;
+        const float* q1p = a.q + ((size_t)s * a.T + min(r1, a.T - 1)) * a.dim + h * hs;
+#pragma unroll
+        for (int kk = 0; kk < NK; kk++) {
+            if (kk < nk) {
+                const int c = 16 * kk + 2 * t;
+                const float2 x0 = r0 < a.T ? *reinterpret_cast<const float2*>(q0p + c) : z2;
+                const float2 x1 = r1 < a.T ? *reinterpret_cast<const float2*>(q1p + c) : z2;
+                const float2 x2 = r0 < a.T ? *reinterpret_cast<const float2*>(q0p + c + 8) : z2;
+                const float2 x3 = r1 < a.T ? *reinterpret_cast<const float2*>(q1p + c + 8) : z2;
+                split2(x0.x, x0.y, qh[kk][0], ql[kk][0]);
+                split2(x1.x, x1.y, qh[kk][1], ql[kk][1]);
+                split2(x2.x, x2.y, qh[kk][2], ql[kk][2]);
+                split2(x3.x, x3.y, qh[kk][3], ql[kk][3]);
+            }
+        }
     }
     const float rs = sqrtf((float)hs);
-    float mx[4], l[4], acc[4][4];
+    float o[ND][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        mx[i] = -INFINITY;
-        l[i] = 0.0f;
+    for (int n = 0; n < ND; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;   // l: this lane's share of the row sums
+
+    for (int k0 = 0; k0 <= t_last; k0 += kPfTK) {
+        __syncthreads();   // the previous block's fragments are read
+        for (int i = threadIdx.x; i < kPfTK * h4; i += blockDim.x) {
+            const int key = i / h4, d = 4 * (i - key * h4);
+            const float4 v = k0 + key <= t_last ? __ldg(reinterpret_cast<const float4*>(kc + (size_t)(k0 + key) * a.kv_dim + d))
+                                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            uint32_t h01, l01, h23, l23;
+            split2(v.x, v.y, h01, l01);
+            split2(v.z, v.w, h23, l23);
+            *reinterpret_cast<uint2*>(kh + key * kPfKs + d) = make_uint2(h01, h23);
+            *reinterpret_cast<uint2*>(kl + key * kPfKs + d) = make_uint2(l01, l23);
+        }
+        for (int i = threadIdx.x; i < (kPfTK / 2) * h4; i += blockDim.x) {
+            const int kp = i / h4, d = 4 * (i - kp * h4), key = k0 + 2 * kp;
+            const float4 va = key <= t_last ? __ldg(reinterpret_cast<const float4*>(vc + (size_t)key * a.kv_dim + d))
+                                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float4 vb = key + 1 <= t_last
+                                  ? __ldg(reinterpret_cast<const float4*>(vc + (size_t)(key + 1) * a.kv_dim + d))
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            const float ea[4] = {va.x, va.y, va.z, va.w}, eb[4] = {vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
-    }
-    for (int k0 = 0; k0 <= t_last; k0 += kPfKB) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < kPfKB * hs; i += blockDim.x) {
-            const int r = i / hs, d = i % hs, t = k0 + r;
-            sk[r][d] = t <= t_last ? kc[(size_t)t * a.kv_dim + d] : 0.0f;
-            sv[r][d] = t <= t_last ? vc[(size_t)t * a.kv_dim + d] : 0.0f;
+            for (int e = 0; e < 4; e++) {
+                uint32_t hi, lo;
+                split2(ea[e], eb[e], hi, lo);
+                *reinterpret_cast<uint32_t*>(vh + (d + e) * kPfVs + 2 * kp) = hi;
+                *reinterpret_cast<uint32_t*>(vl + (d + e) * kPfVs + 2 * kp) = lo;
+            }
         }
         __syncthreads();
+
+        // S = Q K^T: 16 rows x 64 keys per warp.
+        float sc[NT][4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int r = 4 * warp + i, t = t_first + r;
-            if (t > t_last) continue;                       // uniform per warp
-            const int key = k0 + lane;
-            float sc = -INFINITY;
-            if (key <= t) {
-                float d = 0.0f;
-                for (int j = 0; j < hs; j++) d = fmaf(sq[r][j], sk[lane][j], d);
-                sc = d / rs;
-            }
-            const float bm = warp_max(sc);
-            const float mnew = fmaxf(mx[i], bm);
-            const float p = key <= t ? expf(sc - mnew) : 0.0f;
-            const float corr = expf(mx[i] - mnew);
-            l[i] = l[i] * corr + warp_sum(p);
+        for (int n = 0; n < NT; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 4; j++) acc[i][j] *= corr;
-            for (int kk = 0; kk < kPfKB; kk++) {
-                const float pk = __shfl_sync(0xffffffffu, p, kk);   // every lane takes part
+        for (int kk = 0; kk < NK; kk++) {
+            if (kk < nk) {
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int d = lane + 32 * j;
-                    if (d < hs) acc[i][j] = fmaf(pk, sv[kk][d], acc[i][j]);
+                for (int n = 0; n < NT; n++) {
+                    const int off = (n * 8 + g) * kPfKs + 16 * kk + 2 * t;
+                    const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(kh + off);
+                    const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(kh + off + 8);
+                    const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(kl + off);
+                    const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(kl + off + 8);
+                    mma_bf16(sc[n], qh[kk], bh0, bh1);
+                    mma_bf16(sc[n], ql[kk], bh0, bh1);
+                    mma_bf16(sc[n], qh[kk], bl0, bl1);
                 }
             }
-            mx[i] = mnew;
+        }
+        // Online softmax: scale, causal mask, block max per row.
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int key = k0 + n * 8 + 2 * t + e;
+                sc[n][e] = key <= r0 ? __fdiv_rn(sc[n][e], rs) : -INFINITY;
+                sc[n][2 + e] = key <= r1 ? __fdiv_rn(sc[n][2 + e], rs) : -INFINITY;
+                mx0 = fmaxf(mx0, sc[n][e]);
+                mx1 = fmaxf(mx1, sc[n][2 + e]);
+            }
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        // Key k0 <= every row of the CTA, so the block maxima are finite.
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float c0 = expf(m0 - mn0), c1 = expf(m1 - mn1);
+        l0 *= c0;
+        l1 *= c1;
+#pragma unroll
+        for (int n = 0; n < ND; n++) {
+            o[n][0] *= c0;
+            o[n][1] *= c0;
+            o[n][2] *= c1;
+            o[n][3] *= c1;
+        }
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                sc[n][e] = expf(sc[n][e] - mn0);
+                sc[n][2 + e] = expf(sc[n][2 + e] - mn1);
+                l0 += sc[n][e];
+                l1 += sc[n][2 + e];
+            }
+        }
+        m0 = mn0;
+        m1 = mn1;
+        // O += P V, P's 16 x 16 fragments from the accumulators of S tiles 2j, 2j + 1.
+#pragma unroll
+        for (int j = 0; j < kPfTK / 16; j++) {
+            uint32_t ph[4], pl[4];
+            split2(sc[2 * j][0], sc[2 * j][1], ph[0], pl[0]);
+            split2(sc[2 * j][2], sc[2 * j][3], ph[1], pl[1]);
+            split2(sc[2 * j + 1][0], sc[2 * j + 1][1], ph[2], pl[2]);
+            split2(sc[2 * j + 1][2], sc[2 * j + 1][3], ph[3], pl[3]);
+#pragma unroll
+            for (int n = 0; n < ND; n++) {
+                if (n < nd) {
+                    const int off = (n * 8 + g) * kPfVs + 16 * j + 2 * t;
+                    const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(vh + off);
+                    const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(vh + off + 8);
+                    const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(vl + off);
+                    const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(vl + off + 8);
+                    mma_bf16(o[n], ph, bh0, bh1);
+                    mma_bf16(o[n], pl, bh0, bh1);
+                    mma_bf16(o[n], ph, bl0, bl1);
+                }
+            }
         }
     }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int r = 4 * warp + i, t = t_first + r;
-        if (t > t_last) continue;
-        __nv_bfloat16* row = a.out + ((size_t)s * a.T + t) * 3 * a.kp;
-        const float inv = 1.0f / l[i];
+    for (int half = 0; half < 2; half++) {
+        const int r = half ? r1 : r0;
+        if (r >= a.T) continue;
+        const float inv = half ? inv1 : inv0;
+        __nv_bfloat16* row = a.out + ((size_t)s * a.T + r) * 3 * a.kp;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int d = lane + 32 * j;
-            if (d < hs) split_store(row, a.kp, h * hs + d, acc[i][j] * inv);
+        for (int n = 0; n < ND; n++) {
+            if (n < nd) {
+                const int col = h * hs + n * 8 + 2 * t;
+                uint32_t hi, lo;
+                split2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv, hi, lo);
+                *reinterpret_cast<uint32_t*>(row + col) = hi;
+                *reinterpret_cast<uint32_t*>(row + a.kp + col) = lo;
+                *reinterpret_cast<uint32_t*>(row + 2 * a.kp + col) = hi;
+            }
         }
     }
 }
