@@ -195,6 +195,11 @@ __device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t&
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
+// 32-bit word of V^T row d holding keys 2 kp, 2 kp + 1.  The XOR of the
+// pair index with bits 3..5 of d spreads a warp's stores (32 rows d, one
+// kp) over 32 banks; a fragment read (rows 8n + g, pairs 8j + t) sees one
+// XOR constant, so its 32 lanes still hit 4g + (pair ^ c): 32 banks.
+__device__ __forceinline__ int vt_word(int d, int kp) { return d * (kPfVs / 2) + (kp ^ ((d >> 3) & 7)); }
 __global__ void __launch_bounds__(128, 2) k_pf_attention(PfAttnArgs a) {
     constexpr int NK = kMaxHead / 16, ND = kMaxHead / 8, NT = kPfTK / 8;
     extern __shared__ __align__(16) unsigned char pf_smem[];
@@ -240,30 +245,54 @@ __global__ void __launch_bounds__(128, 2) k_pf_attention(PfAttnArgs a) {
 
     for (int k0 = 0; k0 <= t_last; k0 += kPfTK) {
         __syncthreads();   // the previous block's fragments are read
-        for (int i = threadIdx.x; i < kPfTK * h4; i += blockDim.x) {
-            const int key = i / h4, d = 4 * (i - key * h4);
-            const float4 v = k0 + key <= t_last ? __ldg(reinterpret_cast<const float4*>(kc + (size_t)(k0 + key) * a.kv_dim + d))
-                                                : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            uint32_t h01, l01, h23, l23;
-            split2(v.x, v.y, h01, l01);
-            split2(v.z, v.w, h23, l23);
-            *reinterpret_cast<uint2*>(kh + key * kPfKs + d) = make_uint2(h01, h23);
-            *reinterpret_cast<uint2*>(kl + key * kPfKs + d) = make_uint2(l01, l23);
-        }
-        for (int i = threadIdx.x; i < (kPfTK / 2) * h4; i += blockDim.x) {
-            const int kp = i / h4, d = 4 * (i - kp * h4), key = k0 + 2 * kp;
-            const float4 va = key <= t_last ? __ldg(reinterpret_cast<const float4*>(vc + (size_t)key * a.kv_dim + d))
-                                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            const float4 vb = key + 1 <= t_last
-                                  ? __ldg(reinterpret_cast<const float4*>(vc + (size_t)(key + 1) * a.kv_dim + d))
-                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            const float ea[4] = {va.x, va.y, va.z, va.w}, eb[4] = {vb.x, vb.y, vb.z, vb.w};
+        // K rows: four float4 loads in flight per thread before their stores.
+        constexpr int U = 4;
+        for (int i0 = threadIdx.x; i0 < kPfTK * h4; i0 += U * blockDim.x) {
+            float4 v[U];
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                uint32_t hi, lo;
-                split2(ea[e], eb[e], hi, lo);
-                *reinterpret_cast<uint32_t*>(vh + (d + e) * kPfVs + 2 * kp) = hi;
-                *reinterpret_cast<uint32_t*>(vl + (d + e) * kPfVs + 2 * kp) = lo;
+            for (int u = 0; u < U; u++) {
+                const int i = i0 + u * blockDim.x, key = i / h4, d = 4 * (i - key * h4);
+                v[u] = (i < kPfTK * h4 && k0 + key <= t_last)
+                           ? __ldg(reinterpret_cast<const float4*>(kc + (size_t)(k0 + key) * a.kv_dim + d))
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = i0 + u * blockDim.x, key = i / h4, d = 4 * (i - key * h4);
+                if (i < kPfTK * h4) {
+                    uint32_t h01, l01, h23, l23;
+                    split2(v[u].x, v[u].y, h01, l01);
+                    split2(v[u].z, v[u].w, h23, l23);
+                    *reinterpret_cast<uint2*>(kh + key * kPfKs + d) = make_uint2(h01, h23);
+                    *reinterpret_cast<uint2*>(kl + key * kPfKs + d) = make_uint2(l01, l23);
+                }
+            }
+        }
+        // V rows, transposed: thread (key pair kp, columns d, d + 1) writes
+        // word kp ^ ((d >> 3) & 7) of rows d and d + 1 (see vt_word).
+        const int h2 = hs / 2;
+        for (int i0 = threadIdx.x; i0 < (kPfTK / 2) * h2; i0 += U * blockDim.x) {
+            float2 va[U], vb[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = i0 + u * blockDim.x, kp = i / h2, d = 2 * (i - kp * h2), key = k0 + 2 * kp;
+                const bool in = i < (kPfTK / 2) * h2;
+                va[u] = in && key <= t_last ? __ldg(reinterpret_cast<const float2*>(vc + (size_t)key * a.kv_dim + d)) : z2;
+                vb[u] = in && key + 1 <= t_last ? __ldg(reinterpret_cast<const float2*>(vc + (size_t)(key + 1) * a.kv_dim + d))
+                                                : z2;
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = i0 + u * blockDim.x, kp = i / h2, d = 2 * (i - kp * h2);
+                if (i < (kPfTK / 2) * h2) {
+                    uint32_t hi, lo;
+                    split2(va[u].x, vb[u].x, hi, lo);
+                    reinterpret_cast<uint32_t*>(vh)[vt_word(d, kp)] = hi;
+                    reinterpret_cast<uint32_t*>(vl)[vt_word(d, kp)] = lo;
+                    split2(va[u].y, vb[u].y, hi, lo);
+                    reinterpret_cast<uint32_t*>(vh)[vt_word(d + 1, kp)] = hi;
+                    reinterpret_cast<uint32_t*>(vl)[vt_word(d + 1, kp)] = lo;
+                }
             }
         }
         __syncthreads();
@@ -340,11 +369,11 @@ __global__ void __launch_bounds__(128, 2) k_pf_attention(PfAttnArgs a) {
 #pragma unroll
             for (int n = 0; n < ND; n++) {
                 if (n < nd) {
-                    const int off = (n * 8 + g) * kPfVs + 16 * j + 2 * t;
-                    const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(vh + off);
-                    const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(vh + off + 8);
-                    const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(vl + off);
-                    const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(vl + off + 8);
+                    const int w0 = vt_word(n * 8 + g, 8 * j + t), w1 = vt_word(n * 8 + g, 8 * j + 4 + t);
+                    const uint32_t bh0 = reinterpret_cast<const uint32_t*>(vh)[w0];
+                    const uint32_t bh1 = reinterpret_cast<const uint32_t*>(vh)[w1];
+                    const uint32_t bl0 = reinterpret_cast<const uint32_t*>(vl)[w0];
+                    const uint32_t bl1 = reinterpret_cast<const uint32_t*>(vl)[w1];
                     mma_bf16(o[n], ph, bh0, bh1);
                     mma_bf16(o[n], pl, bh0, bh1);
                     mma_bf16(o[n], ph, bl0, bl1);
