@@ -1950,7 +1950,7 @@ static __device__ int g_gemm_err_word;
 static aion_status launch_gemm_bf16(const void* a, const void* b, float* c, int64_t m, int64_t n, int64_t k,
                                     int64_t ldc, int dev, cudaStream_t st, int* err_dev, std::string* err) {
     if (m <= 0 || n <= 0 || k <= 0 || m % kGemmBM || n % kGemmBN || k % kGemmBK || ldc < n || ldc % 4 ||
-        m / kGemmBM > 0x7FFFFFFF || n / kGemmBN > 65535) {
+        (m / kGemmBM) * (n / kGemmBN) > 0x7FFFFFFF) {
         set_err(err, "gemm: M, N, K must be positive multiples of %d, %d, %d (got %lld, %lld, %lld)", kGemmBM,
                 kGemmBN, kGemmBK, (long long)m, (long long)n, (long long)k);
         return AION_ERR_SHAPE;
@@ -1972,7 +1972,7 @@ static aion_status launch_gemm_bf16(const void* a, const void* b, float* c, int6
     g.K = (int)k;
     g.ldc = (int)ldc;
     g.err = err_dev;
-    k_gemm_bf16_tn<<<dim3((unsigned)(m / kGemmBM), (unsigned)(n / kGemmBN)), kGemmThreads, kGemmSmem, st>>>(ma, mb, g);
+    k_gemm_bf16_tn<<<(unsigned)((m / kGemmBM) * (n / kGemmBN)), kGemmThreads, kGemmSmem, st>>>(ma, mb, g);
     CK_RET(err, cudaGetLastError());
     return AION_OK;
 }

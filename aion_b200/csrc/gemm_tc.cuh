@@ -82,6 +82,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+constexpr int kGemmGroupM = 16;   // row tiles per rasterisation group
+
 struct GemmArgs {
     float* C;          // [M][ldc]
     int M, N, K;       // multiples of 128, 256 and 64
@@ -98,7 +100,18 @@ k_gemm_bf16_tn(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     unsigned char* gsm =
         gsm_raw + ((1024u - (smem_addr(gsm_raw) & 1023u)) & 1023u);   // stages start 1024-aligned
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kGemmBM, n0 = blockIdx.y * kGemmBN;
+    // Tile order: groups of kGemmGroupM row tiles, each group walked column
+    // tile by column tile, so the CTAs resident at one time share ~16 A
+    // tiles and ~10 B tiles and each operand tile is mostly read from L2
+    // (row-tile-fastest order streams all of A from DRAM once per column tile).
+    int m0, n0;
+    {
+        const int mt = g.M / kGemmBM, nt = g.N / kGemmBN, id = (int)blockIdx.x;
+        const int per_group = kGemmGroupM * nt, gi = id / per_group, first = gi * kGemmGroupM;
+        const int gm = min(mt - first, kGemmGroupM), r = id - gi * per_group;
+        m0 = (first + r % gm) * kGemmBM;
+        n0 = (r / gm) * kGemmBN;
+    }
     const int nkb = g.K / kGemmBK;
 
     if (threadIdx.x == 0) {
