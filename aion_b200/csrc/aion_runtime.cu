@@ -1972,7 +1972,9 @@ static aion_status launch_gemm_bf16(const void* a, const void* b, float* c, int6
     g.K = (int)k;
     g.ldc = (int)ldc;
     g.err = err_dev;
-    k_gemm_bf16_tn<<<(unsigned)((m / kGemmBM) * (n / kGemmBN)), kGemmThreads, kGemmSmem, st>>>(ma, mb, g);
+    const long long tiles = (m / kGemmBM) * (n / kGemmBN);
+    const int grid = (int)std::min<long long>(tiles, dev_info(dev).sms);   // persistent: one CTA per SM
+    k_gemm_bf16_tn<<<(unsigned)grid, kGemmThreads, kGemmSmem, st>>>(ma, mb, g);
     CK_RET(err, cudaGetLastError());
     return AION_OK;
 }
