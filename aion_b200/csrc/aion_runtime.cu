@@ -1385,7 +1385,7 @@ extern "C" AION_API aion_status aion_prefill(aion_ctx* c, const int32_t* tokens,
         aa.kv_mul = (int)c->kv_mul;
         aa.kp = (int)kpd;
         aa.out = pf.a;
-        k_pf_attention<<<dim3((unsigned)((n_tok + kPfTQ - 1) / kPfTQ), (unsigned)c->nh, (unsigned)n_seq), 128,
+        k_pf_attention<<<dim3((unsigned)((n_tok + kPfTQ - 1) / kPfTQ), (unsigned)c->nh, (unsigned)n_seq), kPfAttnThreads,
                          kPfAttnSmem, c->stream>>>(aa);
         CK_RET(&c->err, cudaGetLastError());
         st = pf_matmul(c, c->wo[l], mpad, kpd, &np);

@@ -158,22 +158,26 @@ __global__ void k_pf_rope_kv(PfRopeArgs a) {
 // positions 0..t, weighted sum of V rows), on the tensor cores.  The output
 // goes straight into the A operand of WO.
 //
-// CTA = (query block of 64, head, sequence), longest blocks first; warp w
-// holds rows 16w..16w+15 of the block.  Keys come in blocks of 64: the CTA
-// converts the block's fp32 K rows to bf16 hi/lo parts in shared memory as
-// [key][d] and its V rows as [d][key], so both are B operands of
-// mma.sync.m16n8k16 read with 32-bit loads (row strides padded by 8
-// elements: the quad lanes of the 8 fragment rows hit 32 distinct banks).
+// CTA = (query block of 128, head, sequence), longest blocks first; warp w
+// holds rows 16w..16w+15 of the block.  Keys come in blocks of 64.  The fp32
+// K and V rows of the next block stream into a raw stage with cp.async
+// while the current block is processed; at the top of each block the CTA
+// converts the raw stage into bf16 hi/lo parts, K as [key][d] and V as
+// [d][key], so both are B operands of mma.sync.m16n8k16 read with 32-bit
+// loads (K rows padded by 8 elements; V^T words XOR-swizzled, vt_word):
+// every fragment read and conversion store hits 32 distinct banks.
 // Each product takes three MMAs, hi.hi + lo.hi + hi.lo, as in the prefill
 // GEMMs (lo.lo, about 2^-16 of a product, is left out): S = Q K^T with Q's
 // fragments held in registers, then an online softmax in fp32 on the S
 // fragments (rows g and g + 8 of a lane, the quad's four lanes reduced by
 // shuffles), then O += P V with P's fragments taken straight from S's
-// accumulator layout.
-constexpr int kPfTQ = 64, kPfTK = 64;
+// accumulator layout.  A warp whose rows all precede the key block skips it.
+constexpr int kPfTQ = 128, kPfTK = 64, kPfAttnThreads = 256;
 constexpr int kPfKs = kMaxHead + 8;   // K row stride (bf16 elements)
 constexpr int kPfVs = kPfTK + 8;      // V^T row stride
-constexpr int kPfAttnSmem = 2 * (kPfTK * kPfKs + kMaxHead * kPfVs) * 2;
+constexpr int kPfAttnImage = 2 * (kPfTK * kPfKs + kMaxHead * kPfVs) * 2;   // bf16 K and V^T, hi and lo
+constexpr int kPfAttnRaw = 2 * kPfTK * kMaxHead * 4;                        // fp32 K and V rows
+constexpr int kPfAttnSmem = kPfAttnImage + kPfAttnRaw;
 struct PfAttnArgs {
     const float* q;                   // [mrows][dim]
     const float *kcache, *vcache;     // sequence 0, layer l
@@ -195,28 +199,50 @@ __device__ __forceinline__ void split2(float x, float y, uint32_t& hi, uint32_t&
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
+// 16-byte cp.async; zero-fills the destination when !valid (nothing is read).
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
 // 32-bit word of V^T row d holding keys 2 kp, 2 kp + 1.  The XOR of the
 // pair index with bits 3..5 of d spreads a warp's stores (32 rows d, one
 // kp) over 32 banks; a fragment read (rows 8n + g, pairs 8j + t) sees one
 // XOR constant, so its 32 lanes still hit 4g + (pair ^ c): 32 banks.
 __device__ __forceinline__ int vt_word(int d, int kp) { return d * (kPfVs / 2) + (kp ^ ((d >> 3) & 7)); }
-__global__ void __launch_bounds__(128, 2) k_pf_attention(PfAttnArgs a) {
+__global__ void __launch_bounds__(kPfAttnThreads, 1) k_pf_attention(PfAttnArgs a) {
     constexpr int NK = kMaxHead / 16, ND = kMaxHead / 8, NT = kPfTK / 8;
     extern __shared__ __align__(16) unsigned char pf_smem[];
     __nv_bfloat16* kh = reinterpret_cast<__nv_bfloat16*>(pf_smem);   // [key][kPfKs]
     __nv_bfloat16* kl = kh + kPfTK * kPfKs;
-    __nv_bfloat16* vh = kl + kPfTK * kPfKs;                          // [d][kPfVs]
+    __nv_bfloat16* vh = kl + kPfTK * kPfKs;                          // [d][kPfVs], words at vt_word
     __nv_bfloat16* vl = vh + kMaxHead * kPfVs;
+    float* rk = reinterpret_cast<float*>(pf_smem + kPfAttnImage);   // raw K rows [kPfTK][hs]
+    float* rv = rk + kPfTK * kMaxHead;                               // raw V rows [kPfTK][hs]
     const int nqb = (a.T + kPfTQ - 1) / kPfTQ;
     const int qb = nqb - 1 - (int)blockIdx.x, h = blockIdx.y, s = blockIdx.z;
-    const int hs = a.hs, nk = hs / 16, nd = hs / 8, h4 = hs / 4, kvh = h / a.kv_mul;
+    const int hs = a.hs, nk = hs / 16, nd = hs / 8, h4 = hs / 4, h2 = hs / 2, kvh = h / a.kv_mul;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int q0 = qb * kPfTQ;
-    const int r0 = q0 + 16 * warp + g, r1 = r0 + 8;   // this lane's rows (positions)
-    const int t_last = min(a.T, q0 + kPfTQ) - 1;      // the last key any row of the CTA sees
+    const int wr0 = q0 + 16 * warp;                  // the warp's first row
+    const int r0 = wr0 + g, r1 = r0 + 8;             // this lane's rows (positions)
+    const int t_last = min(a.T, q0 + kPfTQ) - 1;     // the last key any row of the CTA sees
     const float* kc = a.kcache + s * a.seq_stride + (size_t)kvh * hs;
     const float* vc = a.vcache + s * a.seq_stride + (size_t)kvh * hs;
     const float2 z2 = make_float2(0.0f, 0.0f);
+
+    // Raw stage: fp32 K and V rows of keys k0..k0+63 (zero past t_last).
+    auto stage_raw = [&](int k0) {
+        for (int i = threadIdx.x; i < kPfTK * h4; i += kPfAttnThreads) {
+            const int key = i / h4, d = 4 * (i - key * h4);
+            const bool in = k0 + key <= t_last;
+            const size_t off = (size_t)(in ? k0 + key : 0) * a.kv_dim + d;
+            cp_async16_zfill(rk + key * hs + d, kc + off, in);
+            cp_async16_zfill(rv + key * hs + d, vc + off, in);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage_raw(0);
 
     uint32_t qh[NK][4], ql[NK][4];
     {
@@ -244,58 +270,32 @@ __global__ void __launch_bounds__(128, 2) k_pf_attention(PfAttnArgs a) {
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;   // l: this lane's share of the row sums
 
     for (int k0 = 0; k0 <= t_last; k0 += kPfTK) {
-        __syncthreads();   // the previous block's fragments are read
-        // K rows: four float4 loads in flight per thread before their stores.
-        constexpr int U = 4;
-        for (int i0 = threadIdx.x; i0 < kPfTK * h4; i0 += U * blockDim.x) {
-            float4 v[U];
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int i = i0 + u * blockDim.x, key = i / h4, d = 4 * (i - key * h4);
-                v[u] = (i < kPfTK * h4 && k0 + key <= t_last)
-                           ? __ldg(reinterpret_cast<const float4*>(kc + (size_t)(k0 + key) * a.kv_dim + d))
-                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            }
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int i = i0 + u * blockDim.x, key = i / h4, d = 4 * (i - key * h4);
-                if (i < kPfTK * h4) {
-                    uint32_t h01, l01, h23, l23;
-                    split2(v[u].x, v[u].y, h01, l01);
-                    split2(v[u].z, v[u].w, h23, l23);
-                    *reinterpret_cast<uint2*>(kh + key * kPfKs + d) = make_uint2(h01, h23);
-                    *reinterpret_cast<uint2*>(kl + key * kPfKs + d) = make_uint2(l01, l23);
-                }
-            }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();   // the raw stage holds block k0; the previous image is read
+        for (int i = threadIdx.x; i < kPfTK * h4; i += kPfAttnThreads) {
+            const int key = i / h4, d = 4 * (i - key * h4);
+            const float4 v = *reinterpret_cast<const float4*>(rk + key * hs + d);
+            uint32_t h01, l01, h23, l23;
+            split2(v.x, v.y, h01, l01);
+            split2(v.z, v.w, h23, l23);
+            *reinterpret_cast<uint2*>(kh + key * kPfKs + d) = make_uint2(h01, h23);
+            *reinterpret_cast<uint2*>(kl + key * kPfKs + d) = make_uint2(l01, l23);
         }
-        // V rows, transposed: thread (key pair kp, columns d, d + 1) writes
-        // word kp ^ ((d >> 3) & 7) of rows d and d + 1 (see vt_word).
-        const int h2 = hs / 2;
-        for (int i0 = threadIdx.x; i0 < (kPfTK / 2) * h2; i0 += U * blockDim.x) {
-            float2 va[U], vb[U];
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int i = i0 + u * blockDim.x, kp = i / h2, d = 2 * (i - kp * h2), key = k0 + 2 * kp;
-                const bool in = i < (kPfTK / 2) * h2;
-                va[u] = in && key <= t_last ? __ldg(reinterpret_cast<const float2*>(vc + (size_t)key * a.kv_dim + d)) : z2;
-                vb[u] = in && key + 1 <= t_last ? __ldg(reinterpret_cast<const float2*>(vc + (size_t)(key + 1) * a.kv_dim + d))
-                                                : z2;
-            }
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int i = i0 + u * blockDim.x, kp = i / h2, d = 2 * (i - kp * h2);
-                if (i < (kPfTK / 2) * h2) {
-                    uint32_t hi, lo;
-                    split2(va[u].x, vb[u].x, hi, lo);
-                    reinterpret_cast<uint32_t*>(vh)[vt_word(d, kp)] = hi;
-                    reinterpret_cast<uint32_t*>(vl)[vt_word(d, kp)] = lo;
-                    split2(va[u].y, vb[u].y, hi, lo);
-                    reinterpret_cast<uint32_t*>(vh)[vt_word(d + 1, kp)] = hi;
-                    reinterpret_cast<uint32_t*>(vl)[vt_word(d + 1, kp)] = lo;
-                }
-            }
+        for (int i = threadIdx.x; i < (kPfTK / 2) * h2; i += kPfAttnThreads) {
+            const int kp = i / h2, d = 2 * (i - kp * h2);
+            const float2 va = *reinterpret_cast<const float2*>(rv + (2 * kp) * hs + d);
+            const float2 vb = *reinterpret_cast<const float2*>(rv + (2 * kp + 1) * hs + d);
+            uint32_t hi, lo;
+            split2(va.x, vb.x, hi, lo);
+            reinterpret_cast<uint32_t*>(vh)[vt_word(d, kp)] = hi;
+            reinterpret_cast<uint32_t*>(vl)[vt_word(d, kp)] = lo;
+            split2(va.y, vb.y, hi, lo);
+            reinterpret_cast<uint32_t*>(vh)[vt_word(d + 1, kp)] = hi;
+            reinterpret_cast<uint32_t*>(vl)[vt_word(d + 1, kp)] = lo;
         }
-        __syncthreads();
+        __syncthreads();   // the image is complete; the raw stage is free
+        if (k0 + kPfTK <= t_last) stage_raw(k0 + kPfTK);
+        if (k0 > wr0 + 15) continue;   // every row of this warp precedes the block
 
         // S = Q K^T: 16 rows x 64 keys per warp.
         float sc[NT][4];
@@ -334,7 +334,8 @@ __global__ void __launch_bounds__(128, 2) k_pf_attention(PfAttnArgs a) {
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        // Key k0 <= every row of the CTA, so the block maxima are finite.
+        // Key 0 is seen by every row in the first block, so the running maxima
+        // are finite from then on; a row with no key in this block keeps its max.
         const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
         const float c0 = expf(m0 - mn0), c1 = expf(m1 - mn1);
         l0 *= c0;
