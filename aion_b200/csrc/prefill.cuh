@@ -244,6 +244,9 @@ __global__ void __launch_bounds__(kPfAttnThreads, 1) k_pf_attention(PfAttnArgs a
     };
     stage_raw(0);
 
+    // Q arrives scaled by log2(e) / sqrt(hs): the scores are then in base-2
+    // units and the softmax uses exp2 (the same weights up to rounding).
+    const float qscale = 1.4426950408889634f / sqrtf((float)hs);
     uint32_t qh[NK][4], ql[NK][4];
     {
         const float* q0p = a.q + ((size_t)s * a.T + min(r0, a.T - 1)) * a.dim + h * hs;
@@ -256,14 +259,13 @@ __global__ void __launch_bounds__(kPfAttnThreads, 1) k_pf_attention(PfAttnArgs a
                 const float2 x1 = r1 < a.T ? *reinterpret_cast<const float2*>(q1p + c) : z2;
                 const float2 x2 = r0 < a.T ? *reinterpret_cast<const float2*>(q0p + c + 8) : z2;
                 const float2 x3 = r1 < a.T ? *reinterpret_cast<const float2*>(q1p + c + 8) : z2;
-                split2(x0.x, x0.y, qh[kk][0], ql[kk][0]);
-                split2(x1.x, x1.y, qh[kk][1], ql[kk][1]);
-                split2(x2.x, x2.y, qh[kk][2], ql[kk][2]);
-                split2(x3.x, x3.y, qh[kk][3], ql[kk][3]);
+                split2(x0.x * qscale, x0.y * qscale, qh[kk][0], ql[kk][0]);
+                split2(x1.x * qscale, x1.y * qscale, qh[kk][1], ql[kk][1]);
+                split2(x2.x * qscale, x2.y * qscale, qh[kk][2], ql[kk][2]);
+                split2(x3.x * qscale, x3.y * qscale, qh[kk][3], ql[kk][3]);
             }
         }
     }
-    const float rs = sqrtf((float)hs);
     float o[ND][4];
 #pragma unroll
     for (int n = 0; n < ND; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
@@ -317,18 +319,24 @@ __global__ void __launch_bounds__(kPfAttnThreads, 1) k_pf_attention(PfAttnArgs a
                 }
             }
         }
-        // Online softmax: scale, causal mask, block max per row.
+        // Online softmax: causal mask (blocks reaching past the warp's first
+        // row only), block max per row.
+        if (k0 + kPfTK - 1 > wr0) {
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int key = k0 + n * 8 + 2 * t + e;
+                    if (key > r0) sc[n][e] = -INFINITY;
+                    if (key > r1) sc[n][2 + e] = -INFINITY;
+                }
+            }
+        }
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
         for (int n = 0; n < NT; n++) {
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int key = k0 + n * 8 + 2 * t + e;
-                sc[n][e] = key <= r0 ? __fdiv_rn(sc[n][e], rs) : -INFINITY;
-                sc[n][2 + e] = key <= r1 ? __fdiv_rn(sc[n][2 + e], rs) : -INFINITY;
-                mx0 = fmaxf(mx0, sc[n][e]);
-                mx1 = fmaxf(mx1, sc[n][2 + e]);
-            }
+            mx0 = fmaxf(mx0, fmaxf(sc[n][0], sc[n][1]));
+            mx1 = fmaxf(mx1, fmaxf(sc[n][2], sc[n][3]));
         }
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
@@ -337,7 +345,7 @@ __global__ void __launch_bounds__(kPfAttnThreads, 1) k_pf_attention(PfAttnArgs a
         // Key 0 is seen by every row in the first block, so the running maxima
         // are finite from then on; a row with no key in this block keeps its max.
         const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float c0 = expf(m0 - mn0), c1 = expf(m1 - mn1);
+        const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
         l0 *= c0;
         l1 *= c1;
 #pragma unroll
@@ -351,8 +359,8 @@ __global__ void __launch_bounds__(kPfAttnThreads, 1) k_pf_attention(PfAttnArgs a
         for (int n = 0; n < NT; n++) {
 #pragma unroll
             for (int e = 0; e < 2; e++) {
-                sc[n][e] = expf(sc[n][e] - mn0);
-                sc[n][2 + e] = expf(sc[n][2 + e] - mn1);
+                sc[n][e] = exp2f(sc[n][e] - mn0);
+                sc[n][2 + e] = exp2f(sc[n][2 + e] - mn1);
                 l0 += sc[n][e];
                 l1 += sc[n][2 + e];
             }
