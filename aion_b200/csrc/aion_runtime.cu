@@ -623,8 +623,8 @@ static aion_status enqueue_steps(aion_ctx* c, int steps) {
     return AION_OK;
 }
 
-static aion_status check_device_error(aion_ctx* c) {
-    CK_RET(&c->err, cudaMemcpy(c->h_step, c->step, sizeof(StepState), cudaMemcpyDeviceToHost));
+// The step state's error word, read from the copy in c->h_step.
+static aion_status decode_device_error(aion_ctx* c) {
     switch (c->h_step->error) {
     case DEV_OK: return AION_OK;
     case DEV_BAD_INPUT:
@@ -634,6 +634,10 @@ static aion_status check_device_error(aion_ctx* c) {
         set_err(&c->err, "a bounded device wait gave up (code %d); call aion_reset", c->h_step->error);
         return AION_ERR_TIMEOUT;
     }
+}
+static aion_status check_device_error(aion_ctx* c) {
+    CK_RET(&c->err, cudaMemcpy(c->h_step, c->step, sizeof(StepState), cudaMemcpyDeviceToHost));
+    return decode_device_error(c);
 }
 
 // ---------------------------------------------------------------------------
@@ -1165,15 +1169,17 @@ static aion_status tp_ready(aion_ctx* c) {
     return AION_OK;
 }
 
-static aion_status set_step(aion_ctx* c, int32_t token, int32_t pos) {
+// Writes the next step's token and position (and clears the error word).
+// The barrier and exchange counters stay (they only ever grow).  The
+// pinned host buffer is reused, so with sync == false the caller must
+// synchronise the stream before the host touches c->h_step again.
+static aion_status set_step(aion_ctx* c, int32_t token, int32_t pos, bool sync = true) {
     memset(c->h_step, 0, sizeof(StepState));
     c->h_step->pos_next = pos;
     c->h_step->forced_token = token;
-    // The pinned host buffer is reused: wait for the copy before returning.
-    // The barrier and exchange counters stay (they only ever grow).
     CK_RET(&c->err, cudaMemcpyAsync(c->step, c->h_step, offsetof(StepState, barrier), cudaMemcpyHostToDevice,
                                     c->stream));
-    CK_RET(&c->err, cudaStreamSynchronize(c->stream));
+    if (sync) CK_RET(&c->err, cudaStreamSynchronize(c->stream));
     return AION_OK;
 }
 
@@ -1185,13 +1191,19 @@ extern "C" AION_API aion_status aion_forward(aion_ctx* c, int32_t token, int32_t
         return AION_ERR_ARG;
     }
     CK_RET(&c->err, cudaSetDevice(c->dev));
-    aion_status s = set_step(c, token, pos);
+    // One host round trip a token: the step state goes in, the logits and
+    // the step state (its error word) come back, all ordered on the stream.
+    aion_status s = set_step(c, token, pos, false);
     if (s == AION_OK) s = enqueue_steps(c, 1);
-    if (s != AION_OK) return s;
+    if (s != AION_OK) {
+        cudaStreamSynchronize(c->stream);   // the pinned step buffer may still be in flight
+        return s;
+    }
     if (logits_host)
         CK_RET(&c->err, cudaMemcpyAsync(logits_host, c->logits, c->vocab_l * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK_RET(&c->err, cudaMemcpyAsync(c->h_step, c->step, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
     CK_RET(&c->err, cudaStreamSynchronize(c->stream));
-    return check_device_error(c);
+    return decode_device_error(c);
 }
 
 extern "C" AION_API aion_status aion_generate(aion_ctx* c, int32_t bos, int32_t steps, int32_t* tokens_out,
