@@ -1,15 +1,15 @@
-"""Tensor parallelism over 2 GPUs (one process per GPU) against one GPU and
-the oracle, on a small model whose shapes shard (dim 512, hidden 1536,
-8 heads, vocab 1024, 2 layers; seed-5 random weights, int4).
+"""Tensor parallelism over 2 and 4 GPUs (one process per GPU) against one
+GPU and the oracle, on a small model whose shapes shard over both (dim 512,
+hidden 1536, 8 heads, vocab 1024, 2 layers; seed-5 random weights, int4).
 
-Each rank holds half of the rows of wq/wk/wv/w1/w3 and of the classifier and
-half of the columns of wo/w2; the decode kernel sums the ranks' partial rows
-over NVLink peer memory and takes the argmax across ranks.  Tolerances: the
-greedy token stream of 32 steps is identical to the single-GPU one and to
-the oracle's; each rank's step-0 logit slice is within 1e-5 relative of the
-single-GPU logits (only the order of the partial sums differs); lock-step
-batched decode of 5 sequences over the two ranks gives the single-GPU
-batch's tokens.  Skipped with fewer than 2 GPUs.
+Each of N ranks holds 1/N of the rows of wq/wk/wv/w1/w3 and of the
+classifier and 1/N of the columns of wo/w2; the decode kernel sums the
+ranks' partial rows over NVLink peer memory and takes the argmax across
+ranks.  Tolerances: the greedy token stream of 32 steps is identical to the
+single-GPU one and to the oracle's; each rank's step-0 logit slice is within
+1e-5 relative of the single-GPU logits (only the order of the partial sums
+differs); lock-step batched decode of 5 sequences over the ranks gives the
+single-GPU batch's tokens.  Each case is skipped with fewer GPUs than ranks.
 """
 from __future__ import annotations
 
@@ -28,18 +28,18 @@ STEPS = 32
 FIRST = [1, 7, 100, 900, 511]   # token ids below the test model's vocab (1024)
 
 
-def _rank_main(rank: int, path: str, q_out, q_in, res) -> None:
+def _rank_main(rank: int, world: int, path: str, q_out, q_in, res) -> None:
     try:
         import torch
         import aion_b200 as A
         torch.cuda.set_device(rank)
-        m = A.Model(path, device=rank, tp_size=2, tp_rank=rank, max_batch=len(FIRST))
+        m = A.Model(path, device=rank, tp_size=world, tp_rank=rank, max_batch=len(FIRST))
         q_out.put((rank, m.tp_handle()))
         m.tp_connect(q_in.get(timeout=120))
         l0 = m.transformer(1, 0)
         m.reset()
         toks, _ = m.generate(STEPS)
-        # Lock-step batched decode over the same two ranks.
+        # Lock-step batched decode over the same ranks.
         bt, _ = m.decode_batch(FIRST, [0] * len(FIRST), STEPS)
         m.close()
         res.put((rank, toks, (l0, bt.tolist())))
@@ -55,8 +55,10 @@ def _gpu_count() -> int:
         return 0
 
 
-@pytest.mark.skipif(_gpu_count() < 2, reason="needs 2 GPUs")
-def test_tp2_matches_single_gpu(cuda, oracle, workdir):
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_matches_single_gpu(cuda, oracle, workdir, world):
+    if _gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import aion_b200 as A
     path = workdir / "tp_small.int4"
     if not path.exists():
@@ -76,27 +78,27 @@ def test_tp2_matches_single_gpu(cuda, oracle, workdir):
 
     ctx = mp.get_context("spawn")
     q_out, res = ctx.Queue(), ctx.Queue()
-    q_in = [ctx.Queue(), ctx.Queue()]
-    procs = [ctx.Process(target=_rank_main, args=(r, str(path), q_out, q_in[r], res)) for r in range(2)]
+    q_in = [ctx.Queue() for _ in range(world)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, str(path), q_out, q_in[r], res)) for r in range(world)]
     for p in procs:
         p.start()
     try:
-        handles = dict(q_out.get(timeout=300) for _ in range(2))
-        for r in range(2):
-            q_in[r].put([handles[0], handles[1]])
-        out = dict((r, (t, l)) for r, t, l in (res.get(timeout=300) for _ in range(2)))
+        handles = dict(q_out.get(timeout=300) for _ in range(world))
+        for r in range(world):
+            q_in[r].put([handles[j] for j in range(world)])
+        out = dict((r, (t, l)) for r, t, l in (res.get(timeout=300) for _ in range(world)))
     finally:
         for p in procs:
             p.join(timeout=60)
             if p.is_alive():
                 p.terminate()
-    half = CFG[5] // 2
-    for r in range(2):
+    part = CFG[5] // world
+    for r in range(world):
         toks_r, extra = out[r]
         assert toks_r != "error", extra
         l0, bt = extra
         assert toks_r == want
-        ref = want_l0[r * half:(r + 1) * half]
-        assert np.abs(l0[:half] - ref).max() <= 1e-5 * np.abs(want_l0).max()
+        ref = want_l0[r * part:(r + 1) * part]
+        assert np.abs(l0[:part] - ref).max() <= 1e-5 * np.abs(want_l0).max()
         # Batched decode over the ranks: the single-GPU batch's tokens.
         assert bt == want_bt.tolist()
