@@ -780,7 +780,10 @@ __device__ __forceinline__ AttnPart attn_unit(const DecodeArgs& a, const float* 
 
 // Merges nch partials laid out [m, l, -, -, o[0..hs)] at stride pstride
 // (chunk order; read through `ld`) into att[h]: the warp's lanes hold 32
-// chunks' max and sum per pass.
+// chunks' max and sum per pass; the o partials of kMergeBatch chunks are
+// loaded before any of them is folded in (chunk order kept), so a merge
+// of many chunks pays one memory round trip per batch, not per chunk.
+constexpr int kMergeBatch = 8;
 template <class Ld>
 __device__ __forceinline__ void attn_merge(const DecodeArgs& a, int h, const float* ph, int nch, int pstride, Ld ld) {
     const int hs = a.head_size, lane = threadIdx.x & 31;
@@ -798,16 +801,30 @@ __device__ __forceinline__ void attn_merge(const DecodeArgs& a, int h, const flo
             wl = expf(ld(ph + (size_t)(c0 + lane) * pstride) - M);
             ll = ld(ph + (size_t)(c0 + lane) * pstride + 1);
         }
-        for (int c = 0; c < cn; c++) {
-            const float wgt = __shfl_sync(0xffffffffu, wl, c);
-            const float lc = __shfl_sync(0xffffffffu, ll, c);
-            L = fmaf(lc, wgt, L);
-            if (vl) {
-                const float* oc = ph + (size_t)(c0 + c) * pstride + 4 + 4 * lane;
-                acc.x = fmaf(ld(oc), wgt, acc.x);
-                acc.y = fmaf(ld(oc + 1), wgt, acc.y);
-                acc.z = fmaf(ld(oc + 2), wgt, acc.z);
-                acc.w = fmaf(ld(oc + 3), wgt, acc.w);
+        for (int cb = 0; cb < cn; cb += kMergeBatch) {
+            float4 ov[kMergeBatch];
+#pragma unroll
+            for (int u = 0; u < kMergeBatch; u++) {
+                ov[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (vl && cb + u < cn) {
+                    const float* oc = ph + (size_t)(c0 + cb + u) * pstride + 4 + 4 * lane;
+                    ov[u] = make_float4(ld(oc), ld(oc + 1), ld(oc + 2), ld(oc + 3));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kMergeBatch; u++) {
+                const int c = cb + u;
+                const float wgt = __shfl_sync(0xffffffffu, wl, c & 31);
+                const float lc = __shfl_sync(0xffffffffu, ll, c & 31);
+                if (c < cn) {
+                    L = fmaf(lc, wgt, L);
+                    if (vl) {
+                        acc.x = fmaf(ov[u].x, wgt, acc.x);
+                        acc.y = fmaf(ov[u].y, wgt, acc.y);
+                        acc.z = fmaf(ov[u].z, wgt, acc.z);
+                        acc.w = fmaf(ov[u].w, wgt, acc.w);
+                    }
+                }
             }
         }
     }
