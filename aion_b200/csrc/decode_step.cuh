@@ -947,7 +947,25 @@ __device__ void attention_layer_exact(const DecodeArgs& a, int layer, int pos, f
         for (int t = tid; t <= pos; t += kThreads) {
             const float* kr = kc + (size_t)t * a.kv_dim + kvh * hs;
             float d = 0.0f;
-            for (int j = 0; j < hs; j++) d = __fadd_rn(d, __fmul_rn(s_q[j], __ldcg(kr + j)));
+            // 32 elements of the row are loaded before they are summed in
+            // order (hs is a multiple of 16: one or more full batches of 16).
+            for (int j0 = 0; j0 < hs; j0 += 32) {
+                float4 kv[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    kv[u] = j0 + 4 * u < hs ? __ldcg(reinterpret_cast<const float4*>(kr + j0 + 4 * u))
+                                            : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int j = j0 + 4 * u;
+                    if (j < hs) {
+                        d = __fadd_rn(d, __fmul_rn(s_q[j], kv[u].x));
+                        d = __fadd_rn(d, __fmul_rn(s_q[j + 1], kv[u].y));
+                        d = __fadd_rn(d, __fmul_rn(s_q[j + 2], kv[u].z));
+                        d = __fadd_rn(d, __fmul_rn(s_q[j + 3], kv[u].w));
+                    }
+                }
+            }
             d = __fdiv_rn(d, rs);
             sc[t] = d;
             m = fmaxf(m, d);
@@ -965,9 +983,18 @@ __device__ void attention_layer_exact(const DecodeArgs& a, int layer, int pos, f
         for (int t = tid; t <= pos; t += kThreads) sc[t] = __fmul_rn(sc[t], scale);
         csync();
         for (int j = tid; j < hs; j += kThreads) {
+            // 16 positions' V elements are loaded before they are summed in order.
+            const float* vj = vc + kvh * hs + j;
             float o = 0.0f;
-            for (int t = 0; t <= pos; t++)
-                o = __fadd_rn(o, __fmul_rn(sc[t], __ldcg(vc + (size_t)t * a.kv_dim + kvh * hs + j)));
+            int t = 0;
+            for (; t + 16 <= pos + 1; t += 16) {
+                float v[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++) v[u] = __ldcg(vj + (size_t)(t + u) * a.kv_dim);
+#pragma unroll
+                for (int u = 0; u < 16; u++) o = __fadd_rn(o, __fmul_rn(sc[t + u], v[u]));
+            }
+            for (; t <= pos; t++) o = __fadd_rn(o, __fmul_rn(sc[t], __ldcg(vj + (size_t)t * a.kv_dim)));
             __stcg(a.att + h * hs + j, o);
         }
         csync();
