@@ -1,7 +1,7 @@
 // Dense bf16 GEMM on the 5th-generation tensor cores (sm_100a), for the
 // batched prefill: C[M][N] (fp32) = A[M][K] * B[N][K]^T, A and B bf16 with K
 // contiguous.  The int4 weights reach it as bf16 tiles written by
-// k_dequant_bf16 (decode_prefill.cuh); the activations as bf16 rows.
+// k_pf_dequant (prefill.cuh); the activations as bf16 rows.
 //
 // A persistent kernel: one CTA per SM walks the 128 x 256 tiles of C in a
 // grouped order (kGemmGroupM row tiles a group, column tile by column tile,
